@@ -1,0 +1,364 @@
+"""The five benchmark workloads, as seeded synthetic scenes built through the `WorldDef` builder API.
+
+Every world of a workload shares one static level (the reference's Model is shared by all worlds of a batch);
+worlds differ in their dynamic bodies' initial state, drawn from the seed per world index. Edge and chain shapes are
+not in the reference engine, so the chain terrain and zero-thickness edges are built as their polygon-terrain
+variants: each chain segment becomes the static convex quad (x_i, floor), (x_i+1, floor), (x_i+1, h_i+1), (x_i, h_i),
+and each zero-thickness edge a 0.02 m thick box.
+
+`scene(name, seed)` gives a `Scene`: the level arrays plus, per world index, the dynamic bodies' parameters.
+`scene.build_world(defn, i)` issues the builder calls of world i on any WorldDef-like object (this package's, or the
+reference's when generating golden vectors); `batch(name, n, seed)` builds the Model once and the n world States
+vectorised, bit-identical to building each world through WorldDef (tests/test_host.py checks that).
+"""
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import shapes
+from .settings import Settings
+from .world import DYNAMIC, STATIC, WorldDef
+
+F32 = np.float32
+DT = F32(0.02)
+GRAVITY = (F32(0.0), F32(-9.81))
+
+
+def _settings(continuous, allow_sleep=True):
+    return Settings.stock(gravity=GRAVITY, velocity_iterations=8, position_iterations=3,
+                          continuous_physics=continuous, allow_sleep=allow_sleep)
+
+
+def _convex(rng, k, r):
+    """A convex polygon: k points on a circle of radius r, evenly spaced angles jittered by under a third of the
+    spacing (strictly convex, counter-clockwise, never closer than Set's weld distance)."""
+    step = 2 * np.pi / k
+    ang = rng.uniform(0, 2 * np.pi) + step * np.arange(k) + rng.uniform(-0.3, 0.3, k) * step
+    return np.stack([r * np.cos(ang), r * np.sin(ang)], 1).astype(F32)
+
+
+def polygon_mass(verts, density):
+    """Mass, centroid and rotational inertia about the centroid of a convex polygon (b2PolygonShape::ComputeMass's
+    triangle-fan formula, evaluated in float64 on the host; the scene only needs plausible values)."""
+    v = np.asarray(verts, np.float64)
+    ref = v.mean(0)
+    area, cx, cy, inertia = 0.0, 0.0, 0.0, 0.0
+    for i in range(len(v)):
+        e1, e2 = v[i] - ref, v[(i + 1) % len(v)] - ref
+        d = e1[0] * e2[1] - e1[1] * e2[0]
+        a = 0.5 * d
+        area += a
+        cx += a * (e1[0] + e2[0]) / 3.0
+        cy += a * (e1[1] + e2[1]) / 3.0
+        intx2 = e1[0] * e1[0] + e2[0] * e1[0] + e2[0] * e2[0]
+        inty2 = e1[1] * e1[1] + e2[1] * e1[1] + e2[1] * e2[1]
+        inertia += (0.25 / 3.0 * d) * (intx2 + inty2)
+    m = density * area
+    c = np.array([cx / area, cy / area])
+    i_ref = density * inertia
+    i_com = i_ref - m * float(c @ c)
+    return float(m), (c + ref), float(i_com)
+
+
+@dataclass
+class Scene:
+    name: str
+    settings: Settings
+    capacity: int
+    steps: int
+    n_worlds: int
+    static_polys: list = field(default_factory=list)  # (verts (k,2), friction)
+    static_boxes: list = field(default_factory=list)  # (half (2,), centre (2,), angle, friction)
+    level_calls: list = field(default_factory=list)  # extra builder calls for the level (anchors)
+    dyn: dict = field(default_factory=dict)  # per-world arrays, first axis = world
+    builder: object = None  # fn(defn, scene, i) adding the dynamic part of world i
+    action_joints: tuple = ()  # joints whose motor speed follows an action channel
+    action_scale: tuple = ()
+    level: tuple = ()
+    anchor: tuple = ()
+
+    def build_world(self, defn, i):
+        g = defn.add_body(STATIC)
+        for verts, fr in self.static_polys:
+            defn.add_polygon(g, verts, friction=fr)
+        for half, ctr, ang, fr in self.static_boxes:
+            defn.add_box(g, tuple(half), tuple(ctr), ang, friction=fr)
+        self.builder(defn, self, i)
+        return defn
+
+    def world_def(self, i, cls=WorldDef):
+        return self.build_world(cls(self.settings), i)
+
+
+# ---- c0: box drop on a terrain chain (polygon-terrain variant)
+
+
+def _terrain_quads(heights, x0, dx, floor, friction):
+    out = []
+    for i in range(len(heights) - 1):
+        xa, xb = x0 + i * dx, x0 + (i + 1) * dx
+        quad = np.array([(xa, floor), (xb, floor), (xb, heights[i + 1]), (xa, heights[i])], F32)
+        out.append((quad, friction))
+    return out
+
+
+def _c0_bodies(defn, sc, i):
+    d = sc.dyn
+    for k in range(8):
+        b = defn.add_body(DYNAMIC, (float(d["x"][i, k]), float(d["y"][i, k])), float(d["angle"][i, k]),
+                          mass=0.25, inertia=F32(0.25) * F32(0.5) / F32(12.0))
+        defn.add_box(b, (0.25, 0.25), friction=0.6)
+
+
+def c0(seed=0, n=256):
+    rng = np.random.default_rng(seed)
+    h = rng.uniform(-0.5, 0.5, 128).astype(F32)
+    x0, dx = -32.0, 0.5
+    sc = Scene("c0_box_drop", _settings(False), 64, 600, n)
+    sc.static_polys = _terrain_quads(h, x0, dx, -2.0, 0.6)
+    wr = np.random.default_rng([seed, 1])
+    sc.dyn = dict(x=wr.uniform(x0 + 1, x0 + 127 * dx - 1, (n, 8)).astype(F32),
+                  y=wr.uniform(2, 6, (n, 8)).astype(F32), angle=wr.uniform(0, 2 * np.pi, (n, 8)).astype(F32))
+    sc.builder = _c0_bodies
+    return sc
+
+
+# ---- c1: character rig (pot, hub, hammer; revolute motor + prismatic slide) on a chain level with rocks
+
+
+def _rig(defn, sc, i, x, y, ang):
+    d = sc.dyn
+    pot = defn.add_body(DYNAMIC, (x, y), 0.0, mass=30.0, inertia=5.4)
+    defn.add_circle(pot, 0.6, friction=0.8, group=-1)  # group -1: the pot and the hammer never collide
+    hub = defn.add_body(DYNAMIC, (x, y), ang, mass=1.0, inertia=0.05)
+    c, s = math.cos(ang), math.sin(ang)
+    hx, hy = x + 1.0 * c, y + 1.0 * s
+    ham = defn.add_body(DYNAMIC, (hx, hy), ang, mass=2.0, inertia=0.43, bullet=True)
+    defn.add_box(ham, (0.7, 0.04), (-0.1, 0.0), friction=0.6, group=-1)
+    defn.add_polygon(ham, _HEAD, friction=0.6, group=-1)
+    defn.add_revolute(pot, hub, (0, 0), (0, 0), ang, motor_speed=float(d["w0"][i]), max_motor_torque=1000.0,
+                      enable_motor=True)
+    defn.add_prismatic(hub, ham, (0, 0), (0, 0), (1, 0), 0.0, limits=(0.3, 1.9), motor_speed=0.0,
+                       max_motor_force=1000.0, enable_motor=True)
+    return pot, hub, ham
+
+
+_HEAD = [(0.55, -0.08), (0.8, -0.08), (0.85, 0.0), (0.8, 0.08), (0.55, 0.08)]
+
+
+def _c1_bodies(defn, sc, i):
+    d = sc.dyn
+    _rig(defn, sc, i, float(d["x"][i]), float(d["y"][i]), float(d["angle"][i]))
+
+
+def _level_c1(rng, friction=0.7):
+    steps = rng.normal(0, 0.15, 2000)
+    h = np.concatenate([[0.0], np.cumsum(steps)]).astype(F32)
+    x0, dx = -250.0, 0.25
+    floor = float(h.min()) - 1.0
+    polys = _terrain_quads(h, x0, dx, floor, friction)
+    for _ in range(60):
+        k = int(rng.integers(3, 9))
+        r = float(rng.uniform(0.3, 2.0))
+        px = float(rng.uniform(x0 + 5, x0 + 2000 * dx - 5))
+        ix = int((px - x0) / dx)
+        py = float(h[ix]) + float(rng.uniform(0.0, 3.0))
+        polys.append(((_convex(rng, k, r) + np.array([px, py], F32)).astype(F32), friction))
+    return h, x0, dx, polys
+
+
+def _rig_starts(h, x0, dx, wr, n):
+    x = wr.uniform(x0 + 10, x0 + 2000 * dx - 10, n)
+    ix = ((x - x0) / dx).astype(int)
+    y = np.maximum(h[ix], h[ix + 1]).astype(np.float64) + 0.7 + 0.02
+    return x.astype(F32), y.astype(F32), wr.uniform(0, 2 * np.pi, n).astype(F32)
+
+
+def c1(seed=0, n=4096):
+    rng = np.random.default_rng(seed)
+    h, x0, dx, polys = _level_c1(rng)
+    sc = Scene("c1_rig", _settings(True), 32, 1000, n)
+    sc.static_polys = polys
+    wr = np.random.default_rng([seed, 1])
+    x, y, ang = _rig_starts(h, x0, dx, wr, n)
+    sc.dyn = dict(x=x, y=y, angle=ang, w0=wr.uniform(-2, 2, n).astype(F32))
+    sc.builder = _c1_bodies
+    sc.level = (h, x0, dx)
+    sc.action_joints, sc.action_scale = (0, 1), (4.0, 2.0)
+    return sc
+
+
+# ---- c2: 256 mixed bodies in a 20 x 20 m box, sleeping off
+
+
+def _c2_bodies(defn, sc, i):
+    d = sc.dyn
+    for k in range(256):
+        kind = int(d["kind"][k])
+        x, y, a = float(d["x"][i, k]), float(d["y"][i, k]), float(d["angle"][i, k])
+        m, ctr, inertia = d["mass"][k], d["center"][k], d["inertia"][k]
+        b = defn.add_body(DYNAMIC, (x, y), a, mass=float(m), center=tuple(float(c) for c in ctr),
+                          inertia=float(inertia))
+        e = float(d["restitution"][k])
+        if kind == 0:
+            defn.add_circle(b, float(d["size"][k, 0]), friction=0.4, restitution=e)
+        elif kind == 1:
+            defn.add_box(b, (float(d["size"][k, 0]), float(d["size"][k, 1])), friction=0.4, restitution=e)
+        else:
+            defn.add_polygon(b, d["poly"][k][: int(d["nv"][k])], friction=0.4, restitution=e)
+
+
+def c2(seed=0, n=1024, bodies=256):
+    rng = np.random.default_rng(seed)
+    sc = Scene("c2_stress", _settings(False, allow_sleep=False), 4 * bodies, 500, n)
+    sc.static_boxes = [((10.0, 0.25), (0.0, -10.25), 0.0, 0.4), ((10.0, 0.25), (0.0, 10.25), 0.0, 0.4),
+                       ((0.25, 10.0), (-10.25, 0.0), 0.0, 0.4), ((0.25, 10.0), (10.25, 0.0), 0.0, 0.4)]
+    kind = rng.integers(0, 3, bodies)
+    size = rng.uniform(0.1, 0.4, (bodies, 2)).astype(F32)
+    dens = rng.uniform(0.5, 2.0, bodies)
+    nv = rng.integers(5, 9, bodies)
+    poly = np.zeros((bodies, 8, 2), F32)
+    mass, center, inertia = np.zeros(bodies, F32), np.zeros((bodies, 2), F32), np.zeros(bodies, F32)
+    for k in range(bodies):
+        if kind[k] == 0:
+            r = float(size[k, 0])
+            m = dens[k] * np.pi * r * r
+            mass[k], inertia[k] = m, 0.5 * m * r * r
+        elif kind[k] == 1:
+            hx, hy = float(size[k, 0]), float(size[k, 1])
+            m = dens[k] * 4 * hx * hy
+            mass[k], inertia[k] = m, m * (hx * hx + hy * hy) / 3.0
+        else:
+            pv = _convex(rng, int(nv[k]), float(size[k, 0]) + 0.05)
+            poly[k, : nv[k]] = pv
+            m, c, icom = polygon_mass(pv, dens[k])
+            mass[k], center[k], inertia[k] = m, c, icom
+    side = int(math.ceil(math.sqrt(bodies)))
+    gx, gy = np.meshgrid(np.arange(side), np.arange(side))
+    gx, gy = gx.ravel()[:bodies], gy.ravel()[:bodies]
+    pitch = 18.0 / side
+    wr = np.random.default_rng([seed, 1])
+    jit = wr.uniform(-0.1, 0.1, (n, bodies, 2))
+    x = (-9.0 + pitch * (gx + 0.5) + jit[..., 0]).astype(F32)
+    y = (-9.0 + pitch * (gy + 0.5) + jit[..., 1]).astype(F32)
+    sc.dyn = dict(kind=kind, size=size, nv=nv, poly=poly, mass=mass, center=center, inertia=inertia,
+                  restitution=rng.uniform(0, 0.3, bodies).astype(F32), x=x, y=y,
+                  angle=wr.uniform(0, 2 * np.pi, (n, bodies)).astype(F32))
+    sc.builder = _c2_bodies
+    return sc
+
+
+# ---- c3: 32 bullet circles among thin static targets
+
+
+def _c3_bodies(defn, sc, i):
+    d = sc.dyn
+    for k in range(32):
+        b = defn.add_body(DYNAMIC, (float(d["x"][i, k]), float(d["y"][i, k])), 0.0,
+                          (float(d["vx"][i, k]), float(d["vy"][i, k])), 0.0, mass=F32(0.0785), inertia=F32(0.0001),
+                          bullet=True)
+        defn.add_circle(b, 0.05, friction=0.2)
+
+
+def c3(seed=0, n=8192):
+    rng = np.random.default_rng(seed)
+    sc = Scene("c3_toi", _settings(True), 64, 300, n)
+    boxes = [((10.0, 0.01), (0.0, -10.0), 0.0, 0.3), ((10.0, 0.01), (0.0, 10.0), 0.0, 0.3),
+             ((0.01, 10.0), (-10.0, 0.0), 0.0, 0.3), ((0.01, 10.0), (10.0, 0.0), 0.0, 0.3)]
+    for _ in range(12):
+        boxes.append(((float(rng.uniform(0.5, 2.0)), 0.01), (float(rng.uniform(-8, 8)), float(rng.uniform(-8, 8))),
+                      float(rng.uniform(0, np.pi)), 0.3))
+    for _ in range(64):  # zero-thickness edges as 0.02 m thick boxes
+        boxes.append(((float(rng.uniform(0.25, 1.5)), 0.01), (float(rng.uniform(-9, 9)), float(rng.uniform(-9, 9))),
+                      float(rng.uniform(0, np.pi)), 0.3))
+    sc.static_boxes = boxes
+    wr = np.random.default_rng([seed, 1])
+    speed = wr.uniform(50, 200, (n, 32))
+    th = wr.uniform(0, 2 * np.pi, (n, 32))
+    sc.dyn = dict(x=wr.uniform(-9.5, 9.5, (n, 32)).astype(F32), y=wr.uniform(-9.5, 9.5, (n, 32)).astype(F32),
+                  vx=(speed * np.cos(th)).astype(F32), vy=(speed * np.sin(th)).astype(F32))
+    sc.builder = _c3_bodies
+    return sc
+
+
+# ---- c4: the c1 rig plus a 20-link revolute chain hanging from a static anchor
+
+
+def _c4_bodies(defn, sc, i):
+    d = sc.dyn
+    x, y = float(d["x"][i]), float(d["y"][i])
+    _rig(defn, sc, i, x, y, float(d["angle"][i]))
+    ax, ay = sc.anchor  # one anchor for every world: static bodies are shared by the batch
+    anchor = defn.add_body(STATIC, (ax, ay))
+    defn.add_box(anchor, (0.1, 0.1))
+    prev, px = anchor, ax
+    for k in range(20):
+        ly = ay - 0.5 * (k + 1)
+        link = defn.add_body(DYNAMIC, (px, ly), 0.0, mass=0.5, inertia=F32(0.5) * F32(0.26) / F32(12.0))
+        defn.add_box(link, (0.05, 0.25), friction=0.5)
+        defn.add_revolute(prev, link, (0, -0.1 if k == 0 else -0.25), (0, 0.25), 0.0)
+        prev = link
+
+
+def c4(seed=0, n=65536):
+    sc = c1(seed, n)
+    sc.name, sc.capacity, sc.steps = "c4_scale", 48, 10000
+    sc.builder = _c4_bodies
+    h, x0, dx = sc.level
+    ix = int((20.0 - x0) / dx)
+    sc.anchor = (20.0, float(h[ix]) + 12.0)
+    return sc
+
+
+CONFIGS = {"c0": c0, "c1": c1, "c2": c2, "c3": c3, "c4": c4}
+
+
+def scene(name, seed=0, n=None):
+    fn = CONFIGS[name]
+    return fn(seed) if n is None else fn(seed, n)
+
+
+# ---- batches
+
+
+def batch(name, n, seed=0, compact=True):
+    """(scene, Model, batched State (leaves (n, ...))) for n worlds of a workload. The Model comes from world 0's
+    full build; each world's bodies, joints and dynamic-fixture AABBs come from replaying that world's dynamic
+    builder calls on a WorldDef holding only the ground body, so every world equals its full WorldDef build (the
+    static level is identical in all of them). compact: the compact fixture layout (static fixtures in the Model)."""
+    from .world import Fixtures, State, compact_model, compact_state, empty_contacts, empty_toi
+
+    sc = scene(name, seed, n)
+    full = sc.world_def(0)
+    model, st0 = full.build(sc.capacity)
+    n_static = len(sc.static_polys) + len(sc.static_boxes)
+    geom = full.fixture_geometry()
+    per = []
+    for i in range(n):
+        d = WorldDef(sc.settings)
+        d.add_body(STATIC)
+        sc.builder(d, sc, i)
+        bodies = d.body_arrays()
+        fx = d.fixture_arrays(bodies)
+        per.append((bodies, fx, d.joint_arrays()))
+    stack = lambda xs: np.stack(xs, 0)  # noqa: E731
+    bodies = type(st0.bodies)(*(stack([p[0][k] for p in per]) for k in range(len(st0.bodies))))
+    joints = type(st0.joints)(*(stack([p[2][k] for p in per]) for k in range(len(st0.joints))))
+    fat = np.broadcast_to(st0.fixtures.fat, (n,) + st0.fixtures.fat.shape).copy()
+    fat[:, n_static:] = stack([p[1].fat for p in per])
+    fixtures = Fixtures(friction=np.broadcast_to(st0.fixtures.friction, (n,) + st0.fixtures.friction.shape).copy(),
+                        restitution=np.broadcast_to(st0.fixtures.restitution,
+                                                    (n,) + st0.fixtures.restitution.shape).copy(), fat=fat)
+    del geom
+    rep = lambda x: np.broadcast_to(x, (n,) + np.shape(x)).copy()  # noqa: E731
+    C, B = sc.capacity, bodies.type.shape[1]
+    contacts = type(st0.contacts)(*(rep(x) for x in empty_contacts(C)))
+    toi = type(st0.toi)(*(rep(x) for x in empty_toi(B, C)))
+    state = State(bodies=bodies, fixtures=fixtures, joints=joints, contacts=contacts, gravity=rep(st0.gravity),
+                  inv_dt0=rep(st0.inv_dt0), next_key=rep(st0.next_key), new_fixture=rep(st0.new_fixture),
+                  overflow=rep(st0.overflow), toi=toi)
+    if compact:
+        model = compact_model(model, state)
+        state = compact_state(model, state, check=False)
+    return sc, model, state

@@ -1,0 +1,136 @@
+/* goib2d: batched Box2D 2.3.1 world step on NVIDIA B200 (sm_100a) - the C ABI of libgoib2d.so.
+ *
+ * The library replaces the batched step of the reference engine goi_jax/box2d (miwate/getting-over-it-rl):
+ *   - goi_jax/box2d/step.py:28        step(model, state, settings, dt, axis_name)   one b2World::Step per world;
+ *   - goi_jax/box2d/gpu/kernel.py:573-599, gpu/pairs.py:242-259, gpu/islands.py:273-286,
+ *     gpu/toi_search.py:567-581, gpu/toi_event.py:732-743   the jax.custom_batching.custom_vmap batch rules that
+ *     receive the whole batch of worlds and launch one kernel over it. A JAX FFI handler registered for
+ *     "goib2d_step" calls goib2d_step() from exactly that seam (INTEGRATION.md shows the binding).
+ *
+ * Data contract. A batch of N worlds shares one Model (scene constants; uploaded once, goib2d_model_create) and
+ * owns one State: GOIB2D_NUM_LEAVES arrays ("leaves"), each laid out (N, ...) row-major - the layout of the
+ * reference's State pytree under jax.vmap, leaf order as in goib2d/world.py leaf_names(). Per world the leaf holds
+ * the element counts given by goib2d_leaf_elems(). bool leaves are one byte (0/1), int leaves int32, float leaves
+ * float32. goib2d_step() reads and writes the leaves in place (device pointers); the library never keeps a caller
+ * pointer past a call.
+ *
+ * Errors: every entry point returns 0 on success and a negative GOIB2D_E* code otherwise, with a message for
+ * goib2d_last_error() (thread-local). Per-world conditions (contact table overflow, non-finite state, an iteration
+ * cap reached) are reported in the State (State.overflow) and by goib2d_status(), never by trapping the GPU.
+ */
+#ifndef GOIB2D_H
+#define GOIB2D_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GOIB2D_ABI_VERSION 1
+
+#define GOIB2D_OK 0
+#define GOIB2D_EINVAL (-1)   /* bad argument (null pointer, size out of range, inconsistent layout) */
+#define GOIB2D_ECUDA (-2)    /* a CUDA runtime call failed */
+#define GOIB2D_ENOMEM (-3)   /* device allocation failed */
+#define GOIB2D_ELIMIT (-4)   /* a capacity the kernels support was exceeded */
+
+/* b2Settings globals + b2World flags; field for field goib2d.settings.SettingsC and the reference's Settings
+ * dataclass (goi_jax/box2d/settings.py:109-148). */
+typedef struct goib2d_settings {
+    float gravity_x, gravity_y;
+    float linear_slop, angular_slop, polygon_radius, velocity_threshold;
+    float max_linear_correction, max_angular_correction, max_translation, max_rotation;
+    float baumgarte, toi_baumgarte, time_to_sleep, linear_sleep_tolerance, angular_sleep_tolerance;
+    int32_t velocity_iterations, position_iterations;
+    int32_t clamps_per_second, allow_sleep, warm_starting, continuous_physics, unity_toi, toi_tie_oldest;
+    int32_t auto_clear_forces, revolute_v24;
+} goib2d_settings;
+
+/* The scene constants of goi_jax/box2d/world.py:30-67 (Model), as host arrays. fixture_slot == NULL: full fixture
+ * layout (State.fixtures has one row per fixture); otherwise the compact layout (reference world.py:437-472): rows
+ * only for fixtures of non-static bodies, static_* hold the static fixtures' values. */
+typedef struct goib2d_model_desc {
+    int32_t n_bodies, n_fixtures, n_joints, n_pairs;
+    const int32_t *fixture_body, *shape_type, *count;   /* [F] */
+    const float *radius;                                /* [F] */
+    const float *verts, *normals;                       /* [F][8][2] */
+    const int32_t *joint_type, *joint_a, *joint_b;      /* [J] */
+    const float *local_anchor_a, *local_anchor_b;       /* [J][2] */
+    const float *local_axis_a, *local_yaxis_a;          /* [J][2] */
+    const float *reference_angle;                       /* [J] */
+    const int32_t *pair_a, *pair_b;                     /* [P], b2BroadPhase::UpdatePairs order */
+    const uint8_t *toi_bodies;                          /* [B] bullet|continuous at build; NULL = unknown */
+    const int32_t *fixture_slot;                        /* [F] or NULL */
+    const float *static_fat;                            /* [F][4] (compact layout) */
+    const float *static_friction, *static_restitution;  /* [F]    (compact layout) */
+} goib2d_model_desc;
+
+/* State leaves, in order (goib2d/world.py STATE_LEAVES). */
+enum goib2d_leaf {
+    /* Bodies [B] */
+    GOIB2D_B_TYPE, GOIB2D_B_ACTIVE, GOIB2D_B_AWAKE, GOIB2D_B_ALLOW_SLEEP, GOIB2D_B_BULLET, GOIB2D_B_CONTINUOUS,
+    GOIB2D_B_SLEEP_TIME, GOIB2D_B_XF_P, GOIB2D_B_XF_Q, GOIB2D_B_LOCAL_CENTER, GOIB2D_B_C0, GOIB2D_B_C,
+    GOIB2D_B_A0, GOIB2D_B_A, GOIB2D_B_V, GOIB2D_B_W, GOIB2D_B_FORCE, GOIB2D_B_TORQUE, GOIB2D_B_MASS,
+    GOIB2D_B_INV_MASS, GOIB2D_B_INERTIA, GOIB2D_B_INV_INERTIA, GOIB2D_B_LINEAR_DAMPING, GOIB2D_B_ANGULAR_DAMPING,
+    GOIB2D_B_GRAVITY_SCALE,
+    /* Fixtures [rows] */
+    GOIB2D_F_FRICTION, GOIB2D_F_RESTITUTION, GOIB2D_F_FAT,
+    /* Joints [J] */
+    GOIB2D_J_ENABLE_MOTOR, GOIB2D_J_MOTOR_SPEED, GOIB2D_J_MAX_MOTOR, GOIB2D_J_ENABLE_LIMIT, GOIB2D_J_LOWER,
+    GOIB2D_J_UPPER, GOIB2D_J_FREQUENCY, GOIB2D_J_DAMPING, GOIB2D_J_IMPULSE, GOIB2D_J_MOTOR_IMPULSE,
+    GOIB2D_J_LIMIT_STATE, GOIB2D_J_LOWER_IMPULSE, GOIB2D_J_UPPER_IMPULSE,
+    /* Contacts [C] */
+    GOIB2D_C_PAIR, GOIB2D_C_FA, GOIB2D_C_FB, GOIB2D_C_KEY, GOIB2D_C_TOUCHING, GOIB2D_C_MTYPE, GOIB2D_C_COUNT,
+    GOIB2D_C_LOCAL_NORMAL, GOIB2D_C_LOCAL_POINT, GOIB2D_C_POINT_LOCAL, GOIB2D_C_POINT_ID, GOIB2D_C_NORMAL_IMPULSE,
+    GOIB2D_C_TANGENT_IMPULSE, GOIB2D_C_FRICTION, GOIB2D_C_RESTITUTION, GOIB2D_C_TANGENT_SPEED,
+    /* world scalars */
+    GOIB2D_GRAVITY, GOIB2D_INV_DT0, GOIB2D_NEXT_KEY, GOIB2D_NEW_FIXTURE, GOIB2D_OVERFLOW,
+    /* ContactTOI */
+    GOIB2D_T_ALPHA0, GOIB2D_T_COUNT, GOIB2D_T_TOI, GOIB2D_T_FLAG, GOIB2D_T_ENABLED, GOIB2D_T_SOLVED,
+    GOIB2D_T_NORMAL_IMPULSE, GOIB2D_T_TANGENT_IMPULSE, GOIB2D_T_EVENTS,
+    GOIB2D_NUM_LEAVES
+};
+
+/* Element type of a leaf: 0 float32, 1 int32, 2 bool (uint8). */
+int goib2d_leaf_dtype(int leaf);
+
+/* Elements per world of a leaf for a model with B bodies, `rows` fixture rows, J joints and C contact slots. */
+int64_t goib2d_leaf_elems(int leaf, int32_t B, int32_t rows, int32_t J, int32_t C);
+
+typedef struct goib2d_model goib2d_model;
+
+/* ABI version (GOIB2D_ABI_VERSION). */
+int goib2d_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *goib2d_last_error(void);
+
+/* Upload a Model to the current CUDA device and build the device-side broadphase tables. Replaces passing the
+ * Model as a jit argument (scripts/bench_gpu.py:76-84): one handle per scene, shared by every world. */
+int goib2d_model_create(const goib2d_model_desc *desc, goib2d_model **out);
+int goib2d_model_destroy(goib2d_model *model);
+
+/* Optional action channels (an RL env's per-step input): before each step, joints.motor_speed[joint[k]] of world w
+ * = scale[k] * actions[w * n + k]. n == 0 clears the map. */
+int goib2d_model_set_action_map(goib2d_model *model, int32_t n, const int32_t *joint, const float *scale);
+
+/* Step n_worlds worlds n_steps times: b2World::Step (reference step.py:28-47) per world, in place on the State
+ * leaves (device pointers, leaves[GOIB2D_NUM_LEAVES]). contact_capacity = C, fixture_rows = F (full layout) or the
+ * number of non-static fixtures (compact). actions: NULL, or device float32 [n_worlds][n_action] used before every
+ * step (goib2d_model_set_action_map). stream: a cudaStream_t (NULL = the legacy default stream). Asynchronous:
+ * returns after enqueueing the launches on `stream`. */
+int goib2d_step(goib2d_model *model, const goib2d_settings *settings, float dt, int32_t contact_capacity,
+                int32_t fixture_rows, int64_t n_worlds, int32_t n_steps, void *const *leaves, const float *actions,
+                void *stream);
+
+/* Per-world status words of the last goib2d_step on this model (device int32 [n_worlds]; bit 0 contact table
+ * overflow in this step, bit 1 non-finite body state, bit 2 an iteration cap was reached, bit 3 a capacity of the
+ * kernels' on-chip tables was exceeded). Valid until the next goib2d_step with this model. */
+int goib2d_status(goib2d_model *model, const int32_t **device_status, int64_t *n_worlds);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GOIB2D_H */

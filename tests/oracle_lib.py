@@ -1,0 +1,83 @@
+"""The parity oracle (oracle/liboracle_goib2d.so, a C++ restatement of the reference engine) through ctypes.
+
+Test and CPU-baseline infrastructure only: it steps numpy States (leading world axis) in place on the host."""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+from goib2d import native
+from goib2d.settings import settings_struct
+from goib2d.world import state_from_leaves, state_leaves
+
+ORACLE_DIR = Path(__file__).resolve().parents[1] / "oracle"
+LIB = ORACLE_DIR / "liboracle_goib2d.so"
+_lib = None
+
+
+def load(build=True):
+    global _lib
+    if _lib is not None:
+        return _lib
+    if build:
+        subprocess.run(["make", "-s", "-C", str(ORACLE_DIR)], check=True)
+    lib = C.CDLL(str(LIB))
+    vp = C.c_void_p
+    lib.oracle_step_batch.restype = C.c_int
+    lib.oracle_step_batch.argtypes = [C.POINTER(native.ModelDesc), vp, C.c_float, C.c_int32, C.c_int32, C.c_int64,
+                                      C.c_int32, C.POINTER(vp), vp, C.c_int32, vp, vp, C.c_int32]
+    lib.oracle_sin_cos.argtypes = [vp, C.c_int64, vp, vp]
+    lib.oracle_max_threads.restype = C.c_int
+    lib.oracle_leaf_elems.restype = C.c_int64
+    lib.oracle_leaf_elems.argtypes = [C.c_int, C.c_int32, C.c_int32, C.c_int32, C.c_int32]
+    lib.oracle_leaf_dtype.argtypes = [C.c_int]
+    _lib = lib
+    return lib
+
+
+def batched(state):
+    """A State with a leading world axis (a single-world State gets one)."""
+    if np.asarray(state.bodies.type).ndim == 1:
+        return state_from_leaves([np.ascontiguousarray(np.asarray(x)[None]) for x in state_leaves(state)])
+    return state_from_leaves([np.ascontiguousarray(np.asarray(x)) for x in state_leaves(state)])
+
+
+def step(model, state, settings, dt, n_steps=1, threads=0, actions=None, action_joints=(), action_scale=()):
+    """Step a copy of `state` (numpy, batched or single world) n_steps times; returns the new State."""
+    lib = load()
+    single = np.asarray(state.bodies.type).ndim == 1
+    st = batched(state)
+    leaves = [np.ascontiguousarray(x).copy() for x in state_leaves(st)]
+    N, B = leaves[0].shape[0], leaves[0].shape[1]
+    rows = st.fixtures.friction.shape[1]
+    J = st.joints.motor_speed.shape[1]
+    Cc = st.contacts.pair.shape[1]
+    pm = native.model_desc(model, B)
+    ss = settings_struct(settings)
+    ptrs = (C.c_void_p * len(leaves))(*[x.ctypes.data for x in leaves])
+    act = aj = asc = None
+    na = 0
+    if actions is not None:
+        actions = np.ascontiguousarray(actions, np.float32)
+        na = actions.shape[1]
+        aj = np.ascontiguousarray(action_joints, np.int32)
+        asc = np.ascontiguousarray(action_scale, np.float32)
+        act, aj_p, asc_p = actions.ctypes.data, aj.ctypes.data, asc.ctypes.data
+    else:
+        aj_p = asc_p = None
+    rc = lib.oracle_step_batch(C.byref(pm.desc), C.addressof(ss), C.c_float(dt), Cc, rows, N, n_steps, ptrs, act,
+                               na, aj_p, asc_p, threads)
+    assert rc == 0
+    out = state_from_leaves(leaves)
+    if single:
+        out = state_from_leaves([x[0] for x in leaves])
+    return out
+
+
+def sin_cos(x):
+    lib = load()
+    x = np.ascontiguousarray(x, np.float32)
+    s, c = np.empty_like(x), np.empty_like(x)
+    lib.oracle_sin_cos(x.ctypes.data, x.size, s.ctypes.data, c.ctypes.data)
+    return s, c
