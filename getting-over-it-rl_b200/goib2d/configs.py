@@ -25,6 +25,13 @@ DT = F32(0.02)
 GRAVITY = (F32(0.0), F32(-9.81))
 
 
+def _per_world(seed, n, draw):
+    """Stack draw(rng) over worlds 0..n-1, each world with its own generator seeded (seed, 1, i): world i's values
+    do not depend on the batch size."""
+    rows = [draw(np.random.default_rng([seed, 1, i])) for i in range(n)]
+    return {k: np.stack([r[k] for r in rows], 0) for k in rows[0]}
+
+
 def _settings(continuous, allow_sleep=True):
     return Settings.stock(gravity=GRAVITY, velocity_iterations=8, position_iterations=3,
                           continuous_physics=continuous, allow_sleep=allow_sleep)
@@ -117,9 +124,9 @@ def c0(seed=0, n=256):
     x0, dx = -32.0, 0.5
     sc = Scene("c0_box_drop", _settings(False), 64, 600, n)
     sc.static_polys = _terrain_quads(h, x0, dx, -2.0, 0.6)
-    wr = np.random.default_rng([seed, 1])
-    sc.dyn = dict(x=wr.uniform(x0 + 1, x0 + 127 * dx - 1, (n, 8)).astype(F32),
-                  y=wr.uniform(2, 6, (n, 8)).astype(F32), angle=wr.uniform(0, 2 * np.pi, (n, 8)).astype(F32))
+    sc.dyn = _per_world(seed, n, lambda r: dict(x=r.uniform(x0 + 1, x0 + 127 * dx - 1, 8).astype(F32),
+                                               y=r.uniform(2, 6, 8).astype(F32),
+                                               angle=r.uniform(0, 2 * np.pi, 8).astype(F32)))
     sc.builder = _c0_bodies
     return sc
 
@@ -168,11 +175,11 @@ def _level_c1(rng, friction=0.7):
     return h, x0, dx, polys
 
 
-def _rig_starts(h, x0, dx, wr, n):
-    x = wr.uniform(x0 + 10, x0 + 2000 * dx - 10, n)
-    ix = ((x - x0) / dx).astype(int)
-    y = np.maximum(h[ix], h[ix + 1]).astype(np.float64) + 0.7 + 0.02
-    return x.astype(F32), y.astype(F32), wr.uniform(0, 2 * np.pi, n).astype(F32)
+def _rig_start(h, x0, dx, r):
+    x = r.uniform(x0 + 10, x0 + 2000 * dx - 10)
+    ix = int((x - x0) / dx)
+    y = max(float(h[ix]), float(h[ix + 1])) + 0.7 + 0.02
+    return dict(x=F32(x), y=F32(y), angle=F32(r.uniform(0, 2 * np.pi)), w0=F32(r.uniform(-2, 2)))
 
 
 def c1(seed=0, n=4096):
@@ -180,9 +187,7 @@ def c1(seed=0, n=4096):
     h, x0, dx, polys = _level_c1(rng)
     sc = Scene("c1_rig", _settings(True), 32, 1000, n)
     sc.static_polys = polys
-    wr = np.random.default_rng([seed, 1])
-    x, y, ang = _rig_starts(h, x0, dx, wr, n)
-    sc.dyn = dict(x=x, y=y, angle=ang, w0=wr.uniform(-2, 2, n).astype(F32))
+    sc.dyn = _per_world(seed, n, lambda r: _rig_start(h, x0, dx, r))
     sc.builder = _c1_bodies
     sc.level = (h, x0, dx)
     sc.action_joints, sc.action_scale = (0, 1), (4.0, 2.0)
@@ -238,13 +243,13 @@ def c2(seed=0, n=1024, bodies=256):
     gx, gy = np.meshgrid(np.arange(side), np.arange(side))
     gx, gy = gx.ravel()[:bodies], gy.ravel()[:bodies]
     pitch = 18.0 / side
-    wr = np.random.default_rng([seed, 1])
-    jit = wr.uniform(-0.1, 0.1, (n, bodies, 2))
-    x = (-9.0 + pitch * (gx + 0.5) + jit[..., 0]).astype(F32)
-    y = (-9.0 + pitch * (gy + 0.5) + jit[..., 1]).astype(F32)
+    def draw(r):
+        jit = r.uniform(-0.1, 0.1, (bodies, 2))
+        return dict(x=(-9.0 + pitch * (gx + 0.5) + jit[:, 0]).astype(F32),
+                    y=(-9.0 + pitch * (gy + 0.5) + jit[:, 1]).astype(F32),
+                    angle=r.uniform(0, 2 * np.pi, bodies).astype(F32))
     sc.dyn = dict(kind=kind, size=size, nv=nv, poly=poly, mass=mass, center=center, inertia=inertia,
-                  restitution=rng.uniform(0, 0.3, bodies).astype(F32), x=x, y=y,
-                  angle=wr.uniform(0, 2 * np.pi, (n, bodies)).astype(F32))
+                  restitution=rng.uniform(0, 0.3, bodies).astype(F32), **_per_world(seed, n, draw))
     sc.builder = _c2_bodies
     return sc
 
@@ -273,11 +278,11 @@ def c3(seed=0, n=8192):
         boxes.append(((float(rng.uniform(0.25, 1.5)), 0.01), (float(rng.uniform(-9, 9)), float(rng.uniform(-9, 9))),
                       float(rng.uniform(0, np.pi)), 0.3))
     sc.static_boxes = boxes
-    wr = np.random.default_rng([seed, 1])
-    speed = wr.uniform(50, 200, (n, 32))
-    th = wr.uniform(0, 2 * np.pi, (n, 32))
-    sc.dyn = dict(x=wr.uniform(-9.5, 9.5, (n, 32)).astype(F32), y=wr.uniform(-9.5, 9.5, (n, 32)).astype(F32),
-                  vx=(speed * np.cos(th)).astype(F32), vy=(speed * np.sin(th)).astype(F32))
+    def draw(r):
+        speed, th = r.uniform(50, 200, 32), r.uniform(0, 2 * np.pi, 32)
+        return dict(x=r.uniform(-9.5, 9.5, 32).astype(F32), y=r.uniform(-9.5, 9.5, 32).astype(F32),
+                    vx=(speed * np.cos(th)).astype(F32), vy=(speed * np.sin(th)).astype(F32))
+    sc.dyn = _per_world(seed, n, draw)
     sc.builder = _c3_bodies
     return sc
 
