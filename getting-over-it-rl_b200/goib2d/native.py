@@ -68,18 +68,18 @@ def model_desc(model, n_bodies):
 
 # State leaf table: (dtype, entity, width) with entity one of "B", "rows", "J", "C", "1"
 _LEAF_SPEC = (
-    [(np.int32, "B", 1)] + [(np.uint8, "B", 1)] * 5 + [(np.float32, "B", 1)] + [(np.float32, "B", 2)] * 5 +
+    [(np.int32, "B", 1)] + [(np.bool_, "B", 1)] * 5 + [(np.float32, "B", 1)] + [(np.float32, "B", 2)] * 5 +
     [(np.float32, "B", 1)] * 2 + [(np.float32, "B", 2), (np.float32, "B", 1), (np.float32, "B", 2),
                                   (np.float32, "B", 1)] + [(np.float32, "B", 1)] * 7 +
     [(np.float32, "rows", 1), (np.float32, "rows", 1), (np.float32, "rows", 4)] +
-    [(np.uint8, "J", 1), (np.float32, "J", 1), (np.float32, "J", 1), (np.uint8, "J", 1)] + [(np.float32, "J", 1)] * 4 +
+    [(np.bool_, "J", 1), (np.float32, "J", 1), (np.float32, "J", 1), (np.bool_, "J", 1)] + [(np.float32, "J", 1)] * 4 +
     [(np.float32, "J", 3), (np.float32, "J", 1), (np.int32, "J", 1), (np.float32, "J", 1), (np.float32, "J", 1)] +
-    [(np.int32, "C", 1)] * 4 + [(np.uint8, "C", 1), (np.int32, "C", 1), (np.int32, "C", 1)] +
+    [(np.int32, "C", 1)] * 4 + [(np.bool_, "C", 1), (np.int32, "C", 1), (np.int32, "C", 1)] +
     [(np.float32, "C", 2), (np.float32, "C", 2), (np.float32, "C", 4), (np.int32, "C", 2), (np.float32, "C", 2),
      (np.float32, "C", 2)] + [(np.float32, "C", 1)] * 3 +
-    [(np.float32, "1", 2), (np.float32, "1", 1), (np.int32, "1", 1), (np.uint8, "1", 1), (np.int32, "1", 1)] +
-    [(np.float32, "B", 1), (np.int32, "C", 1), (np.float32, "C", 1), (np.uint8, "C", 1), (np.uint8, "C", 1),
-     (np.uint8, "C", 1), (np.float32, "C", 2), (np.float32, "C", 2), (np.int32, "1", 1)])
+    [(np.float32, "1", 2), (np.float32, "1", 1), (np.int32, "1", 1), (np.bool_, "1", 1), (np.int32, "1", 1)] +
+    [(np.float32, "B", 1), (np.int32, "C", 1), (np.float32, "C", 1), (np.bool_, "C", 1), (np.bool_, "C", 1),
+     (np.bool_, "C", 1), (np.float32, "C", 2), (np.float32, "C", 2), (np.int32, "1", 1)])
 assert len(_LEAF_SPEC) == len(leaf_names()) == 71
 
 # leaves whose per-world shape is (n, width) rather than (n,) / (2, 2) for point_local
