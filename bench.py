@@ -1,0 +1,274 @@
+"""world-steps/s of the batched Box2D step on B200 (BASELINE.json's metric), one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--worlds 4096] [--impl ours|reference]
+
+Workload: BASELINE.json configs[1] (the character rig: pot, hub and bullet hammer on a revolute motor and a
+prismatic slide, over a 2000-segment chain level with 60 rocks), polygon-terrain variant (the reference engine has
+no edge/chain shapes), seeded synthetic worlds (goib2d/configs.py), 4096 worlds per GPU, dt 0.02, 8/3 iterations,
+continuous physics on. A step = one b2World::Step of every world (one kernel launch), with per-world actions from a
+disc of radius 2 driving the two joint motors. L2 is flushed (a 256 MiB write) between timed steps; each step is
+timed with CUDA events on the launching stream and the K durations are summed; max over ranks.
+
+--impl reference: the reference engine's algorithm on the host cores - the parity oracle (oracle/, a C++
+restatement of goi_jax/box2d, bit-identical to it on every golden vector) on all host threads, over a bounded sample
+of the same workload. The reference's own JAX engine cannot run here (no jax/jaxlib in the image).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "getting-over-it-rl_b200"))
+sys.path.insert(0, str(ROOT / "tests"))
+
+METRIC = "world-steps/sec"
+UNIT = "world-steps/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c1", choices=("c0", "c1", "c2", "c3", "c4"))
+    ap.add_argument("--worlds", type=int, default=None, help="worlds per GPU (default: the config's N)")
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-sample-worlds", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def actions_for(n, steps, seed, first=0):
+    """Per-world, per-step targets on a disc of radius 2, uniform in area (r = 2 sqrt(u), theta = 2 pi v)."""
+    rng = np.random.default_rng([seed, 7, first])
+    u, v = rng.uniform(0, 1, (steps, n)), rng.uniform(0, 1, (steps, n))
+    r, th = 2.0 * np.sqrt(u), 2.0 * np.pi * v
+    return np.stack([r * np.cos(th), r * np.sin(th)], -1).astype(np.float32)  # (steps, n, 2)
+
+
+def state_bytes(state):
+    """Algorithmic bytes of one world-step: the per-world State read once and written once (compact layout)."""
+    from goib2d import native
+    B, rows = state.bodies.type.shape[1], state.fixtures.friction.shape[1]
+    J, C = state.joints.motor_speed.shape[1], state.contacts.pair.shape[1]
+    return 2 * native.state_bytes_per_world(B, rows, J, C)
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc = index, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm = [float(r[1]) for r in rows if len(r) > 8 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 8 and r[2].strip().replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows if len(r) > 8 for n, v in zip(names, r[5:9]) if "Active" in v and
+                          "Not" not in v})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_baseline(sc, model, host, n_sample, steps, threads=0):
+    """The parity oracle on the host cores over a bounded sample (the first n_sample worlds, `steps` steps)."""
+    import oracle_lib
+    from goib2d import configs
+    from goib2d.world import map_state
+    sample = map_state(lambda x: np.ascontiguousarray(np.asarray(x)[:n_sample]), host)
+    lib = oracle_lib.load(build=False)
+    threads = threads or lib.oracle_max_threads()
+    acts = actions_for(n_sample, steps, 0)
+    t0 = time.perf_counter()
+    st = sample
+    for k in range(steps):
+        st = oracle_lib.step(model, st, sc.settings, configs.DT, 1, threads=threads, actions=acts[k],
+                             action_joints=sc.action_joints, action_scale=sc.action_scale)
+    dt = time.perf_counter() - t0
+    return {"value": n_sample * steps / dt, "unit": UNIT, "cores": int(threads), "kind": "port",
+            "sample": f"{n_sample} worlds x {steps} steps of {sc.name} (the first worlds of the workload)"}
+
+
+def run_reference(args, rank):
+    """--impl reference: rank 0 times the oracle (the reference's algorithm, C++) on the host cores."""
+    if rank != 0:
+        return
+    import oracle_lib
+    from goib2d import configs
+    n = args.cpu_sample_worlds
+    sc, model, host = configs.batch(args.config, n, args.seed)
+    oracle_lib.load(build=not (ROOT / "oracle" / "liboracle_goib2d.so").exists())
+    steps = max(1, min(args.steps, 20))
+    for _ in range(min(args.warmup, 1)):
+        cpu_baseline(sc, model, host, min(n, 32), 1)
+    cb = cpu_baseline(sc, model, host, n, steps)
+    v = cb["value"]
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * n / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded, goib2d/configs.py)", "impl": "reference",
+            "config": {"workload": f"{sc.name} (BASELINE configs[1], polygon-terrain variant)",
+                       "worlds": n, "dt": float(configs.DT), "iterations": "8/3", "continuous_physics": True},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's JAX engine is not installed here; its algorithm runs as the bit-identical C++ "
+                    "parity oracle (oracle/), all host threads"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world_size = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch
+    import torch.distributed as dist
+    from goib2d import api, configs
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world_size > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    n = args.worlds or configs.DEFAULT_N[args.config]
+    first = rank * n  # weak scaling: every rank steps its own n seeded worlds
+    sc, model, host = configs.batch(args.config, n, args.seed, first=first)
+    eng = api.Engine(model, host.bodies.type.shape[1], sc.action_joints, sc.action_scale)
+    state = api.to_device(host, dev)
+    K, Wm = args.steps, args.warmup
+    na = len(sc.action_joints)
+    acts_host = actions_for(n, K + Wm, args.seed, first) if na else None
+    acts = torch.from_numpy(acts_host).to(dev) if na else None
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for k in range(Wm):
+        eng.step_(state, sc.settings, configs.DT, 1, acts[k] if na else None)
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    clocks = Clocks(local_rank)
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    wall0 = time.perf_counter()
+    for k in range(K):
+        flush.fill_(float(k))
+        starts[k].record(stream)
+        eng.step_(state, sc.settings, configs.DT, 1, acts[Wm + k] if na else None)
+        ends[k].record(stream)
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - wall0
+    if world_size > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = float(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
+    status = eng.status()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world_size > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world_size * n * K / (ms_max / 1e3)
+
+    # e2e through the public API with host buffers: per step, this step's actions from pinned host memory to the
+    # device, the step, and the pot's position (the env's observation) back to pinned host memory
+    Ke = max(3, min(K, 20))
+    a_pin = torch.from_numpy(actions_for(n, Ke, args.seed + 1, first)).pin_memory() if na else None
+    a_dev = torch.empty((n, max(na, 1)), dtype=torch.float32, device=dev)
+    obs_pin = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world_size > 1:
+        dist.barrier()
+    e0.record(stream)
+    for k in range(Ke):
+        if na:
+            a_dev.copy_(a_pin[k], non_blocking=True)
+        eng.step_(state, sc.settings, configs.DT, 1, a_dev if na else None)
+        obs_pin.copy_(state.bodies.c[:, 1], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world_size > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world_size * n * Ke / (float(te.item()) / 1e3)
+
+    # episode statistics gathered over NCCL (off the timed path): pot x position and status per world
+    stats = torch.stack([state.bodies.c[:, 1, 0], state.bodies.v[:, 1, 0],
+                         torch.from_numpy(status.astype(np.float32)).to(dev)], 1).contiguous()
+    if world_size > 1:
+        allst = [torch.empty_like(stats) for _ in range(world_size)]
+        dist.all_gather(allst, stats)
+        stats = torch.cat(allst)
+    nonfinite = int(((stats[:, 2].to(torch.int32) & 2) != 0).sum().item())
+
+    if rank == 0:
+        bytes_ws = state_bytes(state) + (8 if na else 0)
+        peak, peak_kind = measured_peak()
+        achieved = bytes_ws * n / (ms_max / 1e3 / K) / 1e9
+        traffic = None
+        tp = ROOT / "profiles" / f"traffic_{args.config}.json"
+        if tp.exists():
+            td = json.loads(tp.read_text())
+            traffic = td.get("dram_bytes_per_world_step", 0) * n
+        cpu = None
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline(sc, model, host, min(args.cpu_sample_worlds, n), 5)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": K, "warmup": Wm,
+            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded worlds, goib2d/configs.py)",
+            "config": {"workload": f"{sc.name} (BASELINE configs[1], polygon-terrain variant)",
+                       "worlds_per_gpu": n, "global_worlds": n * world_size, "dt": float(configs.DT),
+                       "iterations": "8/3", "continuous_physics": True, "contact_capacity": sc.capacity,
+                       "bodies": int(host.bodies.type.shape[1]), "fixtures": int(model.fixture_body.shape[0]),
+                       "candidate_pairs": int(model.pair_a.shape[0]), "parallelism": f"worlds sharded x{world_size}",
+                       "l2": "flushed between timed steps (256 MiB write), per-step CUDA events summed"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                         "algorithmic_bytes_per_world_step": bytes_ws},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": n * na * 4 * world_size,
+                    "d2h_bytes_per_step": n * 2 * 4 * world_size, "steps": Ke},
+            "gpu_launches": K, "clocks": clk, "wall_s_timed": wall, "nonfinite_worlds": nonfinite,
+            "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world_size > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,319 @@
+// goib2d C ABI (include/goib2d.h): model upload, scratch management, kernel launch, errors.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "engine.cuh"
+
+extern "C" __global__ void goib2d_step_kernel(const __grid_constant__ gb::StepParams p);
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                          \
+    do {                                                                                        \
+        cudaError_t e_ = (expr);                                                                \
+        if (e_ != cudaSuccess) return fail(GOIB2D_ECUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+    } while (0)
+
+struct LeafSpec {
+    int dtype, dim, width;  // dtype 0 f32 1 i32 2 bool; dim 0 B 1 rows 2 J 3 C 4 scalar
+};
+const LeafSpec LEAVES[GOIB2D_NUM_LEAVES] = {
+    {1, 0, 1}, {2, 0, 1}, {2, 0, 1}, {2, 0, 1}, {2, 0, 1}, {2, 0, 1}, {0, 0, 1}, {0, 0, 2}, {0, 0, 2}, {0, 0, 2},
+    {0, 0, 2}, {0, 0, 2}, {0, 0, 1}, {0, 0, 1}, {0, 0, 2}, {0, 0, 1}, {0, 0, 2}, {0, 0, 1}, {0, 0, 1}, {0, 0, 1},
+    {0, 0, 1}, {0, 0, 1}, {0, 0, 1}, {0, 0, 1}, {0, 0, 1},
+    {0, 1, 1}, {0, 1, 1}, {0, 1, 4},
+    {2, 2, 1}, {0, 2, 1}, {0, 2, 1}, {2, 2, 1}, {0, 2, 1}, {0, 2, 1}, {0, 2, 1}, {0, 2, 1}, {0, 2, 3}, {0, 2, 1},
+    {1, 2, 1}, {0, 2, 1}, {0, 2, 1},
+    {1, 3, 1}, {1, 3, 1}, {1, 3, 1}, {1, 3, 1}, {2, 3, 1}, {1, 3, 1}, {1, 3, 1}, {0, 3, 2}, {0, 3, 2}, {0, 3, 4},
+    {1, 3, 2}, {0, 3, 2}, {0, 3, 2}, {0, 3, 1}, {0, 3, 1}, {0, 3, 1},
+    {0, 4, 2}, {0, 4, 1}, {1, 4, 1}, {2, 4, 1}, {1, 4, 1},
+    {0, 0, 1}, {1, 3, 1}, {0, 3, 1}, {2, 3, 1}, {2, 3, 1}, {2, 3, 1}, {0, 3, 2}, {0, 3, 2}, {1, 4, 1}};
+
+// Per-world scratch arena: every array of the step's working set, 16-byte aligned, stride a multiple of 256 B.
+gb::Layout scratch_layout(int B, int C, int J, int P) {
+    gb::Layout L{};
+    int64_t off = 0;
+    auto take = [&](int64_t bytes) {
+        int64_t o = off;
+        off += (bytes + 15) & ~int64_t(15);
+        return o;
+    };
+    const int64_t b4 = 4 * (int64_t)(B > 0 ? B : 1), c4 = 4 * (int64_t)(C > 0 ? C : 1), j4 = 4 * (int64_t)(J > 0 ? J : 1);
+    L.vx = take(b4), L.vy = take(b4), L.vw = take(b4), L.cx = take(b4), L.cy = take(b4), L.ca = take(b4);
+    L.qc = take(b4), L.qs = take(b4);
+    L.aw = take(b4), L.bisl = take(b4), L.stack = take(b4), L.bflag = take(b4), L.last = take(b4);
+    L.moved = take(b4), L.done = take(b4), L.minsep = take(b4), L.jok = take(b4), L.islsleep = take(b4);
+    L.minst = take(b4), L.st = take(b4);
+    L.adv = take(8 * b4);
+    L.order = take(c4), L.lpos = take(c4), L.corder = take(c4), L.cisl = take(c4), L.cflag = take(c4);
+    L.freeslot = take(c4), L.active = take(c4), L.over = take(c4), L.edges = take(c4), L.tneed = take(c4);
+    L.tisl = take(c4), L.solved = take(c4);
+    L.man = take((int64_t)sizeof(gb::Man) * (C > 0 ? C : 1));
+    L.vc = take((int64_t)sizeof(gb::VCRow) * (C > 0 ? C : 1));
+    L.rec = take(8 * c4);
+    L.jr = take((int64_t)sizeof(gb::JRow) * (J > 0 ? J : 1));
+    L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
+    L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
+    L.stride = (off + 255) & ~int64_t(255);
+    return L;
+}
+
+template <class T>
+int upload(std::vector<void *> &allocs, const T *src, size_t n, const T **dst) {
+    *dst = nullptr;
+    size_t bytes = sizeof(T) * (n > 0 ? n : 1);
+    void *p = nullptr;
+    CUDA_TRY(cudaMalloc(&p, bytes));
+    allocs.push_back(p);
+    if (src && n) CUDA_TRY(cudaMemcpy(p, src, sizeof(T) * n, cudaMemcpyHostToDevice));
+    else CUDA_TRY(cudaMemset(p, 0, bytes));
+    *dst = (const T *)p;
+    return 0;
+}
+
+}  // namespace
+
+struct goib2d_model {
+    gb::DevModel full{}, compact{};  // the same model read through the full or the compact fixture layout
+    int has_compact = 0, n_rows_compact = 0;
+    int device = 0;
+    std::vector<void *> allocs;
+    char *scratch = nullptr;
+    size_t scratch_bytes = 0;
+    int32_t *status = nullptr;
+    int64_t status_cap = 0, status_n = 0;
+    int32_t n_action = 0;
+    int32_t *action_joint = nullptr;
+    float *action_scale = nullptr;
+    std::mutex mu;
+};
+
+extern "C" {
+
+int goib2d_version(void) { return GOIB2D_ABI_VERSION; }
+
+const char *goib2d_last_error(void) { return g_err.c_str(); }
+
+int goib2d_leaf_dtype(int leaf) {
+    if (leaf < 0 || leaf >= GOIB2D_NUM_LEAVES) return fail(GOIB2D_EINVAL, "leaf %d out of range", leaf);
+    return LEAVES[leaf].dtype;
+}
+
+int64_t goib2d_leaf_elems(int leaf, int32_t B, int32_t rows, int32_t J, int32_t C) {
+    if (leaf < 0 || leaf >= GOIB2D_NUM_LEAVES) return fail(GOIB2D_EINVAL, "leaf %d out of range", leaf);
+    const LeafSpec &s = LEAVES[leaf];
+    int64_t n = s.dim == 0 ? B : s.dim == 1 ? rows : s.dim == 2 ? J : s.dim == 3 ? C : 1;
+    return n * s.width;
+}
+
+int goib2d_model_create(const goib2d_model_desc *d, goib2d_model **out) {
+    if (!d || !out) return fail(GOIB2D_EINVAL, "null argument");
+    *out = nullptr;
+    const int B = d->n_bodies, F = d->n_fixtures, J = d->n_joints, P = d->n_pairs;
+    if (B < 0 || F < 0 || J < 0 || P < 0) return fail(GOIB2D_EINVAL, "negative model size");
+    if (F && (!d->fixture_body || !d->shape_type || !d->count || !d->radius || !d->verts || !d->normals))
+        return fail(GOIB2D_EINVAL, "fixture arrays missing");
+    if (J && (!d->joint_type || !d->joint_a || !d->joint_b || !d->local_anchor_a || !d->local_anchor_b ||
+              !d->local_axis_a || !d->local_yaxis_a || !d->reference_angle))
+        return fail(GOIB2D_EINVAL, "joint arrays missing");
+    if (P && (!d->pair_a || !d->pair_b)) return fail(GOIB2D_EINVAL, "pair arrays missing");
+    for (int f = 0; f < F; ++f) {
+        if (d->fixture_body[f] < 0 || d->fixture_body[f] >= B) return fail(GOIB2D_EINVAL, "fixture %d body", f);
+        if (d->count[f] < 1 || d->count[f] > gb::MAXV) return fail(GOIB2D_EINVAL, "fixture %d vertex count", f);
+        if (d->shape_type[f] != gb::CIRCLE && d->shape_type[f] != gb::POLYGON)
+            return fail(GOIB2D_EINVAL, "fixture %d shape type %d (circle and polygon only)", f, d->shape_type[f]);
+    }
+    for (int j = 0; j < J; ++j)
+        if (d->joint_a[j] < 0 || d->joint_a[j] >= B || d->joint_b[j] < 0 || d->joint_b[j] >= B)
+            return fail(GOIB2D_EINVAL, "joint %d bodies", j);
+    for (int p = 0; p < P; ++p)
+        if (d->pair_a[p] < 0 || d->pair_a[p] >= F || d->pair_b[p] < 0 || d->pair_b[p] >= F)
+            return fail(GOIB2D_EINVAL, "pair %d fixtures", p);
+    auto *m = new goib2d_model();
+    int rc = 0;
+    cudaGetDevice(&m->device);
+    gb::DevModel &g = m->full;
+    g.B = B, g.F = F, g.J = J, g.P = P;
+    std::vector<int32_t> ident(F > 0 ? F : 1);
+    for (int f = 0; f < F; ++f) ident[f] = f;
+    int any_toi = 0;
+    if (d->toi_bodies) {
+        for (int b = 0; b < B; ++b) any_toi |= d->toi_bodies[b] != 0;
+    } else {
+        any_toi = 1;
+    }
+    g.any_toi_body = any_toi;
+#define UP(field, n) \
+    if (!rc) rc = upload(m->allocs, d->field, (size_t)(n), &g.field)
+    UP(fixture_body, F);
+    UP(shape_type, F);
+    UP(count, F);
+    UP(radius, F);
+    UP(verts, 16 * (size_t)F);
+    UP(normals, 16 * (size_t)F);
+    UP(joint_type, J);
+    UP(joint_a, J);
+    UP(joint_b, J);
+    UP(local_anchor_a, 2 * (size_t)J);
+    UP(local_anchor_b, 2 * (size_t)J);
+    UP(local_axis_a, 2 * (size_t)J);
+    UP(local_yaxis_a, 2 * (size_t)J);
+    UP(reference_angle, J);
+    UP(pair_a, P);
+    UP(pair_b, P);
+#undef UP
+    const int32_t *d_ident = nullptr;
+    if (!rc) rc = upload(m->allocs, ident.data(), (size_t)F, &d_ident);
+    g.fixture_slot = d_ident, g.row_fixture = d_ident, g.compact = 0;
+    const float *zf = nullptr;
+    if (!rc) rc = upload<float>(m->allocs, nullptr, 4 * (size_t)(F > 0 ? F : 1), &zf);
+    g.static_fat = zf, g.static_friction = zf, g.static_restitution = zf;
+    m->compact = g;
+    if (!rc && d->fixture_slot) {
+        if (!d->static_fat || !d->static_friction || !d->static_restitution) {
+            rc = fail(GOIB2D_EINVAL, "compact model without static fixture tables");
+        } else {
+            std::vector<int32_t> rows;
+            for (int f = 0; f < F; ++f)
+                if (d->fixture_slot[f] >= 0) {
+                    if (d->fixture_slot[f] != (int)rows.size()) {
+                        rc = fail(GOIB2D_EINVAL, "fixture_slot must number the non-static fixtures in order");
+                        break;
+                    }
+                    rows.push_back(f);
+                }
+            gb::DevModel &c = m->compact;
+            const int32_t *slot = nullptr, *rowf = nullptr;
+            const float *sf = nullptr, *sfr = nullptr, *srs = nullptr;
+            if (!rc) rc = upload(m->allocs, d->fixture_slot, (size_t)F, &slot);
+            if (!rc) rc = upload(m->allocs, rows.data(), rows.size(), &rowf);
+            if (!rc) rc = upload(m->allocs, d->static_fat, 4 * (size_t)F, &sf);
+            if (!rc) rc = upload(m->allocs, d->static_friction, (size_t)F, &sfr);
+            if (!rc) rc = upload(m->allocs, d->static_restitution, (size_t)F, &srs);
+            c.fixture_slot = slot, c.row_fixture = rowf, c.static_fat = sf, c.static_friction = sfr;
+            c.static_restitution = srs, c.compact = 1;
+            m->has_compact = 1, m->n_rows_compact = (int)rows.size();
+        }
+    }
+    if (rc) {
+        goib2d_model_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return 0;
+}
+
+int goib2d_model_destroy(goib2d_model *m) {
+    if (!m) return 0;
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->scratch) cudaFree(m->scratch);
+    if (m->status) cudaFree(m->status);
+    if (m->action_joint) cudaFree(m->action_joint);
+    if (m->action_scale) cudaFree(m->action_scale);
+    delete m;
+    return 0;
+}
+
+int goib2d_model_set_action_map(goib2d_model *m, int32_t n, const int32_t *joint, const float *scale) {
+    if (!m) return fail(GOIB2D_EINVAL, "null model");
+    if (n < 0 || n > 32) return fail(GOIB2D_EINVAL, "action channels %d outside 0..32", n);
+    std::lock_guard<std::mutex> lk(m->mu);
+    for (int k = 0; k < n; ++k)
+        if (!joint || !scale || joint[k] < 0 || joint[k] >= m->full.J)
+            return fail(GOIB2D_EINVAL, "action channel %d joint", k);
+    if (m->action_joint) cudaFree(m->action_joint), m->action_joint = nullptr;
+    if (m->action_scale) cudaFree(m->action_scale), m->action_scale = nullptr;
+    m->n_action = 0;
+    if (n == 0) return 0;
+    CUDA_TRY(cudaMalloc(&m->action_joint, sizeof(int32_t) * n));
+    CUDA_TRY(cudaMalloc(&m->action_scale, sizeof(float) * n));
+    CUDA_TRY(cudaMemcpy(m->action_joint, joint, sizeof(int32_t) * n, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(m->action_scale, scale, sizeof(float) * n, cudaMemcpyHostToDevice));
+    m->n_action = n;
+    return 0;
+}
+
+int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, int32_t rows, int64_t n_worlds,
+                int32_t n_steps, void *const *leaves, const float *actions, void *stream) {
+    if (!m || !s || !leaves) return fail(GOIB2D_EINVAL, "null argument");
+    if (C < 0 || n_worlds < 0 || n_steps < 0) return fail(GOIB2D_EINVAL, "negative size");
+    if (s->velocity_iterations < 0 || s->position_iterations < 0) return fail(GOIB2D_EINVAL, "negative iterations");
+    std::lock_guard<std::mutex> lk(m->mu);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != m->device) return fail(GOIB2D_EINVAL, "model lives on device %d, current device is %d", m->device, dev);
+    const gb::DevModel *dm = nullptr;
+    if (rows == m->full.F)
+        dm = &m->full;
+    else if (m->has_compact && rows == m->n_rows_compact)
+        dm = &m->compact;
+    else
+        return fail(GOIB2D_EINVAL, "fixture rows %d match neither the full (%d) nor the compact (%d) layout", rows,
+                    m->full.F, m->has_compact ? m->n_rows_compact : -1);
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i)
+        if (!leaves[i] && goib2d_leaf_elems(i, dm->B, rows, dm->J, C) > 0 && n_worlds > 0)
+            return fail(GOIB2D_EINVAL, "leaf %d is null", i);
+    if (n_worlds == 0 || n_steps == 0) return 0;
+    gb::StepParams p{};
+    p.m = *dm;
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
+    p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
+    p.lay = scratch_layout(dm->B, C, dm->J, dm->P);
+    size_t need = (size_t)p.lay.stride * (size_t)n_worlds;
+    if (need > m->scratch_bytes) {
+        if (m->scratch) cudaFree(m->scratch), m->scratch = nullptr, m->scratch_bytes = 0;
+        CUDA_TRY(cudaMalloc(&m->scratch, need));
+        m->scratch_bytes = need;
+    }
+    if (n_worlds > m->status_cap) {
+        if (m->status) cudaFree(m->status), m->status = nullptr, m->status_cap = 0;
+        CUDA_TRY(cudaMalloc(&m->status, sizeof(int32_t) * n_worlds));
+        m->status_cap = n_worlds;
+    }
+    m->status_n = n_worlds;
+    p.scratch = m->scratch, p.status = m->status;
+    if (actions && m->n_action > 0) {
+        p.actions = actions, p.n_action = m->n_action, p.action_joint = m->action_joint;
+        p.action_scale = m->action_scale;
+    }
+    const int wpb = 4;  // worlds (warps) per block
+    int64_t blocks = (n_worlds + wpb - 1) / wpb;
+    if (blocks > 0x7fffffff) return fail(GOIB2D_ELIMIT, "too many worlds");
+    goib2d_step_kernel<<<(unsigned)blocks, 32 * wpb, 0, (cudaStream_t)stream>>>(p);
+    CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
+int goib2d_status(goib2d_model *m, const int32_t **device_status, int64_t *n) {
+    if (!m || !device_status || !n) return fail(GOIB2D_EINVAL, "null argument");
+    *device_status = m->status, *n = m->status_n;
+    return 0;
+}
+
+int goib2d_status_copy(goib2d_model *m, int32_t *host, int64_t n) {
+    if (!m || (!host && n)) return fail(GOIB2D_EINVAL, "null argument");
+    if (n < 0 || n > m->status_n) return fail(GOIB2D_EINVAL, "status count %lld outside 0..%lld", (long long)n,
+                                              (long long)m->status_n);
+    if (n) CUDA_TRY(cudaMemcpy(host, m->status, sizeof(int32_t) * n, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,134 @@
+// goib2d device-side data: the Model in HBM, the State leaves of one world, and the per-world scratch arena.
+#pragma once
+#include <cstdint>
+
+#include "../../include/goib2d.h"
+#include "b2dev.cuh"
+
+namespace gb {
+
+// The Model on the device (uploaded once by goib2d_model_create).
+struct DevModel {
+    int B, F, J, P;
+    int compact;  // fixture_slot given (compact fixture layout)
+    const int32_t *fixture_body, *shape_type, *count;
+    const float *radius, *verts, *normals;
+    const int32_t *joint_type, *joint_a, *joint_b;
+    const float *local_anchor_a, *local_anchor_b, *local_axis_a, *local_yaxis_a, *reference_angle;
+    const int32_t *pair_a, *pair_b;
+    const int32_t *fixture_slot;  // [F] row of each fixture (identity for the full layout), -1 static
+    const float *static_fat, *static_friction, *static_restitution;
+    const int32_t *row_fixture;   // [F] fixture of each State.fixtures row (valid for rows < n_rows)
+    int any_toi_body;             // some body is bullet or continuous at build
+};
+
+struct Leaves {
+    void *p[GOIB2D_NUM_LEAVES];
+};
+
+// Velocity + position constraint of one ordered contact (contact_solver.py:103-146).
+struct alignas(16) VCRow {
+    int slot, ia, ib, count, pc_count, mtype, pad0, pad1;
+    float mA, mB, iA, iB;
+    V2 n;
+    float friction, tangent_speed;
+    V2 rA[2], rB[2];
+    float nmass[2], tmass[2], bias[2], ni[2], ti[2];
+    float K[4], NM[4];
+    V2 ln, lp, pl[2], lcA, lcB;
+    float radA, radB;
+};
+
+// One ordered joint (joints.py:163-173).
+struct alignas(16) JRow {
+    int jid, type, ia, ib, limit_state, enable_motor, enable_limit, soft;
+    float mA, mB, iA, iB;
+    V2 rA, rB;
+    V3 Kx, Ky, Kz;
+    float motor_mass, motor_speed, max_impulse;
+    V2 ax, pe;
+    float a1, a2, s1, s2;
+    float gamma, bias, angle, inv_dt;
+    V2 la, lb;
+    float ref, lower, upper;
+    V2 lx, ly;
+    float imp[5];
+    float mimp;
+};
+
+// A narrow-phase result (collide.py:5-7).
+struct Man {
+    int mtype, count;
+    V2 ln, lp, pt[2];
+    int id[2];
+};
+
+// Byte offsets of the per-world scratch arrays (computed on the host by scratch_layout()).
+struct Layout {
+    // [B]
+    int64_t vx, vy, vw, cx, cy, ca, qc, qs;
+    int64_t aw, bisl, stack, bflag, last, moved, done, minsep, jok, islsleep, minst, st;
+    int64_t adv;  // [B][8] TOI: advanced c0x, c0y, a0, alpha0, xf (px, py, c, s)
+    // [C]
+    int64_t order, lpos, corder, cisl, cflag, freeslot, active, over, edges, tneed;
+    int64_t man;  // [C] Man
+    int64_t vc;   // [C] VCRow
+    int64_t rec;  // [C][8] TOI sweep records
+    int64_t tisl; // [C] TOI island contacts
+    int64_t solved;  // [C]
+    // [J]
+    int64_t jr, jorder, jisl, jflag;
+    // [ceil(P/32)]
+    int64_t bitmap;
+    int64_t stride;  // bytes per world (multiple of 256)
+};
+
+struct StepParams {
+    DevModel m;
+    Leaves L;
+    goib2d_settings s;
+    float dt;
+    int C, rows;
+    int64_t n_worlds;
+    int n_steps;
+    const float *actions;
+    int n_action;
+    const int32_t *action_joint;
+    const float *action_scale;
+    char *scratch;
+    Layout lay;
+    int32_t *status;
+};
+
+// Status bits (include/goib2d.h goib2d_status)
+enum { ST_OVERFLOW = 1, ST_NONFINITE = 2, ST_CAP = 4, ST_LIMIT = 8 };
+
+// Typed pointers into the State leaves of one world (the row of every leaf for world `wi`).
+struct W {
+    int B, rows, J, C;
+    int32_t *type;
+    uint8_t *active, *awake, *allow_sleep, *bullet, *continuous;
+    float *sleep_time, *xf_p, *xf_q, *local_center, *c0, *c, *a0, *a, *v, *w, *force, *torque, *mass, *inv_mass,
+        *inertia, *inv_inertia, *linear_damping, *angular_damping, *gravity_scale;
+    float *fx_friction, *fx_restitution, *fx_fat;
+    uint8_t *enable_motor, *enable_limit;
+    float *motor_speed, *max_motor, *lower, *upper, *frequency, *damping, *impulse, *motor_impulse, *lower_impulse,
+        *upper_impulse;
+    int32_t *limit_state;
+    int32_t *pair, *fa, *fb, *key, *mtype, *count, *point_id;
+    uint8_t *touching;
+    float *local_normal, *local_point, *point_local, *normal_impulse, *tangent_impulse, *friction, *restitution,
+        *tangent_speed;
+    float *gravity, *inv_dt0;
+    int32_t *next_key, *overflow;
+    uint8_t *new_fixture;
+    float *t_alpha0, *t_toi, *t_ni, *t_ti;
+    int32_t *t_count, *t_events;
+    uint8_t *t_flag, *t_enabled, *t_solved;
+
+    __device__ V2 bc(int b) const { return {c[2 * b], c[2 * b + 1]}; }
+    __device__ V2 blc(int b) const { return {local_center[2 * b], local_center[2 * b + 1]}; }
+    __device__ Xf bxf(int b) const { return {{xf_p[2 * b], xf_p[2 * b + 1]}, {xf_q[2 * b], xf_q[2 * b + 1]}}; }
+};
+
+}  // namespace gb

@@ -1,0 +1,791 @@
+// goib2d: the batched b2World::Step kernel for sm_100a. One warp per world; K steps per launch.
+//
+// Mapping. Each world's State is a row of every leaf (contiguous per world), so a warp reads and writes its own
+// world with unit-stride lane accesses. Data-parallel phases run one element per lane: the candidate-pair scan
+// (ballot-compacted in candidate order), the narrow phase over contact slots, constraint set-up, integration, fixture
+// synchronisation and b2TimeOfImpact over the TOI candidates. The phases whose order defines the floats - Collide's
+// wake walk, the island DFS, the Gauss-Seidel velocity / position sweeps and the TOI island walk - run on lane 0 in
+// exactly the reference's order (goi_jax/box2d/step.py, island.py, pairs.py, toi.py), so results are bit-identical
+// to it. Per-world working arrays live in a scratch arena (L1/L2-resident), laid out by scratch_layout().
+#include <cstdio>
+
+#include "solver.cuh"
+#include "toi.cuh"
+
+namespace gb {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+template <class T>
+__device__ __forceinline__ T *sp(char *base, int64_t off) {
+    return reinterpret_cast<T *>(base + off);
+}
+
+struct Ctx {
+    const StepParams &p;
+    const DevModel &m;
+    const goib2d_settings &s;
+    W w;
+    char *scr;
+    int lane;
+    int status;
+};
+
+__device__ __forceinline__ void wake_body(W &w, int b) {  // b2Body::SetAwake(true)
+    if (!w.awake[b]) {
+        w.awake[b] = 1;
+        w.sleep_time[b] = 0.0f;
+    }
+}
+
+// ---------------------------------------------------------------- FindNewContacts (pairs.py:134-178)
+__device__ void find_new_contacts(Ctx &x) {
+    const DevModel &m = x.m;
+    W &w = x.w;
+    const int P = m.P, C = w.C, lane = x.lane;
+    if (P == 0) return;
+    uint32_t *bitmap = sp<uint32_t>(x.scr, x.p.lay.bitmap);
+    int *freeslot = sp<int>(x.scr, x.p.lay.freeslot);
+    const int nw = (P + 31) >> 5;
+    for (int i = lane; i < nw; i += 32) bitmap[i] = 0u;
+    __syncwarp();
+    for (int s = lane; s < C; s += 32) {
+        int pr = w.pair[s];
+        if (pr >= 0 && pr < P) atomicOr(&bitmap[pr >> 5], 1u << (pr & 31));
+    }
+    int n_free = 0;
+    for (int base = 0; base < C; base += 32) {
+        int s = base + lane;
+        bool f = s < C && w.pair[s] < 0;
+        unsigned mk = __ballot_sync(FULL, f);
+        if (f) freeslot[n_free + __popc(mk & ((1u << lane) - 1))] = s;
+        n_free += __popc(mk);
+    }
+    const int key0 = *w.next_key;
+    __syncwarp();
+    int n_new = 0;
+    for (int base = 0; base < P; base += 32) {
+        int p = base + lane;
+        bool nw_ = false;
+        int fa = 0, fb = 0, ba = 0, bb = 0;
+        if (p < P) {
+            fa = m.pair_a[p], fb = m.pair_b[p];
+            ba = m.fixture_body[fa], bb = m.fixture_body[fb];
+            if (overlap(fixture_fat(m, w, fa), fixture_fat(m, w, fb))) {
+                bool can = (w.type[ba] == DYNAMIC || w.type[bb] == DYNAMIC) && w.active[ba] && w.active[bb];
+                nw_ = can && !((bitmap[p >> 5] >> (p & 31)) & 1u);
+            }
+        }
+        unsigned mk = __ballot_sync(FULL, nw_);
+        if (nw_) {
+            int rank = n_new + __popc(mk & ((1u << lane) - 1));
+            if (rank < n_free) {
+                int s = freeslot[rank];
+                w.pair[s] = p, w.fa[s] = fa, w.fb[s] = fb, w.key[s] = key0 + rank;
+                w.touching[s] = 0, w.count[s] = 0;
+                w.normal_impulse[2 * s] = w.normal_impulse[2 * s + 1] = 0.0f;
+                w.tangent_impulse[2 * s] = w.tangent_impulse[2 * s + 1] = 0.0f;
+                w.point_id[2 * s] = w.point_id[2 * s + 1] = 0;
+                w.friction[s] = sqrtf(fixture_friction(m, w, fa) * fixture_friction(m, w, fb));
+                float ra = fixture_restitution(m, w, fa), rb = fixture_restitution(m, w, fb);
+                w.restitution[s] = ra > rb ? ra : rb;
+                w.tangent_speed[s] = 0.0f;
+                wake_body(w, ba);
+                wake_body(w, bb);
+            }
+        }
+        n_new += __popc(mk);
+    }
+    __syncwarp();
+    if (lane == 0) {
+        *w.next_key = key0 + n_new;
+        int placed = n_new < n_free ? n_new : n_free;
+        *w.overflow += n_new - placed;
+        if (n_new > placed) x.status |= ST_OVERFLOW;
+    }
+    __syncwarp();
+}
+
+// Live slots in contact-list order (descending key): order[0..n) and each slot's position lpos[slot] (C if dead)
+__device__ int list_order(Ctx &x, int *order, int *lpos) {
+    W &w = x.w;
+    const int C = w.C, lane = x.lane;
+    int n_live = 0;
+    for (int base = 0; base < C; base += 32) {
+        int s = base + lane;
+        bool live = s < C && w.pair[s] >= 0;
+        if (s < C) {
+            int pos = C;
+            if (live) {
+                int k = w.key[s], cnt = 0;
+                for (int t = 0; t < C; ++t)  // ties (never in a valid State) by slot, as a stable sort
+                    cnt += (w.pair[t] >= 0 && (w.key[t] > k || (w.key[t] == k && t < s)));
+                pos = cnt;
+                order[cnt] = s;
+            }
+            lpos[s] = pos;
+        }
+        n_live += __popc(__ballot_sync(FULL, live));
+    }
+    __syncwarp();
+    return n_live;
+}
+
+// ---------------------------------------------------------------- b2ContactManager::Collide (pairs.py:38-117)
+__device__ void collide(Ctx &x) {
+    const DevModel &m = x.m;
+    W &w = x.w;
+    const int C = w.C, B = w.B, lane = x.lane;
+    const Layout &L = x.p.lay;
+    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *active = sp<int>(x.scr, L.active);
+    int *over = sp<int>(x.scr, L.over), *aw = sp<int>(x.scr, L.aw);
+    Man *man = sp<Man>(x.scr, L.man);
+    int n_live = list_order(x, order, lpos);
+    for (int s = lane; s < C; s += 32) {
+        active[s] = 0;
+        if (w.pair[s] < 0) continue;
+        int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
+        over[s] = overlap(fixture_fat(m, w, w.fa[s]), fixture_fat(m, w, w.fb[s]));
+        evaluate(m, w.fa[s], w.fb[s], w.bxf(ba), w.bxf(bb), x.s.linear_slop, man[s]);
+    }
+    for (int b = lane; b < B; b += 32) aw[b] = w.awake[b];
+    __syncwarp();
+    if (lane == 0) {  // the walk newest first: visits and the wakes they cause
+        for (int k = 0; k < n_live; ++k) {
+            int s = order[k];
+            int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
+            bool visit = (aw[ba] && w.type[ba] != STATIC) || (aw[bb] && w.type[bb] != STATIC);
+            active[s] = visit;
+            bool wakes = over[s] ? ((man[s].count > 0) != (bool)w.touching[s]) : (w.count[s] > 0);
+            if (visit && wakes) aw[ba] = aw[bb] = 1;
+        }
+    }
+    __syncwarp();
+    for (int s = lane; s < C; s += 32) {
+        if (!active[s]) continue;
+        if (!over[s]) {
+            w.pair[s] = -1, w.touching[s] = 0, w.count[s] = 0;
+        } else {
+            apply_manifold(w, s, man[s]);
+        }
+    }
+    for (int b = lane; b < B; b += 32) {
+        if (aw[b] && !w.awake[b]) w.sleep_time[b] = 0.0f;
+        w.awake[b] = aw[b];
+    }
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------- islands (island.py:41-140), lane 0
+struct IslandOut {
+    int n_contacts, n_joints, n_islands;
+};
+
+__device__ IslandOut find_islands(Ctx &x) {
+    const DevModel &m = x.m;
+    W &w = x.w;
+    const int C = w.C, B = w.B, J = w.J, lane = x.lane;
+    const Layout &L = x.p.lay;
+    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *edges = sp<int>(x.scr, L.edges);
+    int *corder = sp<int>(x.scr, L.corder), *cisl = sp<int>(x.scr, L.cisl), *cflag = sp<int>(x.scr, L.cflag);
+    int *jorder = sp<int>(x.scr, L.jorder), *jisl = sp<int>(x.scr, L.jisl), *jflag = sp<int>(x.scr, L.jflag);
+    int *bisl = sp<int>(x.scr, L.bisl), *bflag = sp<int>(x.scr, L.bflag), *stack = sp<int>(x.scr, L.stack);
+    int n_live = list_order(x, order, lpos);
+    for (int s = lane; s < C; s += 32) cisl[s] = -1, cflag[s] = 0;
+    for (int j = lane; j < J; j += 32) jisl[j] = -1, jflag[j] = 0;
+    for (int b = lane; b < B; b += 32) bisl[b] = -1, bflag[b] = 0;
+    __syncwarp();
+    IslandOut out{0, 0, 0};
+    if (lane == 0) {
+        int n_edges = 0;
+        for (int k = 0; k < n_live; ++k)
+            if (w.touching[order[k]]) edges[n_edges++] = order[k];
+        int sp_ = 0, nc = 0, nj = 0, ni = 0;
+        for (;;) {
+            if (sp_ == 0) {
+                int seed = -1;
+                for (int b = B - 1; b >= 0; --b)
+                    if (w.active[b] && w.type[b] != STATIC && w.awake[b] && !bflag[b]) {
+                        seed = b;
+                        break;
+                    }
+                if (seed < 0) break;
+                ++ni;
+                stack[sp_++] = seed;
+                bflag[seed] = 1;
+                continue;
+            }
+            int b = stack[--sp_];
+            int id = ni - 1;
+            for (int e = 0; e < n_edges; ++e) {
+                int s = edges[e];
+                int ca = m.fixture_body[w.fa[s]], cb = m.fixture_body[w.fb[s]];
+                if ((ca != b && cb != b) || cflag[s]) continue;
+                corder[nc++] = s;
+                cisl[s] = id;
+                cflag[s] = 1;
+                int other = ca == b ? cb : ca;
+                if (!bflag[other] && w.type[other] != STATIC) stack[sp_++] = other, bflag[other] = 1;
+            }
+            for (int j = J - 1; j >= 0; --j) {
+                int ja = m.joint_a[j], jb = m.joint_b[j];
+                if ((ja != b && jb != b) || jflag[j]) continue;
+                int other = ja == b ? jb : ja;
+                if (!w.active[other]) continue;
+                jorder[nj++] = j;
+                jisl[j] = id;
+                jflag[j] = 1;
+                if (!bflag[other] && w.type[other] != STATIC) stack[sp_++] = other, bflag[other] = 1;
+            }
+            bisl[b] = id;
+            wake_body(w, b);
+        }
+        out = {nc, nj, ni};
+    }
+    out.n_contacts = __shfl_sync(FULL, out.n_contacts, 0);
+    out.n_joints = __shfl_sync(FULL, out.n_joints, 0);
+    out.n_islands = __shfl_sync(FULL, out.n_islands, 0);
+    __syncwarp();
+    return out;
+}
+
+// ---------------------------------------------------------------- SynchronizeFixtures (pairs.py:181-207)
+__device__ void synchronize_fixtures(Ctx &x, const int *moved, int n_rows) {
+    const DevModel &m = x.m;
+    W &w = x.w;
+    for (int r = x.lane; r < n_rows; r += 32) {
+        int f = m.row_fixture[r];
+        int b = m.fixture_body[f];
+        if (!moved[b]) continue;
+        Rot q1 = rot_of(w.a0[b]);
+        V2 rr = rot(q1, w.blc(b));
+        V2 p1{w.c0[2 * b] - rr.x, w.c0[2 * b + 1] - rr.y};
+        AABB a1 = fixture_aabb(m, f, Xf{p1, q1});
+        AABB a2 = fixture_aabb(m, f, w.bxf(b));
+        float lx = bmin(a1.lx, a2.lx), ly = bmin(a1.ly, a2.ly), ux = bmax(a1.ux, a2.ux), uy = bmax(a1.uy, a2.uy);
+        float dx = w.xf_p[2 * b] - p1.x, dy = w.xf_p[2 * b + 1] - p1.y;
+        float *old = w.fx_fat + 4 * r;
+        bool contains = old[0] <= lx && old[1] <= ly && ux <= old[2] && uy <= old[3];
+        if (contains) continue;
+        lx = lx - AABB_EXT, ly = ly - AABB_EXT, ux = ux + AABB_EXT, uy = uy + AABB_EXT;
+        float ddx = AABB_MUL * dx, ddy = AABB_MUL * dy;
+        if (ddx < 0)
+            lx = lx + ddx;
+        else
+            ux = ux + ddx;
+        if (ddy < 0)
+            ly = ly + ddy;
+        else
+            uy = uy + ddy;
+        old[0] = lx, old[1] = ly, old[2] = ux, old[3] = uy;
+    }
+    __syncwarp();
+}
+
+__device__ __forceinline__ Bodies bodies_of(Ctx &x) {
+    const Layout &L = x.p.lay;
+    return {sp<float>(x.scr, L.vx), sp<float>(x.scr, L.vy), sp<float>(x.scr, L.vw), sp<float>(x.scr, L.cx),
+            sp<float>(x.scr, L.cy), sp<float>(x.scr, L.ca), sp<float>(x.scr, L.qc), sp<float>(x.scr, L.qs)};
+}
+
+// ---------------------------------------------------------------- b2World::Solve (step.py:73-194)
+__device__ void solve(Ctx &x, float dt, float dt_ratio) {
+    const DevModel &m = x.m;
+    const goib2d_settings &s = x.s;
+    W &w = x.w;
+    const int B = w.B, C = w.C, J = w.J, lane = x.lane;
+    const Layout &L = x.p.lay;
+    IslandOut isl = find_islands(x);
+    int *bisl = sp<int>(x.scr, L.bisl), *corder = sp<int>(x.scr, L.corder), *cisl = sp<int>(x.scr, L.cisl);
+    int *jorder = sp<int>(x.scr, L.jorder), *jisl = sp<int>(x.scr, L.jisl);
+    int *done = sp<int>(x.scr, L.done), *jok = sp<int>(x.scr, L.jok), *moved = sp<int>(x.scr, L.moved);
+    float *minsep = sp<float>(x.scr, L.minsep);
+    VCRow *vc = sp<VCRow>(x.scr, L.vc);
+    JRow *jr = sp<JRow>(x.scr, L.jr);
+    Bodies bd = bodies_of(x);
+    const float h = dt;
+    const float gx = w.gravity[0], gy = w.gravity[1];
+    for (int b = lane; b < B; b += 32) {  // integrate velocities (step.py:83-100)
+        bool in_isl = bisl[b] >= 0;
+        float gs = w.gravity_scale[b];
+        float ax = gs * gx + w.inv_mass[b] * w.force[2 * b];
+        float ay = gs * gy + w.inv_mass[b] * w.force[2 * b + 1];
+        float vx = w.v[2 * b] + h * ax, vy = w.v[2 * b + 1] + h * ay;
+        float ww = w.w[b] + (h * w.inv_inertia[b]) * w.torque[b];
+        float ld = 1.0f / (1.0f + h * w.linear_damping[b]);
+        float ad = 1.0f / (1.0f + h * w.angular_damping[b]);
+        vx = vx * ld, vy = vy * ld, ww = ww * ad;
+        bool dyn = in_isl && w.type[b] == DYNAMIC;
+        bd.vx[b] = dyn ? vx : w.v[2 * b];
+        bd.vy[b] = dyn ? vy : w.v[2 * b + 1];
+        bd.vw[b] = dyn ? ww : w.w[b];
+        bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
+        if (in_isl) w.c0[2 * b] = w.c[2 * b], w.c0[2 * b + 1] = w.c[2 * b + 1], w.a0[b] = w.a[b];
+        Rot q = rot_of(bd.ca[b]);
+        bd.qc[b] = q.c, bd.qs[b] = q.s;
+    }
+    __syncwarp();
+    const bool warm = s.warm_starting;
+    for (int k = lane; k < isl.n_contacts; k += 32)
+        prepare_contact(m, w, corder[k], bd, warm, dt_ratio, s.velocity_threshold, vc[k]);
+    for (int k = lane; k < isl.n_joints; k += 32) prepare_joint(m, w, jorder[k], bd, s, dt, dt_ratio, warm, jr[k]);
+    __syncwarp();
+    const bool v24 = s.revolute_v24;
+    if (lane == 0) {
+        if (warm)
+            for (int k = 0; k < isl.n_contacts; ++k) contact_warm_start(vc[k], bd);
+        for (int k = 0; k < isl.n_joints; ++k) joint_warm_start(jr[k], bd, v24);
+        for (int it = 0; it < s.velocity_iterations; ++it) {
+            for (int k = 0; k < isl.n_joints; ++k) joint_solve_velocity(jr[k], bd, v24);
+            for (int k = 0; k < isl.n_contacts; ++k) contact_solve_velocity(vc[k], bd);
+        }
+    }
+    __syncwarp();
+    for (int k = lane; k < isl.n_contacts; k += 32) {  // StoreImpulses (contact_solver.py:293-304)
+        const VCRow &c = vc[k];
+        for (int j = 0; j < c.count; ++j)
+            w.normal_impulse[2 * c.slot + j] = c.ni[j], w.tangent_impulse[2 * c.slot + j] = c.ti[j];
+    }
+    for (int k = lane; k < isl.n_joints; k += 32) {  // joints.py:609-622
+        const JRow &r = jr[k];
+        if (v24) w.lower_impulse[r.jid] = r.imp[3], w.upper_impulse[r.jid] = r.imp[4];
+        for (int i = 0; i < 3; ++i) w.impulse[3 * r.jid + i] = r.imp[i];
+        w.motor_impulse[r.jid] = r.mimp;
+        w.limit_state[r.jid] = r.limit_state;
+    }
+    const float max_t = s.clamps_per_second ? s.max_translation * h : s.max_translation;
+    const float max_r = s.clamps_per_second ? s.max_rotation * h : s.max_rotation;
+    for (int b = lane; b < B; b += 32) {  // integrate positions (step.py:120-135)
+        if (bisl[b] < 0) continue;
+        float vx = bd.vx[b], vy = bd.vy[b], ww = bd.vw[b];
+        float tx = h * vx, ty = h * vy;
+        if (tx * tx + ty * ty > max_t * max_t) {
+            float ratio = max_t / length(V2{tx, ty});
+            vx = vx * ratio, vy = vy * ratio;
+        }
+        float rt = h * ww;
+        if (rt * rt > max_r * max_r) ww = ww * (max_r / babs(rt));
+        bd.cx[b] = bd.cx[b] + h * vx, bd.cy[b] = bd.cy[b] + h * vy, bd.ca[b] = bd.ca[b] + h * ww;
+        bd.vx[b] = vx, bd.vy[b] = vy, bd.vw[b] = ww;
+    }
+    for (int i = lane; i < B; i += 32) done[i] = i >= isl.n_islands;
+    __syncwarp();
+    if (lane == 0) {  // position iterations with per-island early exit (step.py:197-251)
+        for (int it = 0; it < s.position_iterations; ++it) {
+            bool all = true;
+            for (int i = 0; i < isl.n_islands; ++i) all = all && done[i];
+            if (all) break;
+            for (int i = 0; i < isl.n_islands; ++i) minsep[i] = 0.0f, jok[i] = 1;
+            for (int k = 0; k < isl.n_contacts; ++k) {
+                const VCRow &c = vc[k];
+                int i = cisl[c.slot];
+                if (done[i]) continue;
+                float ms = contact_solve_position(c, bd, s.baumgarte, s.linear_slop, s.max_linear_correction, c.mA,
+                                                  c.mB, c.iA, c.iB);
+                minsep[i] = bmin(minsep[i], ms);
+            }
+            for (int k = 0; k < isl.n_joints; ++k) {
+                const JRow &r = jr[k];
+                int i = jisl[r.jid];
+                if (done[i]) continue;
+                bool ok = joint_solve_position(r, bd, s);
+                jok[i] = jok[i] && ok;
+            }
+            for (int i = 0; i < isl.n_islands; ++i)
+                if (minsep[i] >= -3.0f * s.linear_slop && jok[i]) done[i] = 1;
+        }
+    }
+    __syncwarp();
+    for (int b = lane; b < B; b += 32) {  // write back + SynchronizeTransform (step.py:141-151)
+        if (bisl[b] < 0) continue;
+        w.c[2 * b] = bd.cx[b], w.c[2 * b + 1] = bd.cy[b], w.a[b] = bd.ca[b];
+        w.v[2 * b] = bd.vx[b], w.v[2 * b + 1] = bd.vy[b], w.w[b] = bd.vw[b];
+        Xf xf = xf_from(V2{bd.cx[b], bd.cy[b]}, bd.ca[b], w.blc(b));
+        w.xf_p[2 * b] = xf.p.x, w.xf_p[2 * b + 1] = xf.p.y, w.xf_q[2 * b] = xf.q.c, w.xf_q[2 * b + 1] = xf.q.s;
+    }
+    __syncwarp();
+    int *islsleep = sp<int>(x.scr, L.islsleep), *last = sp<int>(x.scr, L.last);
+    float *minst = sp<float>(x.scr, L.minst), *st = sp<float>(x.scr, L.st);
+    if (lane == 0) {  // sleep per island (step.py:153-171), static bodies' awake flag (step.py:173-194)
+        for (int i = 0; i < B; ++i) islsleep[i] = 0;
+        if (s.allow_sleep) {
+            float lin_tol = s.linear_sleep_tolerance * s.linear_sleep_tolerance;
+            float ang_tol = s.angular_sleep_tolerance * s.angular_sleep_tolerance;
+            for (int i = 0; i < B; ++i) minst[i] = MAXF;
+            for (int b = 0; b < B; ++b) {
+                bool nonstatic = bisl[b] >= 0 && w.type[b] != STATIC;
+                bool mov = !w.allow_sleep[b] || (w.w[b] * w.w[b] > ang_tol) ||
+                           (w.v[2 * b] * w.v[2 * b] + w.v[2 * b + 1] * w.v[2 * b + 1] > lin_tol);
+                float t = mov ? 0.0f : w.sleep_time[b] + h;
+                st[b] = nonstatic ? t : w.sleep_time[b];
+                if (nonstatic) minst[bisl[b]] = fminf(minst[bisl[b]], mov ? 0.0f : st[b]);
+            }
+            for (int i = 0; i < B; ++i) islsleep[i] = minst[i] >= s.time_to_sleep && done[i];
+            for (int b = 0; b < B; ++b) {
+                bool nonstatic = bisl[b] >= 0 && w.type[b] != STATIC;
+                bool sl = nonstatic && islsleep[bisl[b]];
+                w.sleep_time[b] = sl ? 0.0f : st[b];
+                if (sl) {
+                    w.awake[b] = 0;
+                    w.v[2 * b] = w.v[2 * b + 1] = 0.0f, w.w[b] = 0.0f;
+                    w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
+                }
+            }
+        }
+        for (int b = 0; b < B; ++b) last[b] = -1;
+        for (int sl = 0; sl < C; ++sl) {
+            int i = cisl[sl];
+            if (i < 0) continue;
+            int ba = m.fixture_body[w.fa[sl]], bb = m.fixture_body[w.fb[sl]];
+            last[ba] = max(last[ba], i), last[bb] = max(last[bb], i);
+        }
+        for (int j = 0; j < J; ++j) {
+            int i = jisl[j];
+            if (i < 0) continue;
+            int ja = m.joint_a[j], jb = m.joint_b[j];
+            last[ja] = max(last[ja], i), last[jb] = max(last[jb], i);
+        }
+        for (int b = 0; b < B; ++b)
+            if (w.type[b] == STATIC && last[b] >= 0) w.awake[b] = !islsleep[last[b]], w.sleep_time[b] = 0.0f;
+    }
+    for (int b = lane; b < B; b += 32) moved[b] = bisl[b] >= 0 && w.type[b] != STATIC;
+    __syncwarp();
+    synchronize_fixtures(x, moved, w.rows);
+    find_new_contacts(x);
+}
+
+// ---------------------------------------------------------------- b2World::SolveTOI (toi.py:462-865)
+// one pass of the min-TOI search; returns found, sets *min_slot / *min_alpha (all lanes)
+__device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
+    const DevModel &m = x.m;
+    W &w = x.w;
+    const int C = w.C, lane = x.lane;
+    const Layout &L = x.p.lay;
+    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *tneed = sp<int>(x.scr, L.tneed);
+    float *rec = sp<float>(x.scr, L.rec);
+    int n_live = list_order(x, order, lpos);
+    if (lane == 0) {  // sweep alignment in list order (toi.py:500-536)
+        for (int k = 0; k < n_live; ++k) {
+            int slot = order[k];
+            tneed[slot] = 0;
+            bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
+            if (!base || w.t_flag[slot]) continue;
+            int A = m.fixture_body[w.fa[slot]], Bb = m.fixture_body[w.fb[slot]];
+            bool actA = w.awake[A] && w.type[A] != STATIC, actB = w.awake[Bb] && w.type[Bb] != STATIC;
+            if (!(actA || actB) || !toi_pair_rule(w, A, Bb, x.s.unity_toi)) continue;
+            float alA = w.t_alpha0[A], alB = w.t_alpha0[Bb];
+            float common = alA;
+            if (alA < alB) {
+                sweep_advance(w.c0[2 * A], w.c0[2 * A + 1], w.a0[A], w.t_alpha0[A], w.c[2 * A], w.c[2 * A + 1],
+                              w.a[A], alB);
+                common = alB;
+            } else if (alB < alA) {
+                sweep_advance(w.c0[2 * Bb], w.c0[2 * Bb + 1], w.a0[Bb], w.t_alpha0[Bb], w.c[2 * Bb],
+                              w.c[2 * Bb + 1], w.a[Bb], alA);
+            }
+            float *r = rec + 8 * slot;
+            r[0] = w.c0[2 * A], r[1] = w.c0[2 * A + 1], r[2] = w.a0[A];
+            r[3] = w.c0[2 * Bb], r[4] = w.c0[2 * Bb + 1], r[5] = w.a0[Bb], r[6] = common;
+            tneed[slot] = 1;
+        }
+    }
+    __syncwarp();
+    for (int k = lane; k < n_live; k += 32) {  // b2TimeOfImpact per queued contact
+        int slot = order[k];
+        if (!tneed[slot]) continue;
+        int A = m.fixture_body[w.fa[slot]], Bb = m.fixture_body[w.fb[slot]];
+        const float *r = rec + 8 * slot;
+        Sweep swA{w.blc(A), {r[0], r[1]}, {w.c[2 * A], w.c[2 * A + 1]}, r[2], w.a[A]};
+        Sweep swB{w.blc(Bb), {r[3], r[4]}, {w.c[2 * Bb], w.c[2 * Bb + 1]}, r[5], w.a[Bb]};
+        float beta;
+        int st = time_of_impact(proxy_of(m, w.fa[slot]), swA, proxy_of(m, w.fb[slot]), swB, x.s.linear_slop, &beta);
+        float common = r[6];
+        w.t_toi[slot] = st == E_TOUCHING ? bmin(common + (1.0f - common) * beta, 1.0f) : 1.0f;
+        w.t_flag[slot] = 1;
+    }
+    __syncwarp();
+    int ms = 0;
+    float best = 1.0f;
+    bool found = false;
+    if (lane == 0) {  // the minimum, first (or last) in list order among exact ties (toi.py:550-557)
+        bool any = false;
+        for (int k = 0; k < n_live; ++k) {
+            int slot = order[k];
+            bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
+            if (base && w.t_flag[slot] && w.t_toi[slot] < 1.0f) any = true, best = fminf(best, w.t_toi[slot]);
+        }
+        int msp = x.s.toi_tie_oldest ? -1 : C;
+        for (int k = 0; k < n_live; ++k) {
+            int slot = order[k];
+            bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
+            if (!(base && w.t_flag[slot] && w.t_toi[slot] < 1.0f && w.t_toi[slot] == best)) continue;
+            if (x.s.toi_tie_oldest ? k > msp : k < msp) ms = slot, msp = k;
+        }
+        const float done_alpha = 1.0f - 10.0f * EPS;
+        found = any && !(done_alpha < best);
+    }
+    *min_slot = __shfl_sync(FULL, ms, 0);
+    *min_alpha = __shfl_sync(FULL, best, 0);
+    return __shfl_sync(FULL, (int)found, 0);
+}
+
+// one TOI event (toi.py:604-716) with b2Island::SolveTOI (toi.py:719-799)
+__device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
+    const DevModel &m = x.m;
+    const goib2d_settings &s = x.s;
+    W &w = x.w;
+    const int B = w.B, C = w.C, lane = x.lane;
+    const Layout &L = x.p.lay;
+    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *tisl = sp<int>(x.scr, L.tisl);
+    int *flip_b = sp<int>(x.scr, L.aw), *in_other = sp<int>(x.scr, L.bflag), *touched = sp<int>(x.scr, L.stack);
+    int *newbody = sp<int>(x.scr, L.last), *moved = sp<int>(x.scr, L.moved), *solved = sp<int>(x.scr, L.solved);
+    int *old_pair = sp<int>(x.scr, L.cflag), *old_key = sp<int>(x.scr, L.active);
+    float *adv = sp<float>(x.scr, L.adv);
+    Man *man = sp<Man>(x.scr, L.man);
+    VCRow *vc = sp<VCRow>(x.scr, L.vc);
+    Bodies bd = bodies_of(x);
+    const int A = m.fixture_body[w.fa[min_slot]], Bb = m.fixture_body[w.fb[min_slot]];
+    for (int b = lane; b < B; b += 32) {  // every body advanced to min_alpha, and its transform there
+        float *d = adv + 8 * b;
+        d[0] = w.c0[2 * b], d[1] = w.c0[2 * b + 1], d[2] = w.a0[b], d[3] = w.t_alpha0[b];
+        sweep_advance(d[0], d[1], d[2], d[3], w.c[2 * b], w.c[2 * b + 1], w.a[b], min_alpha);
+        Xf xf = xf_from(V2{d[0], d[1]}, d[2], w.blc(b));
+        d[4] = xf.p.x, d[5] = xf.p.y, d[6] = xf.q.c, d[7] = xf.q.s;
+        flip_b[b] = in_other[b] = touched[b] = newbody[b] = 0;
+    }
+    int n_live = list_order(x, order, lpos);
+    for (int s_ = lane; s_ < C; s_ += 32) {  // manifolds at the advanced poses for the pair's contacts
+        solved[s_] = 0;
+        if (w.pair[s_] < 0) continue;
+        int ba = m.fixture_body[w.fa[s_]], bb = m.fixture_body[w.fb[s_]];
+        if (ba != A && bb != A && ba != Bb && bb != Bb) continue;
+        const float *da = adv + 8 * ba, *db = adv + 8 * bb;
+        evaluate(m, w.fa[s_], w.fb[s_], Xf{{da[4], da[5]}, {da[6], da[7]}}, Xf{{db[4], db[5]}, {db[6], db[7]}},
+                 s.linear_slop, man[s_]);
+    }
+    __syncwarp();
+    int n_isl = 0;
+    bool t_min = false;
+    if (lane == 0) {
+        t_min = man[min_slot].count > 0;
+        if (apply_manifold(w, min_slot, man[min_slot]))
+            flip_b[m.fixture_body[w.fa[min_slot]]] = flip_b[m.fixture_body[w.fb[min_slot]]] = 1;
+        w.t_enabled[min_slot] = t_min;
+        w.t_count[min_slot] += 1;
+        w.t_flag[min_slot] = 0;
+        if (t_min) {  // the island walk: bodyA's contact list then bodyB's, newest first (toi.py:633-657)
+            tisl[n_isl++] = min_slot;
+            int n_bodies = 2;
+            const int owners[2] = {A, Bb};
+            bool stop = false;
+            for (int oi = 0; oi < 2 && !stop; ++oi) {
+                int owner = owners[oi];
+                if (w.type[owner] != DYNAMIC) continue;
+                for (int k = 0; k < n_live; ++k) {
+                    int slot = order[k];
+                    int ca = m.fixture_body[w.fa[slot]], cb = m.fixture_body[w.fb[slot]];
+                    if (ca != owner && cb != owner) continue;
+                    if (oi == 1 && w.type[A] == DYNAMIC && (ca == A || cb == A)) continue;
+                    if (!(n_isl < MAX_TOI_CONTACTS && n_bodies < 2 * MAX_TOI_CONTACTS)) {
+                        stop = true;
+                        break;
+                    }
+                    if (slot == min_slot) continue;
+                    int other = ca == owner ? cb : ca;
+                    if (w.type[other] == DYNAMIC && !w.bullet[owner] && !w.bullet[other]) continue;
+                    if (s.unity_toi && !toi_pair_rule(w, owner, other, true)) continue;
+                    if (apply_manifold(w, slot, man[slot])) flip_b[ca] = flip_b[cb] = 1;
+                    w.t_enabled[slot] = 1;
+                    touched[other] = 1;
+                    if (man[slot].count <= 0) continue;
+                    tisl[n_isl++] = slot;
+                    in_other[other] = 1;
+                    if (other != A && other != Bb && !newbody[other]) newbody[other] = 1, ++n_bodies;
+                }
+            }
+        }
+    }
+    t_min = __shfl_sync(FULL, (int)t_min, 0);
+    n_isl = __shfl_sync(FULL, n_isl, 0);
+    __syncwarp();
+    for (int b = lane; b < B; b += 32) {  // body sweeps after the walk (toi.py:667-681)
+        bool pair_b = b == A || b == Bb;
+        bool keep = (pair_b && t_min) || in_other[b];
+        bool restore = (pair_b && !t_min) || (touched[b] && !in_other[b]);
+        const float *d = adv + 8 * b;
+        if (keep) {
+            w.c0[2 * b] = d[0], w.c0[2 * b + 1] = d[1], w.a0[b] = d[2];
+            w.c[2 * b] = d[0], w.c[2 * b + 1] = d[1], w.a[b] = d[2];
+            w.t_alpha0[b] = d[3];
+            w.xf_p[2 * b] = d[4], w.xf_p[2 * b + 1] = d[5], w.xf_q[2 * b] = d[6], w.xf_q[2 * b + 1] = d[7];
+        } else if (restore) {
+            Xf o = xf_from(w.bc(b), w.a[b], w.blc(b));
+            w.xf_p[2 * b] = o.p.x, w.xf_p[2 * b + 1] = o.p.y, w.xf_q[2 * b] = o.q.c, w.xf_q[2 * b + 1] = o.q.s;
+        }
+        if (flip_b[b] || (pair_b && t_min) || (newbody[b] && w.type[b] != STATIC)) wake_body(w, b);
+        moved[b] = t_min && (pair_b || in_other[b]) && w.type[b] == DYNAMIC;
+    }
+    __syncwarp();
+    if (!t_min) {
+        if (lane == 0) *w.t_events += 1;
+        __syncwarp();
+        return;
+    }
+    // b2Island::SolveTOI: position passes moving only the TOI pair, then velocity passes, then integration
+    for (int b = lane; b < B; b += 32) {
+        bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
+        bd.vx[b] = w.v[2 * b], bd.vy[b] = w.v[2 * b + 1], bd.vw[b] = w.w[b];
+        bd.qc[b] = 1.0f, bd.qs[b] = 0.0f;
+    }
+    __syncwarp();
+    for (int k = lane; k < n_isl; k += 32)  // position rows (the position-independent fields)
+        prepare_contact(m, w, tisl[k], bd, false, 1.0f, s.velocity_threshold, vc[k]);
+    __syncwarp();
+    if (lane == 0) {
+        const float okay_sep = -1.5f * s.linear_slop;
+        for (int it = 0; it < 20; ++it) {
+            float min_sep = 0.0f;
+            for (int k = 0; k < n_isl; ++k) {
+                const VCRow &c = vc[k];
+                bool ta = c.ia == A || c.ia == Bb, tb = c.ib == A || c.ib == Bb;
+                float ms = contact_solve_position(c, bd, s.toi_baumgarte, s.linear_slop, s.max_linear_correction,
+                                                  ta ? c.mA : 0.0f, tb ? c.mB : 0.0f, ta ? c.iA : 0.0f,
+                                                  tb ? c.iB : 0.0f);
+                min_sep = bmin(min_sep, ms);
+            }
+            if (min_sep >= okay_sep) break;
+        }
+        // leap of faith: the TOI bodies' sweep start is the solved pose
+        w.c0[2 * A] = bd.cx[A], w.c0[2 * A + 1] = bd.cy[A], w.a0[A] = bd.ca[A];
+        w.c0[2 * Bb] = bd.cx[Bb], w.c0[2 * Bb + 1] = bd.cy[Bb], w.a0[Bb] = bd.ca[Bb];
+    }
+    __syncwarp();
+    for (int b = lane; b < B; b += 32) {
+        Rot q = rot_of(bd.ca[b]);
+        bd.qc[b] = q.c, bd.qs[b] = q.s;
+    }
+    __syncwarp();
+    for (int k = lane; k < n_isl; k += 32)  // velocity constraints at the solved poses, no warm start
+        prepare_contact(m, w, tisl[k], bd, false, 1.0f, s.velocity_threshold, vc[k]);
+    __syncwarp();
+    if (lane == 0)
+        for (int it = 0; it < s.velocity_iterations; ++it)
+            for (int k = 0; k < n_isl; ++k) contact_solve_velocity(vc[k], bd);
+    __syncwarp();
+    const float h = (1.0f - min_alpha) * dt;
+    const float max_t = s.clamps_per_second ? s.max_translation * dt : s.max_translation;
+    const float max_r = s.clamps_per_second ? s.max_rotation * dt : s.max_rotation;
+    for (int b = lane; b < B; b += 32) {  // integrate the island bodies over the rest of the step
+        bool pair_b = b == A || b == Bb;
+        if (!(pair_b || in_other[b])) continue;
+        float vx = bd.vx[b], vy = bd.vy[b], ww = bd.vw[b];
+        float tx = h * vx, ty = h * vy;
+        if (tx * tx + ty * ty > max_t * max_t) {
+            float ratio = max_t / length(V2{tx, ty});
+            vx = vx * ratio, vy = vy * ratio;
+        }
+        float rt = h * ww;
+        if (rt * rt > max_r * max_r) ww = ww * (max_r / babs(rt));
+        float ncx = bd.cx[b] + h * vx, ncy = bd.cy[b] + h * vy, na = bd.ca[b] + h * ww;
+        Xf xf = xf_from(V2{ncx, ncy}, na, w.blc(b));
+        w.c[2 * b] = ncx, w.c[2 * b + 1] = ncy, w.a[b] = na;
+        w.v[2 * b] = vx, w.v[2 * b + 1] = vy, w.w[b] = ww;
+        w.xf_p[2 * b] = xf.p.x, w.xf_p[2 * b + 1] = xf.p.y, w.xf_q[2 * b] = xf.q.c, w.xf_q[2 * b + 1] = xf.q.s;
+    }
+    for (int k = lane; k < n_isl; k += 32) {  // b2Island::Report
+        const VCRow &c = vc[k];
+        solved[c.slot] = 1;
+        w.t_solved[c.slot] = 1;
+        for (int j = 0; j < 2; ++j) {
+            w.t_ni[2 * c.slot + j] = j < c.count ? c.ni[j] : 0.0f;
+            w.t_ti[2 * c.slot + j] = j < c.count ? c.ti[j] : 0.0f;
+        }
+    }
+    __syncwarp();
+    synchronize_fixtures(x, moved, w.rows);
+    for (int s_ = lane; s_ < C; s_ += 32) {
+        if (moved[m.fixture_body[w.fa[s_]]] || moved[m.fixture_body[w.fb[s_]]]) w.t_flag[s_] = 0;  // every slot
+        old_pair[s_] = w.pair[s_], old_key[s_] = w.key[s_];
+    }
+    __syncwarp();
+    find_new_contacts(x);
+    for (int s_ = lane; s_ < C; s_ += 32) {
+        bool is_new = w.pair[s_] >= 0 && (old_pair[s_] < 0 || old_key[s_] != w.key[s_]);
+        if (is_new) w.t_count[s_] = 0, w.t_flag[s_] = 0, w.t_enabled[s_] = 1;
+    }
+    if (lane == 0) *w.t_events += 1;
+    __syncwarp();
+}
+
+__device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
+    W &w = x.w;
+    const int C = w.C, B = w.B, lane = x.lane;
+    if (C == 0 || x.m.P == 0) return;
+    if (x.s.unity_toi && !x.m.any_toi_body) return;
+    for (int b = lane; b < B; b += 32) w.t_alpha0[b] = 0.0f;
+    for (int c = lane; c < C; c += 32) {
+        w.t_count[c] = 0, w.t_toi[c] = 1.0f, w.t_flag[c] = 0, w.t_enabled[c] = 1, w.t_solved[c] = 0;
+        w.t_ni[2 * c] = w.t_ni[2 * c + 1] = w.t_ti[2 * c] = w.t_ti[2 * c + 1] = 0.0f;
+    }
+    if (lane == 0) *w.t_events = 0;
+    __syncwarp();
+    if (!(dt > 0)) return;
+    const int max_events = C * (MAX_SUB_STEPS + 1) + 8;
+    int min_slot = 0;
+    float min_alpha = 1.0f;
+    bool pending = false;
+    for (int it = 0; it <= max_events; ++it) {
+        if (pending) toi_event(x, dt, min_slot, min_alpha);
+        if (!toi_search(x, &min_slot, &min_alpha)) {
+            pending = false;
+            break;
+        }
+        pending = true;
+    }
+    if (pending) x.status |= ST_CAP;  // events capped with one still pending (the reference's limit too)
+}
+
+// b2World::Step (step.py:28-47)
+__device__ void world_step(Ctx &x, float dt) {
+    W &w = x.w;
+    const goib2d_settings &s = x.s;
+    if (*w.new_fixture) find_new_contacts(x);
+    __syncwarp();
+    if (x.lane == 0) *w.new_fixture = 0;
+    const float inv_dt = dt > 0 ? 1.0f / dt : 0.0f;
+    const float dt_ratio = *w.inv_dt0 * dt;
+    __syncwarp();
+    collide(x);
+    solve(x, dt, dt_ratio);
+    if (s.continuous_physics) solve_toi(x, dt);
+    __syncwarp();
+    if (x.lane == 0 && dt > 0) *w.inv_dt0 = inv_dt;
+    if (s.auto_clear_forces)
+        for (int b = x.lane; b < w.B; b += 32) w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
+    __syncwarp();
+}
+
+}  // namespace gb
+
+using namespace gb;
+
+// One warp per world; blockDim.x = 32 * worlds per block.
+extern "C" __global__ void __launch_bounds__(128) goib2d_step_kernel(const __grid_constant__ StepParams p) {
+    const int warp = threadIdx.x >> 5;
+    const int64_t world = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    if (world >= p.n_worlds) return;
+    Ctx x{p, p.m, p.s, {}, p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0};
+    bind_world(x.w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
+    for (int k = 0; k < p.n_steps; ++k) {
+        if (p.actions && x.lane < p.n_action)  // action channels -> joint motor speeds
+            x.w.motor_speed[p.action_joint[x.lane]] = p.action_scale[x.lane] * p.actions[world * p.n_action + x.lane];
+        __syncwarp();
+        world_step(x, p.dt);
+    }
+    bool bad = false;  // non-finite body state
+    for (int b = x.lane; b < x.w.B; b += 32)
+        bad = bad || !isfinite(x.w.c[2 * b]) || !isfinite(x.w.c[2 * b + 1]) || !isfinite(x.w.a[b]) ||
+              !isfinite(x.w.v[2 * b]) || !isfinite(x.w.v[2 * b + 1]) || !isfinite(x.w.w[b]);
+    if (__any_sync(FULL, bad)) x.status |= ST_NONFINITE;
+    if (x.lane == 0 && p.status) p.status[world] = x.status;
+}

@@ -1,0 +1,325 @@
+// goib2d device code: b2Distance (GJK), b2SeparationFunction and b2TimeOfImpact (toi.py:114-457), one contact per
+// lane. Box2D's nested loops; every loop has its fixed iteration cap (GJK 20, separating axes 20, push-backs 8,
+// root finder 50), so a lane always finishes.
+#pragma once
+#include "narrow.cuh"
+
+namespace gb {
+
+enum { E_UNKNOWN = 0, E_FAILED = 1, E_OVERLAPPED = 2, E_TOUCHING = 3, E_SEPARATED = 4 };
+enum { E_POINTS = 0, E_FACE_A = 1, E_FACE_B = 2 };
+
+struct Sweep {
+    V2 lc, c0, c;
+    float a0, a;
+};
+struct Proxy {
+    const float *v;
+    int count;
+    float radius;
+    __device__ V2 vert(int i) const {
+        i = i < 0 ? 0 : (i > MAXV - 1 ? MAXV - 1 : i);
+        return {v[2 * i], v[2 * i + 1]};
+    }
+    __device__ int support(V2 d) const {  // b2DistanceProxy::GetSupport
+        int best = 0;
+        float bv = 0.0f;
+        for (int i = 0; i < count; ++i) {
+            float val = v[2 * i] * d.x + v[2 * i + 1] * d.y;
+            if (i == 0 || val > bv) best = i, bv = val;
+        }
+        return best;
+    }
+};
+__device__ __forceinline__ Proxy proxy_of(const DevModel &m, int f) {
+    return {m.verts + 16 * f, m.count[f], m.radius[f]};
+}
+
+__device__ __forceinline__ Xf sweep_xf(const Sweep &sw, float t) {  // b2Sweep::GetTransform (toi.py:73-81)
+    float omb = 1.0f - t;
+    float px = omb * sw.c0.x + t * sw.c.x, py = omb * sw.c0.y + t * sw.c.y;
+    Rot q = rot_of(omb * sw.a0 + t * sw.a);
+    V2 r = rot(q, sw.lc);
+    return {{px - r.x, py - r.y}, q};
+}
+
+struct SV {
+    V2 wA, wB, w;
+    float a;
+    int iA, iB;
+};
+struct Cache {
+    int count;
+    int iA[3], iB[3];
+    float metric;
+};
+
+__device__ __forceinline__ SV make_vertex(const Proxy &pA, Xf xfA, int iA, const Proxy &pB, Xf xfB, int iB) {
+    SV v;
+    v.wA = xf_mul(xfA, pA.vert(iA));
+    v.wB = xf_mul(xfB, pB.vert(iB));
+    v.w = sub(v.wB, v.wA);
+    v.a = 0.0f, v.iA = iA, v.iB = iB;
+    return v;
+}
+__device__ __forceinline__ float simplex_metric(const SV *s, int count) {
+    if (count == 2) return length(sub(s[0].w, s[1].w));
+    if (count == 3) return cross(sub(s[1].w, s[0].w), sub(s[2].w, s[0].w));
+    return 0.0f;
+}
+
+__device__ void gjk_solve2(SV *s, int &count) {  // toi.py:160-175
+    V2 w1 = s[0].w, w2 = s[1].w;
+    V2 e12 = sub(w2, w1);
+    float d12_2 = -dot(w1, e12), d12_1 = dot(w2, e12);
+    if (d12_2 <= 0) {
+        s[0].a = 1.0f, count = 1;
+        return;
+    }
+    if (d12_1 <= 0) {
+        s[1].a = 1.0f, s[0] = s[1], count = 1;
+        return;
+    }
+    float inv = 1.0f / (d12_1 + d12_2);
+    s[0].a = d12_1 * inv, s[1].a = d12_2 * inv, count = 2;
+}
+
+__device__ void gjk_solve3(SV *s, int &count) {  // toi.py:178-227
+    V2 w1 = s[0].w, w2 = s[1].w, w3 = s[2].w;
+    V2 e12 = sub(w2, w1);
+    float d12_1 = dot(w2, e12), d12_2 = -dot(w1, e12);
+    V2 e13 = sub(w3, w1);
+    float d13_1 = dot(w3, e13), d13_2 = -dot(w1, e13);
+    V2 e23 = sub(w3, w2);
+    float d23_1 = dot(w3, e23), d23_2 = -dot(w2, e23);
+    float n123 = cross(e12, e13);
+    float d123_1 = n123 * cross(w2, w3), d123_2 = n123 * cross(w3, w1), d123_3 = n123 * cross(w1, w2);
+    if (d12_2 <= 0 && d13_2 <= 0) {
+        s[0].a = 1.0f, count = 1;
+    } else if (d12_1 > 0 && d12_2 > 0 && d123_3 <= 0) {
+        float inv = 1.0f / (d12_1 + d12_2);
+        s[0].a = d12_1 * inv, s[1].a = d12_2 * inv, count = 2;
+    } else if (d13_1 > 0 && d13_2 > 0 && d123_2 <= 0) {
+        float inv = 1.0f / (d13_1 + d13_2);
+        s[0].a = d13_1 * inv, s[2].a = d13_2 * inv, s[1] = s[2], count = 2;
+    } else if (d12_1 <= 0 && d23_2 <= 0) {
+        s[1].a = 1.0f, s[0] = s[1], count = 1;
+    } else if (d13_1 <= 0 && d23_1 <= 0) {
+        s[2].a = 1.0f, s[0] = s[2], count = 1;
+    } else if (d23_1 > 0 && d23_2 > 0 && d123_1 <= 0) {
+        float inv = 1.0f / (d23_1 + d23_2);
+        s[1].a = d23_1 * inv, s[2].a = d23_2 * inv, s[0] = s[2], count = 2;
+    } else {
+        float inv = 1.0f / ((d123_1 + d123_2) + d123_3);
+        s[0].a = d123_1 * inv, s[1].a = d123_2 * inv, s[2].a = d123_3 * inv, count = 3;
+    }
+}
+
+// b2Distance, useRadii = false (toi.py:230-294)
+__device__ __noinline__ float gjk_distance(Cache &cache, const Proxy &pA, Xf xfA, const Proxy &pB, Xf xfB) {
+    SV s[3];
+    for (int j = 0; j < 3; ++j) s[j] = SV{{0, 0}, {0, 0}, {0, 0}, 0.0f, 0, 0};
+    for (int j = 0; j < cache.count; ++j) s[j] = make_vertex(pA, xfA, cache.iA[j], pB, xfB, cache.iB[j]);
+    int count = cache.count;
+    float metric2 = simplex_metric(s, count);
+    if (count > 1 && (metric2 < 0.5f * cache.metric || 2.0f * cache.metric < metric2 || metric2 < EPS)) count = 0;
+    if (count == 0) {
+        s[0] = make_vertex(pA, xfA, 0, pB, xfB, 0);
+        s[0].a = 1.0f;
+        count = 1;
+    }
+    for (int it = 0; it < 20;) {
+        int save_count = count, saveA[3], saveB[3];
+        for (int j = 0; j < 3; ++j) saveA[j] = s[j].iA, saveB[j] = s[j].iB;
+        if (count == 2)
+            gjk_solve2(s, count);
+        else if (count == 3)
+            gjk_solve3(s, count);
+        if (count == 3) break;
+        V2 d;
+        if (count == 1) {
+            d = neg(s[0].w);
+        } else {
+            V2 e12 = sub(s[1].w, s[0].w);
+            float sgn = cross(e12, neg(s[0].w));
+            d = sgn > 0 ? cross_sv(1.0f, e12) : cross_vs(e12, 1.0f);
+        }
+        if (dot(d, d) < EPS * EPS) break;
+        int iA = pA.support(rot_t(xfA.q, neg(d)));
+        int iB = pB.support(rot_t(xfB.q, d));
+        SV v = make_vertex(pA, xfA, iA, pB, xfB, iB);
+        v.a = s[count].a;  // the tentative vertex's weight is not set
+        s[count] = v;
+        ++it;
+        bool dup = false;
+        for (int j = 0; j < save_count; ++j) dup = dup || (saveA[j] == iA && saveB[j] == iB);
+        if (dup) break;
+        ++count;
+    }
+    V2 pa, pb;
+    if (count == 1) {
+        pa = s[0].wA, pb = s[0].wB;
+    } else if (count == 2) {
+        pa = {s[0].a * s[0].wA.x + s[1].a * s[1].wA.x, s[0].a * s[0].wA.y + s[1].a * s[1].wA.y};
+        pb = {s[0].a * s[0].wB.x + s[1].a * s[1].wB.x, s[0].a * s[0].wB.y + s[1].a * s[1].wB.y};
+    } else {
+        V2 p2{s[0].a * s[0].wA.x + s[1].a * s[1].wA.x, s[0].a * s[0].wA.y + s[1].a * s[1].wA.y};
+        pa = {p2.x + s[2].a * s[2].wA.x, p2.y + s[2].a * s[2].wA.y};
+        pb = pa;
+    }
+    cache.count = count;
+    for (int j = 0; j < 3; ++j) cache.iA[j] = s[j].iA, cache.iB[j] = s[j].iB;
+    cache.metric = simplex_metric(s, count);
+    return length(sub(pa, pb));
+}
+
+struct SepFn {
+    int type;
+    V2 axis, lp;
+};
+
+__device__ SepFn sep_init(const Cache &cache, const Proxy &pA, Xf xfA, const Proxy &pB, Xf xfB) {  // toi.py:299-326
+    SepFn f;
+    if (cache.count == 1) {
+        V2 pa = xf_mul(xfA, pA.vert(cache.iA[0])), pb = xf_mul(xfB, pB.vert(cache.iB[0]));
+        f.type = E_POINTS, f.axis = normalize(sub(pb, pa)), f.lp = {0.0f, 0.0f};
+    } else if (cache.iA[0] == cache.iA[1]) {
+        V2 b1 = pB.vert(cache.iB[0]), b2 = pB.vert(cache.iB[1]);
+        V2 ax = normalize(cross_vs(sub(b2, b1), 1.0f));
+        V2 n = rot(xfB.q, ax);
+        V2 lp{0.5f * (b1.x + b2.x), 0.5f * (b1.y + b2.y)};
+        V2 qb = xf_mul(xfB, lp), pa = xf_mul(xfA, pA.vert(cache.iA[0]));
+        float s = dot(sub(pa, qb), n);
+        f.type = E_FACE_B, f.axis = s < 0 ? neg(ax) : ax, f.lp = lp;
+    } else {
+        V2 a1 = pA.vert(cache.iA[0]), a2 = pA.vert(cache.iA[1]);
+        V2 ax = normalize(cross_vs(sub(a2, a1), 1.0f));
+        V2 n = rot(xfA.q, ax);
+        V2 lp{0.5f * (a1.x + a2.x), 0.5f * (a1.y + a2.y)};
+        V2 qa = xf_mul(xfA, lp), pb = xf_mul(xfB, pB.vert(cache.iB[0]));
+        float s = dot(sub(pb, qa), n);
+        f.type = E_FACE_A, f.axis = s < 0 ? neg(ax) : ax, f.lp = lp;
+    }
+    return f;
+}
+
+__device__ float sep_eval(const SepFn &f, const Proxy &pA, Xf xfA, int iA, const Proxy &pB, Xf xfB, int iB) {
+    if (f.type == E_POINTS) {
+        V2 pa = xf_mul(xfA, pA.vert(iA)), pb = xf_mul(xfB, pB.vert(iB));
+        return dot(sub(pb, pa), f.axis);
+    }
+    if (f.type == E_FACE_A) {
+        V2 n = rot(xfA.q, f.axis), qa = xf_mul(xfA, f.lp), pb = xf_mul(xfB, pB.vert(iB));
+        return dot(sub(pb, qa), n);
+    }
+    V2 n = rot(xfB.q, f.axis), qb = xf_mul(xfB, f.lp), pa = xf_mul(xfA, pA.vert(iA));
+    return dot(sub(pa, qb), n);
+}
+
+__device__ float sep_find_min(const SepFn &f, const Proxy &pA, Xf xfA, const Proxy &pB, Xf xfB, int &iA, int &iB) {
+    if (f.type == E_POINTS) {
+        iA = pA.support(rot_t(xfA.q, f.axis));
+        iB = pB.support(rot_t(xfB.q, neg(f.axis)));
+    } else if (f.type == E_FACE_A) {
+        iA = -1;
+        iB = pB.support(rot_t(xfB.q, neg(rot(xfA.q, f.axis))));
+    } else {
+        iB = -1;
+        iA = pA.support(rot_t(xfA.q, neg(rot(xfB.q, f.axis))));
+    }
+    return sep_eval(f, pA, xfA, iA, pB, xfB, iB);
+}
+
+// b2TimeOfImpact with tMax = 1 (toi.py:364-457). Returns the b2TOIOutput state; *t_out its t.
+__device__ __noinline__ int time_of_impact(const Proxy &pA, Sweep swA, const Proxy &pB, Sweep swB, float slop,
+                                           float *t_out) {
+    const float two_pi = 2.0f * PI_F;
+    {  // b2Sweep::Normalize
+        float d = two_pi * floorf(swA.a0 / two_pi);
+        swA.a0 = swA.a0 - d, swA.a = swA.a - d;
+        d = two_pi * floorf(swB.a0 / two_pi);
+        swB.a0 = swB.a0 - d, swB.a = swB.a - d;
+    }
+    float total_radius = pA.radius + pB.radius;
+    float target = bmax(slop, total_radius - 3.0f * slop);
+    float tol = 0.25f * slop;
+    float t1 = 0.0f;
+    Cache cache;
+    cache.count = 0, cache.metric = 0.0f;
+    for (int j = 0; j < 3; ++j) cache.iA[j] = cache.iB[j] = 0;
+    for (int iter = 0;;) {
+        Xf xfA = sweep_xf(swA, t1), xfB = sweep_xf(swB, t1);
+        float dist = gjk_distance(cache, pA, xfA, pB, xfB);
+        if (dist <= 0.0f) {
+            *t_out = 0.0f;
+            return E_OVERLAPPED;
+        }
+        if (dist < target + tol) {
+            *t_out = t1;
+            return E_TOUCHING;
+        }
+        SepFn f = sep_init(cache, pA, xfA, pB, xfB);
+        float t2 = 1.0f;
+        for (int push = 0;;) {
+            int iA, iB;
+            float s2 = sep_find_min(f, pA, sweep_xf(swA, t2), pB, sweep_xf(swB, t2), iA, iB);
+            if (s2 > target + tol) {
+                *t_out = 1.0f;
+                return E_SEPARATED;
+            }
+            if (s2 > target - tol) {
+                t1 = t2;
+                break;
+            }
+            float s1 = sep_eval(f, pA, sweep_xf(swA, t1), iA, pB, sweep_xf(swB, t1), iB);
+            if (s1 < target - tol) {
+                *t_out = t1;
+                return E_FAILED;
+            }
+            if (s1 <= target + tol) {
+                *t_out = t1;
+                return E_TOUCHING;
+            }
+            float a1 = t1, a2 = t2;
+            for (int cnt = 0;;) {
+                float t = (cnt & 1) ? a1 + ((target - s1) * (a2 - a1)) / (s2 - s1) : 0.5f * (a1 + a2);
+                ++cnt;
+                float s = sep_eval(f, pA, sweep_xf(swA, t), iA, pB, sweep_xf(swB, t), iB);
+                if (babs(s - target) < tol) {
+                    t2 = t;
+                    break;
+                }
+                if (s > target)
+                    a1 = t, s1 = s;
+                else
+                    a2 = t, s2 = s;
+                if (cnt == 50) break;
+            }
+            ++push;
+            if (push == MAXV) break;
+        }
+        ++iter;
+        if (iter == 20) {
+            *t_out = t1;
+            return E_FAILED;
+        }
+    }
+}
+
+__device__ __forceinline__ void sweep_advance(float &c0x, float &c0y, float &a0, float &alpha0, float cx, float cy,
+                                              float a, float alpha) {  // b2Sweep::Advance (toi.py:100-104)
+    float den = 1.0f - alpha0;
+    float beta = (alpha - alpha0) / (den != 0 ? den : 1.0f);
+    c0x = c0x + beta * (cx - c0x), c0y = c0y + beta * (cy - c0y), a0 = a0 + beta * (a - a0), alpha0 = alpha;
+}
+
+__device__ __forceinline__ bool toi_pair_rule(const W &w, int a, int b, bool unity) {  // toi.py:462-470
+    bool dyn_a = w.type[a] == DYNAMIC, dyn_b = w.type[b] == DYNAMIC;
+    bool stock = w.bullet[a] || !dyn_a || w.bullet[b] || !dyn_b;
+    if (!unity) return stock;
+    bool rule = (w.bullet[a] || w.bullet[b]) ||
+                (!dyn_b ? (bool)w.continuous[a] : (!dyn_a ? (bool)w.continuous[b] : false));
+    return stock && rule;
+}
+
+}  // namespace gb

@@ -1,0 +1,169 @@
+"""The device-side API: States in HBM (torch tensors as device memory) stepped by libgoib2d.so.
+
+    engine = Engine(model)                       # uploads the Model once (goib2d_model_create)
+    dev = to_device(broadcast(state, 4096))      # batched State, leaves (N, ...) on cuda
+    step_(model, dev, settings, dt, n_steps=10)  # in place, asynchronous on the current stream
+    new = step(model, dev, settings, dt)         # pure, like the reference's step
+
+`step(model, state, settings, dt, axis_name=None)` keeps the reference's signature (goi_jax/box2d/step.py:28): state
+in, new state out. `axis_name` is accepted and ignored: the batch is whatever leading axis the leaves carry. The
+Model is passed each call, as in the reference; its device copy is cached per (Model object, device).
+There is no CPU path: without the library every call raises.
+"""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import native
+from .settings import Settings, settings_struct
+from .world import State, map_state, state_from_leaves, state_leaves
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE.parent / "csrc"
+
+_TORCH = {np.dtype(np.float32): torch.float32, np.dtype(np.int32): torch.int32, np.dtype(np.bool_): torch.bool}
+
+
+def build(out=None):
+    """Compile libgoib2d.so for sm_100a in-tree (csrc/build.sh)."""
+    out = Path(out or native.lib_path())
+    subprocess.run(["sh", str(CSRC / "build.sh"), str(out)], check=True)
+    return out
+
+
+class Engine:
+    """A Model uploaded to the current CUDA device (one goib2d_model handle)."""
+
+    def __init__(self, model, n_bodies=None, action_joints=(), action_scale=()):
+        self.lib = native.load()
+        if n_bodies is None:
+            n_bodies = _n_bodies(model)
+        self.n_bodies = int(n_bodies)
+        self.model = model
+        packed = native.model_desc(model, self.n_bodies)
+        h = C.c_void_p()
+        native.check(self.lib.goib2d_model_create(C.byref(packed.desc), C.byref(h)))
+        self.handle = h
+        self.device = torch.cuda.current_device()
+        self.n_action = 0
+        if len(action_joints):
+            self.set_action_map(action_joints, action_scale)
+
+    def set_action_map(self, joints, scale):
+        j = np.ascontiguousarray(joints, np.int32)
+        s = np.ascontiguousarray(scale, np.float32)
+        native.check(self.lib.goib2d_model_set_action_map(self.handle, len(j), j.ctypes.data_as(native._i),
+                                                          s.ctypes.data_as(native._f)))
+        self.n_action = len(j)
+
+    def step_(self, state, settings, dt, n_steps=1, actions=None, stream=None):
+        """Step every world of a batched device State n_steps times, in place; returns the State."""
+        leaves = state_leaves(state)
+        first = leaves[0]
+        if not (isinstance(first, torch.Tensor) and first.is_cuda):
+            raise TypeError("step_ needs a device State (goib2d.to_device)")
+        n = first.shape[0]
+        if state.bodies.type.shape[1] != self.n_bodies or state.joints.motor_speed.shape[1] != len(self.model.joint_type):
+            raise ValueError(f"State has {state.bodies.type.shape[1]} bodies / {state.joints.motor_speed.shape[1]} joints,"
+                             f" the Model {self.n_bodies} / {len(self.model.joint_type)}")
+        C_ = state.contacts.pair.shape[1]
+        rows = state.fixtures.friction.shape[1]
+        for t in leaves:
+            if not t.is_contiguous() or t.device != first.device:
+                raise ValueError("State leaves must be contiguous tensors on one device")
+        ptrs = (C.c_void_p * len(leaves))(*[t.data_ptr() for t in leaves])
+        ss = settings_struct(settings)
+        act = None
+        if actions is not None:
+            if not (isinstance(actions, torch.Tensor) and actions.is_cuda and actions.dtype == torch.float32):
+                raise TypeError("actions must be a float32 cuda tensor (N, n_action)")
+            if tuple(actions.shape) != (n, self.n_action) or not actions.is_contiguous():
+                raise ValueError(f"actions must be contiguous ({n}, {self.n_action})")
+            act = actions.data_ptr()
+        if stream is None:
+            stream = torch.cuda.current_stream(first.device).cuda_stream
+        native.check(self.lib.goib2d_step(self.handle, C.addressof(ss), C.c_float(float(dt)), C_, rows, n,
+                                          int(n_steps), ptrs, act, stream))
+        return state
+
+    def status(self):
+        """Per-world status words of the last step, copied to the host (numpy int32; see goib2d_status)."""
+        n = C.c_int64()
+        p = C.c_void_p()
+        native.check(self.lib.goib2d_status(self.handle, C.byref(p), C.byref(n)))
+        out = np.zeros(n.value, np.int32)
+        if n.value:
+            native.check(self.lib.goib2d_status_copy(self.handle, out.ctypes.data_as(native._i), n.value))
+        return out
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.goib2d_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _n_bodies(model):
+    fb = np.asarray(model.fixture_body)
+    ja, jb = np.asarray(model.joint_a), np.asarray(model.joint_b)
+    tb = model.toi_bodies
+    if tb is not None:
+        return int(np.asarray(tb).shape[0])
+    return int(max([fb.max(initial=-1), ja.max(initial=-1), jb.max(initial=-1)]) + 1)
+
+
+_ENGINES = {}
+
+
+def engine_for(model, n_bodies=None):
+    key = (id(model), torch.cuda.current_device())
+    e = _ENGINES.get(key)
+    if e is None:
+        if len(_ENGINES) >= 32:
+            _ENGINES.pop(next(iter(_ENGINES))).close()
+        e = Engine(model, n_bodies)
+        _ENGINES[key] = e
+    return e
+
+
+def broadcast(state, n):
+    """n copies of a single-world numpy State, as a batched numpy State."""
+    return map_state(lambda x: np.ascontiguousarray(np.broadcast_to(np.asarray(x), (n,) + np.shape(x))), state)
+
+
+def to_device(state, device="cuda"):
+    """A numpy State (batched) as torch tensors on the device."""
+    return map_state(lambda x: torch.from_numpy(np.array(x, copy=True, order="C")).to(device), state)
+
+
+def to_host(state):
+    return map_state(lambda x: x.cpu().numpy() if isinstance(x, torch.Tensor) else np.asarray(x), state)
+
+
+def step_(model, state, settings, dt, n_steps=1, actions=None, stream=None):
+    """In-place batched step of a device State (leaves (N, ...) torch cuda tensors)."""
+    B = state.bodies.type.shape[1]
+    return engine_for(model, B).step_(state, settings, dt, n_steps, actions, stream)
+
+
+def step(model, state, settings, dt, axis_name=None):
+    """b2World::Step of every world of `state` (device tensors, leading world axis; a single-world State gets one
+    and loses it again). Pure: returns a new State."""
+    leaves = state_leaves(state)
+    single = leaves[0].dim() == 1
+    out = state_from_leaves([(t.unsqueeze(0) if single else t).clone().contiguous() for t in leaves])
+    step_(model, out, settings, dt)
+    if single:
+        out = state_from_leaves([t[0] for t in state_leaves(out)])
+    return out
+
+
+__all__ = ["Engine", "build", "step", "step_", "to_device", "to_host", "broadcast", "State", "Settings"]

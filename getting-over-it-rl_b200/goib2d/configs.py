@@ -6,6 +6,9 @@ not in the reference engine, so the chain terrain and zero-thickness edges are b
 variants: each chain segment becomes the static convex quad (x_i, floor), (x_i+1, floor), (x_i+1, h_i+1), (x_i, h_i),
 and each zero-thickness edge a 0.02 m thick box.
 
+Contact capacities are sized so that no world of the benchmark horizon overflows its contact table (a full table
+drops new contacts, as the reference does): c0 64, c1 48, c2 1024, c3 256, c4 64.
+
 `scene(name, seed)` gives a `Scene`: the level arrays plus, per world index, the dynamic bodies' parameters.
 `scene.build_world(defn, i)` issues the builder calls of world i on any WorldDef-like object (this package's, or the
 reference's when generating golden vectors); `batch(name, n, seed)` builds the Model once and the n world States
@@ -25,10 +28,11 @@ DT = F32(0.02)
 GRAVITY = (F32(0.0), F32(-9.81))
 
 
-def _per_world(seed, n, draw):
-    """Stack draw(rng) over worlds 0..n-1, each world with its own generator seeded (seed, 1, i): world i's values
-    do not depend on the batch size."""
-    rows = [draw(np.random.default_rng([seed, 1, i])) for i in range(n)]
+def _per_world(seed, n, draw, first=0):
+    """Stack draw(rng) over worlds first..first+n-1, each world with its own generator seeded (seed, 1, i): world
+    i's values do not depend on the batch size or on which shard holds it."""
+    first = first or _FIRST[0]
+    rows = [draw(np.random.default_rng([seed, 1, i])) for i in range(first, first + n)]
     return {k: np.stack([r[k] for r in rows], 0) for k in rows[0]}
 
 
@@ -185,7 +189,7 @@ def _rig_start(h, x0, dx, r):
 def c1(seed=0, n=4096):
     rng = np.random.default_rng(seed)
     h, x0, dx, polys = _level_c1(rng)
-    sc = Scene("c1_rig", _settings(True), 32, 1000, n)
+    sc = Scene("c1_rig", _settings(True), 48, 1000, n)
     sc.static_polys = polys
     sc.dyn = _per_world(seed, n, lambda r: _rig_start(h, x0, dx, r))
     sc.builder = _c1_bodies
@@ -268,7 +272,7 @@ def _c3_bodies(defn, sc, i):
 
 def c3(seed=0, n=8192):
     rng = np.random.default_rng(seed)
-    sc = Scene("c3_toi", _settings(True), 64, 300, n)
+    sc = Scene("c3_toi", _settings(True), 256, 300, n)
     boxes = [((10.0, 0.01), (0.0, -10.0), 0.0, 0.3), ((10.0, 0.01), (0.0, 10.0), 0.0, 0.3),
              ((0.01, 10.0), (-10.0, 0.0), 0.0, 0.3), ((0.01, 10.0), (10.0, 0.0), 0.0, 0.3)]
     for _ in range(12):
@@ -308,7 +312,7 @@ def _c4_bodies(defn, sc, i):
 
 def c4(seed=0, n=65536):
     sc = c1(seed, n)
-    sc.name, sc.capacity, sc.steps = "c4_scale", 48, 10000
+    sc.name, sc.capacity, sc.steps = "c4_scale", 64, 10000
     sc.builder = _c4_bodies
     h, x0, dx = sc.level
     ix = int((20.0 - x0) / dx)
@@ -316,25 +320,33 @@ def c4(seed=0, n=65536):
     return sc
 
 
+_FIRST = [0]
+
+DEFAULT_N = {"c0": 256, "c1": 4096, "c2": 1024, "c3": 8192, "c4": 65536}
 CONFIGS = {"c0": c0, "c1": c1, "c2": c2, "c3": c3, "c4": c4}
 
 
-def scene(name, seed=0, n=None):
+def scene(name, seed=0, n=None, first=0):
+    """The workload's Scene; its per-world arrays hold worlds first..first+n-1 (row 0 = world `first`)."""
     fn = CONFIGS[name]
-    return fn(seed) if n is None else fn(seed, n)
+    _FIRST[0] = first
+    try:
+        return fn(seed) if n is None else fn(seed, n)
+    finally:
+        _FIRST[0] = 0
 
 
 # ---- batches
 
 
-def batch(name, n, seed=0, compact=True):
+def batch(name, n, seed=0, compact=True, first=0):
     """(scene, Model, batched State (leaves (n, ...))) for n worlds of a workload. The Model comes from world 0's
     full build; each world's bodies, joints and dynamic-fixture AABBs come from replaying that world's dynamic
     builder calls on a WorldDef holding only the ground body, so every world equals its full WorldDef build (the
     static level is identical in all of them). compact: the compact fixture layout (static fixtures in the Model)."""
     from .world import Fixtures, State, compact_model, compact_state, empty_contacts, empty_toi
 
-    sc = scene(name, seed, n)
+    sc = scene(name, seed, n, first)
     full = sc.world_def(0)
     model, st0 = full.build(sc.capacity)
     n_static = len(sc.static_polys) + len(sc.static_boxes)

@@ -129,6 +129,9 @@ int goib2d_step(goib2d_model *model, const goib2d_settings *settings, float dt, 
  * kernels' on-chip tables was exceeded). Valid until the next goib2d_step with this model. */
 int goib2d_status(goib2d_model *model, const int32_t **device_status, int64_t *n_worlds);
 
+/* The same status words copied to host memory (n <= the last step's n_worlds); synchronises the device. */
+int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,7 +44,7 @@ inline FF ff_mul(FF a, FF b) {  // math2d.py:255-257
 }
 // Taylor coefficients (-1)^k/(2k+1)! and (-1)^k/(2k)!, k = 0..9, each as the float pair (f32(c), f32(c - f32(c)))
 // of the double value (math2d.py:260-278)
-const float SIN_C[10][2] = {{0x1p+0f, 0x0p+0f}, {-0x1.555556p-3f, 0x1.555556p-28f}, {0x1.111112p-7f, -0x1.ddddddep-32f},
+const float SIN_C[10][2] = {{0x1p+0f, 0x0p+0f}, {-0x1.555556p-3f, 0x1.555556p-28f}, {0x1.111112p-7f, -0x1.dddddep-32f},
                             {-0x1.a01a02p-13f, 0x1.7f97fap-39f}, {0x1.71de3ap-19f, 0x1.55b1ccp-45f},
                             {-0x1.ae6456p-26f, -0x1.fd5138p-52f}, {0x1.612462p-33f, -0x1.8af25ep-58f},
                             {-0x1.ae7f3ep-41f, -0x1.ccee08p-67f}, {0x1.952c78p-49f, -0x1.f9ea56p-74f},

@@ -95,7 +95,7 @@ def test_leaf_table_matches_header():
 def test_state_bytes_formula():
     """Per-world leaf bytes match the element table for a c1 world (rows = Fd)."""
     sc, model, state = configs.batch("c1", 2)
-    B, rows, J, C = 4, 3, 2, 32
+    B, rows, J, C = 4, 3, 2, 48
     spec = native.leaf_spec(B, rows, J, C)
     for (name, shape, dt), leaf in zip(spec, state_leaves(state)):
         assert leaf.shape[1:] == shape and leaf.dtype == dt, name
