@@ -3,6 +3,8 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -48,7 +50,7 @@ const LeafSpec LEAVES[GOIB2D_NUM_LEAVES] = {
     {0, 0, 1}, {1, 3, 1}, {0, 3, 1}, {2, 3, 1}, {2, 3, 1}, {2, 3, 1}, {0, 3, 2}, {0, 3, 2}, {1, 4, 1}};
 
 // Per-world scratch arena: every array of the step's working set, 16-byte aligned, stride a multiple of 256 B.
-gb::Layout scratch_layout(int B, int C, int J, int P) {
+gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     gb::Layout L{};
     int64_t off = 0;
     auto take = [&](int64_t bytes) {
@@ -58,7 +60,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P) {
     };
     const int64_t b4 = 4 * (int64_t)(B > 0 ? B : 1), c4 = 4 * (int64_t)(C > 0 ? C : 1), j4 = 4 * (int64_t)(J > 0 ? J : 1);
     L.vx = take(b4), L.vy = take(b4), L.vw = take(b4), L.cx = take(b4), L.cy = take(b4), L.ca = take(b4);
-    L.qc = take(b4), L.qs = take(b4);
+    L.qc = take(b4), L.qs = take(b4), L.qa = take(b4);
     L.aw = take(b4), L.bisl = take(b4), L.stack = take(b4), L.bflag = take(b4), L.last = take(b4);
     L.moved = take(b4), L.done = take(b4), L.minsep = take(b4), L.jok = take(b4), L.islsleep = take(b4);
     L.minst = take(b4), L.st = take(b4);
@@ -72,6 +74,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P) {
     L.jr = take((int64_t)sizeof(gb::JRow) * (J > 0 ? J : 1));
     L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
+    L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);
     return L;
 }
@@ -86,6 +89,93 @@ int upload(std::vector<void *> &allocs, const T *src, size_t n, const T **dst) {
     if (src && n) CUDA_TRY(cudaMemcpy(p, src, sizeof(T) * n, cudaMemcpyHostToDevice));
     else CUDA_TRY(cudaMemset(p, 0, bytes));
     *dst = (const T *)p;
+    return 0;
+}
+
+// The static-fixture grid of a compact model (see gb::DevModel).
+int build_grid(const goib2d_model_desc &d, const std::vector<int32_t> &rows, std::vector<void *> &allocs,
+               gb::DevModel &g) {
+    const int F = d.n_fixtures, P = d.n_pairs, R = (int)rows.size();
+    std::vector<int32_t> sfix, sidx(F, -1);
+    for (int f = 0; f < F; ++f)
+        if (d.fixture_slot[f] < 0) sidx[f] = (int)sfix.size(), sfix.push_back(f);
+    const int S = (int)sfix.size();
+    g.grid = 0;
+    if (S == 0 || R == 0 || (int64_t)R * S > (int64_t)1 << 26) return 0;  // full scan
+    std::vector<float> sfat(4 * (size_t)S);
+    float x0 = INFINITY, y0 = INFINITY, x1 = -INFINITY, y1 = -INFINITY;
+    std::vector<float> small;
+    for (int i = 0; i < S; ++i) {
+        const float *a = d.static_fat + 4 * sfix[i];
+        for (int k = 0; k < 4; ++k) sfat[4 * i + k] = a[k];
+        if (!(a[0] <= a[2] && a[1] <= a[3])) return 0;  // a non-finite or inverted box: keep the full scan
+        x0 = fminf(x0, a[0]), y0 = fminf(y0, a[1]), x1 = fmaxf(x1, a[2]), y1 = fmaxf(y1, a[3]);
+        small.push_back(fminf(a[2] - a[0], a[3] - a[1]));
+    }
+    std::nth_element(small.begin(), small.begin() + small.size() / 2, small.end());
+    float cell = fmaxf(2.0f * small[small.size() / 2], 1e-3f);
+    int nx = 0, ny = 0;
+    std::vector<int32_t> start, items;
+    for (int attempt = 0; attempt < 24; ++attempt, cell *= 1.5f) {
+        double fx = ((double)x1 - x0) / cell + 1, fy = ((double)y1 - y0) / cell + 1;
+        if (fx * fy > 4e6) continue;
+        nx = (int)fx, ny = (int)fy;
+        float inv = 1.0f / cell;
+        std::vector<int32_t> cnt((size_t)nx * ny + 1, 0);
+        int64_t total = 0;
+        for (int i = 0; i < S; ++i) {
+            int cx0 = gb::grid_cell(sfat[4 * i], x0, inv, nx), cx1 = gb::grid_cell(sfat[4 * i + 2], x0, inv, nx);
+            int cy0 = gb::grid_cell(sfat[4 * i + 1], y0, inv, ny), cy1 = gb::grid_cell(sfat[4 * i + 3], y0, inv, ny);
+            total += (int64_t)(cx1 - cx0 + 1) * (cy1 - cy0 + 1);
+        }
+        if (total > (int64_t)1 << 24) continue;
+        start.assign((size_t)nx * ny + 1, 0);
+        for (int i = 0; i < S; ++i) {
+            int cx0 = gb::grid_cell(sfat[4 * i], x0, inv, nx), cx1 = gb::grid_cell(sfat[4 * i + 2], x0, inv, nx);
+            int cy0 = gb::grid_cell(sfat[4 * i + 1], y0, inv, ny), cy1 = gb::grid_cell(sfat[4 * i + 3], y0, inv, ny);
+            for (int cy = cy0; cy <= cy1; ++cy)
+                for (int cx = cx0; cx <= cx1; ++cx) start[(size_t)cy * nx + cx + 1]++;
+        }
+        for (size_t k = 1; k < start.size(); ++k) start[k] += start[k - 1];
+        items.assign((size_t)total, 0);
+        std::vector<int32_t> fill(start.begin(), start.end() - 1);
+        for (int i = 0; i < S; ++i) {
+            int cx0 = gb::grid_cell(sfat[4 * i], x0, inv, nx), cx1 = gb::grid_cell(sfat[4 * i + 2], x0, inv, nx);
+            int cy0 = gb::grid_cell(sfat[4 * i + 1], y0, inv, ny), cy1 = gb::grid_cell(sfat[4 * i + 3], y0, inv, ny);
+            for (int cy = cy0; cy <= cy1; ++cy)
+                for (int cx = cx0; cx <= cx1; ++cx) items[fill[(size_t)cy * nx + cx]++] = i;
+        }
+        g.inv_cell = inv;
+        break;
+    }
+    if (start.empty()) return 0;
+    std::vector<int32_t> cand((size_t)R * S, -1), dd;
+    std::vector<int32_t> row_of(F, -1);
+    for (int r = 0; r < R; ++r) row_of[rows[r]] = r;
+    for (int p = 0; p < P; ++p) {
+        int a = d.pair_a[p], b = d.pair_b[p];
+        if (row_of[a] >= 0 && row_of[b] >= 0)
+            dd.push_back(p);
+        else if (row_of[a] >= 0 && sidx[b] >= 0)
+            cand[(size_t)row_of[a] * S + sidx[b]] = p;
+        else if (row_of[b] >= 0 && sidx[a] >= 0)
+            cand[(size_t)row_of[b] * S + sidx[a]] = p;
+    }
+    int rc = 0;
+    const int32_t *d_start, *d_items, *d_sfix, *d_cand, *d_dd;
+    const float *d_sfat;
+    rc = rc ? rc : upload(allocs, start.data(), start.size(), &d_start);
+    rc = rc ? rc : upload(allocs, items.data(), items.size(), &d_items);
+    rc = rc ? rc : upload(allocs, sfix.data(), sfix.size(), &d_sfix);
+    rc = rc ? rc : upload(allocs, sfat.data(), sfat.size(), &d_sfat);
+    rc = rc ? rc : upload(allocs, cand.data(), cand.size(), &d_cand);
+    rc = rc ? rc : upload(allocs, dd.data(), dd.size(), &d_dd);
+    if (rc) return rc;
+    g.n_static = S, g.n_rows = R, g.nx = nx, g.ny = ny, g.gx0 = x0, g.gy0 = y0;
+    g.cell_start = d_start, g.cell_items = d_items, g.sfix = d_sfix, g.sfat = d_sfat, g.cand_rs = d_cand;
+    g.n_dd = (int)dd.size(), g.dd = d_dd;
+    g.max_hits = 256;
+    g.grid = 1;
     return 0;
 }
 
@@ -211,6 +301,7 @@ int goib2d_model_create(const goib2d_model_desc *d, goib2d_model **out) {
             c.fixture_slot = slot, c.row_fixture = rowf, c.static_fat = sf, c.static_friction = sfr;
             c.static_restitution = srs, c.compact = 1;
             m->has_compact = 1, m->n_rows_compact = (int)rows.size();
+            if (!rc) rc = build_grid(*d, rows, m->allocs, c);
         }
     }
     if (rc) {
@@ -276,7 +367,7 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
     p.m = *dm;
     for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
     p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
-    p.lay = scratch_layout(dm->B, C, dm->J, dm->P);
+    p.lay = scratch_layout(dm->B, C, dm->J, dm->P, dm->grid ? dm->max_hits : 0);
     size_t need = (size_t)p.lay.stride * (size_t)n_worlds;
     if (need > m->scratch_bytes) {
         if (m->scratch) cudaFree(m->scratch), m->scratch = nullptr, m->scratch_bytes = 0;

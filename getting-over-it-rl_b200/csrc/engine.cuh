@@ -20,7 +20,28 @@ struct DevModel {
     const float *static_fat, *static_friction, *static_restitution;
     const int32_t *row_fixture;   // [F] fixture of each State.fixtures row (valid for rows < n_rows)
     int any_toi_body;             // some body is bullet or continuous at build
+    // Static-fixture grid (compact models; built by goib2d_model_create). FindNewContacts asks it for the static
+    // fixtures near each non-static fixture instead of scanning every candidate pair; the hits are sorted back into
+    // candidate order, so the created contacts are the same as the full scan's.
+    int grid;                     // 1 when the tables below are set
+    int n_static, n_rows, nx, ny;
+    float gx0, gy0, inv_cell;     // origin and 1 / cell size
+    const int32_t *cell_start;    // [nx * ny + 1] CSR over cells
+    const int32_t *cell_items;    // static indices, per cell
+    const float *sfat;            // [n_static][4] fat AABB of each static fixture
+    const int32_t *sfix;          // [n_static] fixture of each static index
+    const int32_t *cand_rs;       // [n_rows][n_static] candidate of (row's fixture, static fixture), -1 if none
+    int n_dd;                     // candidates whose fixtures are both non-static
+    const int32_t *dd;            // [n_dd] those candidates, ascending
+    int max_hits;                 // per-world hit buffer; more hits fall back to the full scan
 };
+
+// Grid cell of a coordinate (the same float operations on the host, when binning, and on the device)
+__host__ __device__ __forceinline__ int grid_cell(float x, float x0, float inv, int n) {
+    float f = floorf((x - x0) * inv);
+    int c = f < 0.0f ? 0 : (f > (float)(n - 1) ? n - 1 : (int)f);
+    return c;
+}
 
 struct Leaves {
     void *p[GOIB2D_NUM_LEAVES];
@@ -66,7 +87,7 @@ struct Man {
 // Byte offsets of the per-world scratch arrays (computed on the host by scratch_layout()).
 struct Layout {
     // [B]
-    int64_t vx, vy, vw, cx, cy, ca, qc, qs;
+    int64_t vx, vy, vw, cx, cy, ca, qc, qs, qa;
     int64_t aw, bisl, stack, bflag, last, moved, done, minsep, jok, islsleep, minst, st;
     int64_t adv;  // [B][8] TOI: advanced c0x, c0y, a0, alpha0, xf (px, py, c, s)
     // [C]
@@ -80,6 +101,7 @@ struct Layout {
     int64_t jr, jorder, jisl, jflag;
     // [ceil(P/32)]
     int64_t bitmap;
+    int64_t hits;  // [max_hits] new-pair candidates of the grid path
     int64_t stride;  // bytes per world (multiple of 256)
 };
 

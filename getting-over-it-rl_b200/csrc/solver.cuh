@@ -5,10 +5,19 @@
 
 namespace gb {
 
-// Body working arrays of the island solve (velocities and positions, B entries each)
+// Body working arrays of the island solve (velocities and positions, B entries each). qc / qs hold rot_of(qa[b]):
+// a memo of each body's last rotation, keyed on the angle's bits, so a body whose angle did not change (a static
+// body in the position passes) reuses it; the same angle gives the same floats, so the memo is exact.
 struct Bodies {
-    float *vx, *vy, *vw, *cx, *cy, *ca, *qc, *qs;
+    float *vx, *vy, *vw, *cx, *cy, *ca, *qc, *qs, *qa;
 };
+
+__device__ __forceinline__ Rot body_rot(const Bodies &bd, int b, float angle) {
+    if (__float_as_uint(bd.qa[b]) == __float_as_uint(angle)) return {bd.qc[b], bd.qs[b]};
+    Rot q = rot_of(angle);
+    bd.qa[b] = angle, bd.qc[b] = q.c, bd.qs[b] = q.s;
+    return q;
+}
 
 // b2ContactSolver constructor + InitializeVelocityConstraints for one ordered contact (contact_solver.py:32-147)
 __device__ __noinline__ void prepare_contact(const DevModel &m, const W &w, int slot, const Bodies &bd, bool warm,
@@ -191,7 +200,7 @@ __device__ __noinline__ float contact_solve_position(const VCRow &c, const Bodie
     float aA = bd.ca[c.ia], aB = bd.ca[c.ib];
     float min_sep = 0.0f;
     for (int j = 0; j < c.pc_count; ++j) {
-        Xf xfA = xf_from(cA, aA, c.lcA), xfB = xf_from(cB, aB, c.lcB);
+        Xf xfA = xf_from_q(cA, body_rot(bd, c.ia, aA), c.lcA), xfB = xf_from_q(cB, body_rot(bd, c.ib, aB), c.lcB);
         V2 nrm, p;
         float sep;
         if (c.mtype == CIRCLES) {
@@ -574,10 +583,11 @@ __device__ __noinline__ void joint_solve_velocity(JRow &r, const Bodies &bd, boo
     bd.vx[r.ib] = vB.x, bd.vy[r.ib] = vB.y, bd.vw[r.ib] = wB;
 }
 
-__device__ __forceinline__ bool rev_point_position(const JRow &r, V2 &cA, float &aA, V2 &cB, float &aB,
-                                                   const goib2d_settings &s, float ang_err) {  // joints.py:501-520
+__device__ __forceinline__ bool rev_point_position(const JRow &r, const Bodies &bd, V2 &cA, float &aA, V2 &cB,
+                                                   float &aB, const goib2d_settings &s,
+                                                   float ang_err) {  // joints.py:501-520
     const float mA = r.mA, mB = r.mB, iA = r.iA, iB = r.iB;
-    Rot qA = rot_of(aA), qB = rot_of(aB);
+    Rot qA = body_rot(bd, r.ia, aA), qB = body_rot(bd, r.ib, aB);
     V2 ra = rot(qA, r.la), rb = rot(qB, r.lb);
     float Cx = ((cB.x + rb.x) - cA.x) - ra.x;
     float Cy = ((cB.y + rb.y) - cA.y) - ra.y;
@@ -626,9 +636,9 @@ __device__ __noinline__ bool joint_solve_position(const JRow &r, const Bodies &b
         }
         float limit_impulse = -r.motor_mass * C;
         if (lim) aA = aA - iA * limit_impulse, aB = aB + iB * limit_impulse;
-        ok = rev_point_position(r, cA, aA, cB, aB, s, ang_err);
+        ok = rev_point_position(r, bd, cA, aA, cB, aB, s, ang_err);
     } else if (r.type == PRISMATIC) {  // joints.py:523-566
-        Rot qA = rot_of(aA), qB = rot_of(aB);
+        Rot qA = body_rot(bd, r.ia, aA), qB = body_rot(bd, r.ib, aB);
         V2 ra = rot(qA, r.la), rb = rot(qB, r.lb);
         float dx = ((cB.x + rb.x) - cA.x) - ra.x, dy = ((cB.y + rb.y) - cA.y) - ra.y;
         V2 ax = rot(qA, r.lx);
@@ -667,7 +677,7 @@ __device__ __noinline__ bool joint_solve_position(const JRow &r, const Bodies &b
         aB = aB + iB * LB;
         ok = lin_err <= s.linear_slop && ang_err <= s.angular_slop;
     } else {  // joints.py:569-595
-        Rot qA = rot_of(aA), qB = rot_of(aB);
+        Rot qA = body_rot(bd, r.ia, aA), qB = body_rot(bd, r.ib, aB);
         V2 ra = rot(qA, r.la), rb = rot(qB, r.lb);
         V3 ex, ey, ez;
         k_rev(mA, mB, iA, iB, ra, rb, ex, ey, ez);

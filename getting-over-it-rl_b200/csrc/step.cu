@@ -29,7 +29,29 @@ struct Ctx {
     char *scr;
     int lane;
     int status;
+    long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
 };
+
+// Optional per-phase cycle counters for profiling builds (-DGOIB2D_PHASE_TIMERS): lane 0 of every warp adds the
+// clock64 cycles spent in each phase; goib2d_debug_phase_cycles() reads them. Compiled out otherwise.
+#ifdef GOIB2D_PHASE_TIMERS
+__device__ unsigned long long g_phase_cycles[16];
+#define GB_PHASE(x, i)                                                                       \
+    do {                                                                                     \
+        long long t1_ = clock64();                                                           \
+        if ((x).lane == 0) atomicAdd(&g_phase_cycles[i], (unsigned long long)(t1_ - (x).t0)); \
+        (x).t0 = t1_;                                                                        \
+    } while (0)
+__device__ unsigned long long g_counts[16];  // 0 events, 1 TOI position passes, 2 TOI solves, 3 searches, 4 max events
+#define GB_COUNT(i, v) atomicAdd(&g_counts[i], (unsigned long long)(v))
+#else
+#define GB_PHASE(x, i) \
+    do {               \
+    } while (0)
+#define GB_COUNT(i, v) \
+    do {               \
+    } while (0)
+#endif
 
 __device__ __forceinline__ void wake_body(W &w, int b) {  // b2Body::SetAwake(true)
     if (!w.awake[b]) {
@@ -39,6 +61,93 @@ __device__ __forceinline__ void wake_body(W &w, int b) {  // b2Body::SetAwake(tr
 }
 
 // ---------------------------------------------------------------- FindNewContacts (pairs.py:134-178)
+// A new contact for every candidate pair whose fat AABBs overlap, whose bodies may collide and that has no contact
+// yet, created in candidate (b2BroadPhase::UpdatePairs) order into the lowest free slots. Two exact ways to find the
+// pairs: the grid path (compact models) asks the static-fixture grid for each non-static fixture's neighbours and
+// scans only the pairs of two non-static fixtures, then sorts its hits into candidate order; the scan path tests
+// every candidate in order (full-layout models, or more hits than the grid path's buffer holds).
+
+__device__ __forceinline__ void place_contact(Ctx &x, int s, int p, int key) {
+    const DevModel &m = x.m;
+    W &w = x.w;
+    int fa = m.pair_a[p], fb = m.pair_b[p];
+    w.pair[s] = p, w.fa[s] = fa, w.fb[s] = fb, w.key[s] = key;
+    w.touching[s] = 0, w.count[s] = 0;
+    w.normal_impulse[2 * s] = w.normal_impulse[2 * s + 1] = 0.0f;
+    w.tangent_impulse[2 * s] = w.tangent_impulse[2 * s + 1] = 0.0f;
+    w.point_id[2 * s] = w.point_id[2 * s + 1] = 0;
+    w.friction[s] = sqrtf(fixture_friction(m, w, fa) * fixture_friction(m, w, fb));
+    float ra = fixture_restitution(m, w, fa), rb = fixture_restitution(m, w, fb);
+    w.restitution[s] = ra > rb ? ra : rb;
+    w.tangent_speed[s] = 0.0f;
+    wake_body(w, m.fixture_body[fa]);
+    wake_body(w, m.fixture_body[fb]);
+}
+
+// is candidate p a new pair (overlap, ShouldCollide, no contact yet)?
+__device__ __forceinline__ bool is_new_pair(Ctx &x, int p, const uint32_t *bitmap) {
+    const DevModel &m = x.m;
+    const W &w = x.w;
+    int fa = m.pair_a[p], fb = m.pair_b[p];
+    int ba = m.fixture_body[fa], bb = m.fixture_body[fb];
+    if (!overlap(fixture_fat(m, w, fa), fixture_fat(m, w, fb))) return false;
+    bool can = (w.type[ba] == DYNAMIC || w.type[bb] == DYNAMIC) && w.active[ba] && w.active[bb];
+    return can && !((bitmap[p >> 5] >> (p & 31)) & 1u);
+}
+
+// the grid path's hits (candidate indices, any order); returns the count, or -1 when the buffer overflowed
+__device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits) {
+    const DevModel &m = x.m;
+    const W &w = x.w;
+    const int lane = x.lane, cap = m.max_hits;
+    int n = 0;
+    for (int r = 0; r < m.n_rows; ++r) {
+        const float *dp = w.fx_fat + 4 * r;
+        AABB D{dp[0], dp[1], dp[2], dp[3]};
+        int cx0 = grid_cell(D.lx, m.gx0, m.inv_cell, m.nx), cx1 = grid_cell(D.ux, m.gx0, m.inv_cell, m.nx);
+        int cy0 = grid_cell(D.ly, m.gy0, m.inv_cell, m.ny), cy1 = grid_cell(D.uy, m.gy0, m.inv_cell, m.ny);
+        const int32_t *cand = m.cand_rs + (int64_t)r * m.n_static;
+        for (int cy = cy0; cy <= cy1; ++cy)
+            for (int cx = cx0; cx <= cx1; ++cx) {
+                int c = cy * m.nx + cx;
+                int b0 = m.cell_start[c], b1 = m.cell_start[c + 1];
+                for (int base = b0; base < b1; base += 32) {
+                    int i = base + lane, p = -1;
+                    if (i < b1) {
+                        int si = m.cell_items[i];
+                        const float *sf = m.sfat + 4 * si;
+                        AABB S{sf[0], sf[1], sf[2], sf[3]};
+                        // report the pair only in the cell holding the lower corner of the two boxes' overlap
+                        bool here = grid_cell(fmaxf(D.lx, S.lx), m.gx0, m.inv_cell, m.nx) == cx &&
+                                    grid_cell(fmaxf(D.ly, S.ly), m.gy0, m.inv_cell, m.ny) == cy;
+                        if (here && overlap(D, S)) {
+                            int pc = cand[si];
+                            if (pc >= 0 && is_new_pair(x, pc, bitmap)) p = pc;
+                        }
+                    }
+                    unsigned mk = __ballot_sync(FULL, p >= 0);
+                    if (p >= 0) {
+                        int k = n + __popc(mk & ((1u << lane) - 1));
+                        if (k < cap) hits[k] = p;
+                    }
+                    n += __popc(mk);
+                }
+            }
+    }
+    for (int base = 0; base < m.n_dd; base += 32) {  // pairs of two non-static fixtures: every one, in order
+        int i = base + lane, p = -1;
+        if (i < m.n_dd && is_new_pair(x, m.dd[i], bitmap)) p = m.dd[i];
+        unsigned mk = __ballot_sync(FULL, p >= 0);
+        if (p >= 0) {
+            int k = n + __popc(mk & ((1u << lane) - 1));
+            if (k < cap) hits[k] = p;
+        }
+        n += __popc(mk);
+    }
+    __syncwarp();
+    return n <= cap ? n : -1;
+}
+
 __device__ void find_new_contacts(Ctx &x) {
     const DevModel &m = x.m;
     W &w = x.w;
@@ -63,38 +172,32 @@ __device__ void find_new_contacts(Ctx &x) {
     }
     const int key0 = *w.next_key;
     __syncwarp();
-    int n_new = 0;
-    for (int base = 0; base < P; base += 32) {
-        int p = base + lane;
-        bool nw_ = false;
-        int fa = 0, fb = 0, ba = 0, bb = 0;
-        if (p < P) {
-            fa = m.pair_a[p], fb = m.pair_b[p];
-            ba = m.fixture_body[fa], bb = m.fixture_body[fb];
-            if (overlap(fixture_fat(m, w, fa), fixture_fat(m, w, fb))) {
-                bool can = (w.type[ba] == DYNAMIC || w.type[bb] == DYNAMIC) && w.active[ba] && w.active[bb];
-                nw_ = can && !((bitmap[p >> 5] >> (p & 31)) & 1u);
+    int n_new = -1;
+    if (m.grid) {
+        int *hits = sp<int>(x.scr, x.p.lay.hits), *sorted = hits + m.max_hits;
+        n_new = grid_new_pairs(x, bitmap, hits);
+        if (n_new > 0) {  // into candidate order (the hits are distinct), then into the lowest free slots
+            for (int i = lane; i < n_new; i += 32) {
+                int h = hits[i], rank = 0;
+                for (int j = 0; j < n_new; ++j) rank += hits[j] < h;
+                sorted[rank] = h;
             }
+            __syncwarp();
+            for (int k = lane; k < n_new && k < n_free; k += 32) place_contact(x, freeslot[k], sorted[k], key0 + k);
         }
-        unsigned mk = __ballot_sync(FULL, nw_);
-        if (nw_) {
-            int rank = n_new + __popc(mk & ((1u << lane) - 1));
-            if (rank < n_free) {
-                int s = freeslot[rank];
-                w.pair[s] = p, w.fa[s] = fa, w.fb[s] = fb, w.key[s] = key0 + rank;
-                w.touching[s] = 0, w.count[s] = 0;
-                w.normal_impulse[2 * s] = w.normal_impulse[2 * s + 1] = 0.0f;
-                w.tangent_impulse[2 * s] = w.tangent_impulse[2 * s + 1] = 0.0f;
-                w.point_id[2 * s] = w.point_id[2 * s + 1] = 0;
-                w.friction[s] = sqrtf(fixture_friction(m, w, fa) * fixture_friction(m, w, fb));
-                float ra = fixture_restitution(m, w, fa), rb = fixture_restitution(m, w, fb);
-                w.restitution[s] = ra > rb ? ra : rb;
-                w.tangent_speed[s] = 0.0f;
-                wake_body(w, ba);
-                wake_body(w, bb);
+    }
+    if (n_new < 0) {  // the scan path
+        n_new = 0;
+        for (int base = 0; base < P; base += 32) {
+            int p = base + lane;
+            bool nw_ = p < P && is_new_pair(x, p, bitmap);
+            unsigned mk = __ballot_sync(FULL, nw_);
+            if (nw_) {
+                int rank = n_new + __popc(mk & ((1u << lane) - 1));
+                if (rank < n_free) place_contact(x, freeslot[rank], p, key0 + rank);
             }
+            n_new += __popc(mk);
         }
-        n_new += __popc(mk);
     }
     __syncwarp();
     if (lane == 0) {
@@ -285,7 +388,8 @@ __device__ void synchronize_fixtures(Ctx &x, const int *moved, int n_rows) {
 __device__ __forceinline__ Bodies bodies_of(Ctx &x) {
     const Layout &L = x.p.lay;
     return {sp<float>(x.scr, L.vx), sp<float>(x.scr, L.vy), sp<float>(x.scr, L.vw), sp<float>(x.scr, L.cx),
-            sp<float>(x.scr, L.cy), sp<float>(x.scr, L.ca), sp<float>(x.scr, L.qc), sp<float>(x.scr, L.qs)};
+            sp<float>(x.scr, L.cy), sp<float>(x.scr, L.ca), sp<float>(x.scr, L.qc), sp<float>(x.scr, L.qs),
+            sp<float>(x.scr, L.qa)};
 }
 
 // ---------------------------------------------------------------- b2World::Solve (step.py:73-194)
@@ -296,6 +400,7 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
     const int B = w.B, C = w.C, J = w.J, lane = x.lane;
     const Layout &L = x.p.lay;
     IslandOut isl = find_islands(x);
+    GB_PHASE(x, 2);
     int *bisl = sp<int>(x.scr, L.bisl), *corder = sp<int>(x.scr, L.corder), *cisl = sp<int>(x.scr, L.cisl);
     int *jorder = sp<int>(x.scr, L.jorder), *jisl = sp<int>(x.scr, L.jisl);
     int *done = sp<int>(x.scr, L.done), *jok = sp<int>(x.scr, L.jok), *moved = sp<int>(x.scr, L.moved);
@@ -322,7 +427,7 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
         bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
         if (in_isl) w.c0[2 * b] = w.c[2 * b], w.c0[2 * b + 1] = w.c[2 * b + 1], w.a0[b] = w.a[b];
         Rot q = rot_of(bd.ca[b]);
-        bd.qc[b] = q.c, bd.qs[b] = q.s;
+        bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = bd.ca[b];
     }
     __syncwarp();
     const bool warm = s.warm_starting;
@@ -330,6 +435,7 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
         prepare_contact(m, w, corder[k], bd, warm, dt_ratio, s.velocity_threshold, vc[k]);
     for (int k = lane; k < isl.n_joints; k += 32) prepare_joint(m, w, jorder[k], bd, s, dt, dt_ratio, warm, jr[k]);
     __syncwarp();
+    GB_PHASE(x, 3);
     const bool v24 = s.revolute_v24;
     if (lane == 0) {
         if (warm)
@@ -341,6 +447,7 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
         }
     }
     __syncwarp();
+    GB_PHASE(x, 4);
     for (int k = lane; k < isl.n_contacts; k += 32) {  // StoreImpulses (contact_solver.py:293-304)
         const VCRow &c = vc[k];
         for (int j = 0; j < c.count; ++j)
@@ -396,6 +503,7 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
         }
     }
     __syncwarp();
+    GB_PHASE(x, 5);
     for (int b = lane; b < B; b += 32) {  // write back + SynchronizeTransform (step.py:141-151)
         if (bisl[b] < 0) continue;
         w.c[2 * b] = bd.cx[b], w.c[2 * b + 1] = bd.cy[b], w.a[b] = bd.ca[b];
@@ -450,8 +558,11 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
     }
     for (int b = lane; b < B; b += 32) moved[b] = bisl[b] >= 0 && w.type[b] != STATIC;
     __syncwarp();
+    GB_PHASE(x, 6);
     synchronize_fixtures(x, moved, w.rows);
+    GB_PHASE(x, 7);
     find_new_contacts(x);
+    GB_PHASE(x, 8);
 }
 
 // ---------------------------------------------------------------- b2World::SolveTOI (toi.py:462-865)
@@ -498,7 +609,14 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
         Sweep swA{w.blc(A), {r[0], r[1]}, {w.c[2 * A], w.c[2 * A + 1]}, r[2], w.a[A]};
         Sweep swB{w.blc(Bb), {r[3], r[4]}, {w.c[2 * Bb], w.c[2 * Bb + 1]}, r[5], w.a[Bb]};
         float beta;
+        GB_COUNT(2, 1);
+#ifdef GOIB2D_PHASE_TIMERS
+        long long tt0 = clock64();
+#endif
         int st = time_of_impact(proxy_of(m, w.fa[slot]), swA, proxy_of(m, w.fb[slot]), swB, x.s.linear_slop, &beta);
+#ifdef GOIB2D_PHASE_TIMERS
+        GB_COUNT(5, clock64() - tt0);
+#endif
         float common = r[6];
         w.t_toi[slot] = st == E_TOUCHING ? bmin(common + (1.0f - common) * beta, 1.0f) : 1.0f;
         w.t_flag[slot] = 1;
@@ -635,7 +753,8 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     for (int b = lane; b < B; b += 32) {
         bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
         bd.vx[b] = w.v[2 * b], bd.vy[b] = w.v[2 * b + 1], bd.vw[b] = w.w[b];
-        bd.qc[b] = 1.0f, bd.qs[b] = 0.0f;
+        Rot q = rot_of(bd.ca[b]);
+        bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = bd.ca[b];
     }
     __syncwarp();
     for (int k = lane; k < n_isl; k += 32)  // position rows (the position-independent fields)
@@ -653,6 +772,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                                                   tb ? c.iB : 0.0f);
                 min_sep = bmin(min_sep, ms);
             }
+            GB_COUNT(1, 1);
             if (min_sep >= okay_sep) break;
         }
         // leap of faith: the TOI bodies' sweep start is the solved pose
@@ -660,10 +780,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         w.c0[2 * Bb] = bd.cx[Bb], w.c0[2 * Bb + 1] = bd.cy[Bb], w.a0[Bb] = bd.ca[Bb];
     }
     __syncwarp();
-    for (int b = lane; b < B; b += 32) {
-        Rot q = rot_of(bd.ca[b]);
-        bd.qc[b] = q.c, bd.qs[b] = q.s;
-    }
+    for (int b = lane; b < B; b += 32) body_rot(bd, b, bd.ca[b]);
     __syncwarp();
     for (int k = lane; k < n_isl; k += 32)  // velocity constraints at the solved poses, no warm start
         prepare_contact(m, w, tisl[k], bd, false, 1.0f, s.velocity_threshold, vc[k]);
@@ -734,28 +851,39 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
     int min_slot = 0;
     float min_alpha = 1.0f;
     bool pending = false;
+    int n_ev = 0;
     for (int it = 0; it <= max_events; ++it) {
-        if (pending) toi_event(x, dt, min_slot, min_alpha);
-        if (!toi_search(x, &min_slot, &min_alpha)) {
+        if (pending) toi_event(x, dt, min_slot, min_alpha), ++n_ev;
+        if (x.lane == 0) GB_COUNT(3, 1);
+        GB_PHASE(x, 10);
+        bool found = toi_search(x, &min_slot, &min_alpha);
+        GB_PHASE(x, 9);
+        if (!found) {
             pending = false;
             break;
         }
         pending = true;
     }
     if (pending) x.status |= ST_CAP;  // events capped with one still pending (the reference's limit too)
+#ifdef GOIB2D_PHASE_TIMERS
+    if (x.lane == 0) GB_COUNT(0, n_ev), atomicMax(&g_counts[4], (unsigned long long)n_ev);
+#endif
 }
 
 // b2World::Step (step.py:28-47)
 __device__ void world_step(Ctx &x, float dt) {
     W &w = x.w;
     const goib2d_settings &s = x.s;
+    GB_PHASE(x, 11);
     if (*w.new_fixture) find_new_contacts(x);
     __syncwarp();
     if (x.lane == 0) *w.new_fixture = 0;
     const float inv_dt = dt > 0 ? 1.0f / dt : 0.0f;
     const float dt_ratio = *w.inv_dt0 * dt;
     __syncwarp();
+    GB_PHASE(x, 0);
     collide(x);
+    GB_PHASE(x, 1);
     solve(x, dt, dt_ratio);
     if (s.continuous_physics) solve_toi(x, dt);
     __syncwarp();
@@ -774,7 +902,7 @@ extern "C" __global__ void __launch_bounds__(128) goib2d_step_kernel(const __gri
     const int warp = threadIdx.x >> 5;
     const int64_t world = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
     if (world >= p.n_worlds) return;
-    Ctx x{p, p.m, p.s, {}, p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0};
+    Ctx x{p, p.m, p.s, {}, p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0, clock64()};
     bind_world(x.w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
     for (int k = 0; k < p.n_steps; ++k) {
         if (p.actions && x.lane < p.n_action)  // action channels -> joint motor speeds
@@ -789,3 +917,16 @@ extern "C" __global__ void __launch_bounds__(128) goib2d_step_kernel(const __gri
     if (__any_sync(FULL, bad)) x.status |= ST_NONFINITE;
     if (x.lane == 0 && p.status) p.status[world] = x.status;
 }
+
+#ifdef GOIB2D_PHASE_TIMERS
+extern "C" int goib2d_debug_phase_cycles(unsigned long long *out, int reset) {
+    if (cudaMemcpyFromSymbol(out, g_phase_cycles, sizeof(g_phase_cycles)) != cudaSuccess) return -2;
+    if (cudaMemcpyFromSymbol(out + 16, g_counts, sizeof(g_counts)) != cudaSuccess) return -2;
+    if (reset) {
+        unsigned long long z[16] = {0};
+        cudaMemcpyToSymbol(g_phase_cycles, z, sizeof(z));
+        cudaMemcpyToSymbol(g_counts, z, sizeof(z));
+    }
+    return 0;
+}
+#endif

@@ -169,6 +169,7 @@ def _level_c1(rng, friction=0.7):
     x0, dx = -250.0, 0.25
     floor = float(h.min()) - 1.0
     polys = _terrain_quads(h, x0, dx, floor, friction)
+    rocks = []
     for _ in range(60):
         k = int(rng.integers(3, 9))
         r = float(rng.uniform(0.3, 2.0))
@@ -176,22 +177,29 @@ def _level_c1(rng, friction=0.7):
         ix = int((px - x0) / dx)
         py = float(h[ix]) + float(rng.uniform(0.0, 3.0))
         polys.append(((_convex(rng, k, r) + np.array([px, py], F32)).astype(F32), friction))
-    return h, x0, dx, polys
+        rocks.append((px, py, r))
+    return h, x0, dx, polys, rocks
 
 
-def _rig_start(h, x0, dx, r):
-    x = r.uniform(x0 + 10, x0 + 2000 * dx - 10)
-    ix = int((x - x0) / dx)
-    y = max(float(h[ix]), float(h[ix + 1])) + 0.7 + 0.02
-    return dict(x=F32(x), y=F32(y), angle=F32(r.uniform(0, 2 * np.pi)), w0=F32(r.uniform(-2, 2)))
+def _rig_start(h, x0, dx, rocks, r):
+    """The pot resting just above the terrain under it, away from every rock; the hammer above the pot (pointing
+    up and to either side), as the character starts in the game."""
+    while True:
+        x = r.uniform(x0 + 10, x0 + 2000 * dx - 10)
+        i0, i1 = int((x - 0.8 - x0) / dx), int((x + 0.8 - x0) / dx) + 1
+        y = float(h[i0:i1 + 1].max()) + 0.62
+        if all((x - px) ** 2 + (y - py) ** 2 > (rr + 2.8) ** 2 for px, py, rr in rocks):
+            break
+    ang = r.uniform(0.2 * np.pi, 0.8 * np.pi)
+    return dict(x=F32(x), y=F32(y), angle=F32(ang), w0=F32(r.uniform(-2, 2)))
 
 
 def c1(seed=0, n=4096):
     rng = np.random.default_rng(seed)
-    h, x0, dx, polys = _level_c1(rng)
+    h, x0, dx, polys, rocks = _level_c1(rng)
     sc = Scene("c1_rig", _settings(True), 48, 1000, n)
     sc.static_polys = polys
-    sc.dyn = _per_world(seed, n, lambda r: _rig_start(h, x0, dx, r))
+    sc.dyn = _per_world(seed, n, lambda r: _rig_start(h, x0, dx, rocks, r))
     sc.builder = _c1_bodies
     sc.level = (h, x0, dx)
     sc.action_joints, sc.action_scale = (0, 1), (4.0, 2.0)
