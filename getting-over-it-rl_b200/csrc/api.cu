@@ -407,4 +407,84 @@ int goib2d_status_copy(goib2d_model *m, int32_t *host, int64_t n) {
     return 0;
 }
 
+// ---- goib2d_step_noalloc: the step without any device allocation
+//
+// Some callers cannot allocate device memory at the moment they step: code running while a stream is being
+// captured into a CUDA graph, a host that hands every byte of the GPU to its own pool allocator, or a real-time loop
+// that forbids allocation after start-up. goib2d_step allocates its per-world scratch arena on first use (and grows
+// it); this variant takes the arena from a file-scope device array instead, so it calls no cudaMalloc, cudaFree or
+// allocating library routine. The array is GOIB2D_NOALLOC_SCRATCH_BYTES on every device that loads this library, held
+// until the process exits. In host code the array's name is only a host-side stand-in, so its device address is
+// looked up with cudaGetSymbolAddress once per device (by that device's first call, which should therefore come
+// before any stream capture). All calls share the array: calls that overlap on the GPU (other streams, other host
+// threads) race on it and must be serialised by the caller. The kernel initialises every scratch word it reads
+// within a call, so the contents left by an earlier call never matter and nothing is cleared here.
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GOIB2D_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+char *g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, int32_t rows,
+                        int64_t n_worlds, int32_t n_steps, void *const *leaves, const float *actions, void *stream) {
+    if (!m || !s || !leaves) return fail(GOIB2D_EINVAL, "null argument");
+    if (C < 0 || n_worlds < 0 || n_steps < 0) return fail(GOIB2D_EINVAL, "negative size");
+    if (s->velocity_iterations < 0 || s->position_iterations < 0) return fail(GOIB2D_EINVAL, "negative iterations");
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(GOIB2D_ELIMIT, "device %d beyond %d", dev, kMaxDevices);
+    if (dev != m->device) return fail(GOIB2D_EINVAL, "model lives on device %d, current device is %d", m->device, dev);
+    char *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {  // set-up, once per device, with that device current
+            void *ptr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (e != cudaSuccess)
+                return fail(GOIB2D_ECUDA, "cudaGetSymbolAddress(no-alloc scratch): %s", cudaGetErrorString(e));
+            g_noalloc_ptr[dev] = (char *)ptr;
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    std::lock_guard<std::mutex> lk(m->mu);
+    const gb::DevModel *dm = nullptr;
+    if (rows == m->full.F)
+        dm = &m->full;
+    else if (m->has_compact && rows == m->n_rows_compact)
+        dm = &m->compact;
+    else
+        return fail(GOIB2D_EINVAL, "fixture rows %d match neither the full (%d) nor the compact (%d) layout", rows,
+                    m->full.F, m->has_compact ? m->n_rows_compact : -1);
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i)
+        if (!leaves[i] && goib2d_leaf_elems(i, dm->B, rows, dm->J, C) > 0 && n_worlds > 0)
+            return fail(GOIB2D_EINVAL, "leaf %d is null", i);
+    gb::StepParams p{};
+    p.lay = scratch_layout(dm->B, C, dm->J, dm->P, dm->grid ? dm->max_hits : 0);
+    const int64_t max_worlds = (int64_t)GOIB2D_NOALLOC_SCRATCH_BYTES / p.lay.stride;
+    if (n_worlds > max_worlds)
+        return fail(GOIB2D_ELIMIT,
+                    "goib2d_step_noalloc: %lld worlds need %lld bytes of scratch, the static arena holds %lld bytes "
+                    "(%lld worlds of %lld bytes each); use goib2d_step or fewer worlds per call",
+                    (long long)n_worlds, (long long)(n_worlds * p.lay.stride),
+                    (long long)GOIB2D_NOALLOC_SCRATCH_BYTES, (long long)max_worlds, (long long)p.lay.stride);
+    if (n_worlds == 0 || n_steps == 0) return 0;
+    p.m = *dm;
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
+    p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
+    p.scratch = scratch;
+    p.status = nullptr;  // no per-world status words (their buffer would need an allocation)
+    if (actions && m->n_action > 0) {
+        p.actions = actions, p.n_action = m->n_action, p.action_joint = m->action_joint;
+        p.action_scale = m->action_scale;
+    }
+    const int wpb = 4;
+    int64_t blocks = (n_worlds + wpb - 1) / wpb;
+    goib2d_step_kernel<<<(unsigned)blocks, 32 * wpb, 0, (cudaStream_t)stream>>>(p);
+    CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
 }  // extern "C"

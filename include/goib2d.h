@@ -132,6 +132,22 @@ int goib2d_status(goib2d_model *model, const int32_t **device_status, int64_t *n
 /* The same status words copied to host memory (n <= the last step's n_worlds); synchronises the device. */
 int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
 
+/* Bytes of the static scratch arena used by goib2d_step_noalloc (on every device that loads the library). */
+#define GOIB2D_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* goib2d_step without any device allocation, for callers that cannot allocate while they step (code inside a CUDA
+ * graph capture, a host whose pool allocator owns the GPU's memory, a loop that forbids allocation after start-up).
+ * No counterpart in the reference engine. Same arguments and results as goib2d_step, but the per-world scratch arena
+ * is a GOIB2D_NOALLOC_SCRATCH_BYTES static device array, so n_worlds is limited to that size divided by the arena
+ * bytes one world needs (which grow with bodies, contact slots, joints and candidate pairs); larger batches return
+ * GOIB2D_ELIMIT with a message and launch nothing. The first call on each device looks the array's address up
+ * (cudaGetSymbolAddress): make that call before any stream capture. All calls share the array, so calls that
+ * overlap on the GPU race and must be serialised by the caller; earlier contents never affect a call. goib2d_status
+ * does not report these calls. */
+int goib2d_step_noalloc(goib2d_model *model, const goib2d_settings *settings, float dt, int32_t contact_capacity,
+                        int32_t fixture_rows, int64_t n_worlds, int32_t n_steps, void *const *leaves,
+                        const float *actions, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
