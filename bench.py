@@ -155,14 +155,14 @@ def main():
         return
     import torch
     import torch.distributed as dist
-    from goib2d import api, configs
+    from goib2d import api, configs, shard
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world_size > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     n = args.worlds or configs.DEFAULT_N[args.config]
-    first = rank * n  # weak scaling: every rank steps its own n seeded worlds
+    first, _ = shard.world_range(n, rank)  # weak scaling: every rank steps its own n seeded worlds
     sc, model, host = configs.batch(args.config, n, args.seed, first=first)
     eng = api.Engine(model, host.bodies.type.shape[1], sc.action_joints, sc.action_scale)
     state = api.to_device(host, dev)
@@ -224,14 +224,9 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = world_size * n * Ke / (float(te.item()) / 1e3)
 
-    # episode statistics gathered over NCCL (off the timed path): pot x position and status per world
-    stats = torch.stack([state.bodies.c[:, 1, 0], state.bodies.v[:, 1, 0],
-                         torch.from_numpy(status.astype(np.float32)).to(dev)], 1).contiguous()
-    if world_size > 1:
-        allst = [torch.empty_like(stats) for _ in range(world_size)]
-        dist.all_gather(allst, stats)
-        stats = torch.cat(allst)
-    nonfinite = int(((stats[:, 2].to(torch.int32) & 2) != 0).sum().item())
+    # episode statistics gathered over NCCL (off the timed path): body 1's position / velocity and the status word
+    stats = shard.gather_stats(shard.episode_stats(state, 1, status))
+    nonfinite = int(((stats[:, 4].to(torch.int32) & 2) != 0).sum().item())
 
     if rank == 0:
         bytes_ws = state_bytes(state) + (8 if na else 0)

@@ -5,7 +5,7 @@
  *   - goi_jax/box2d/gpu/kernel.py:573-599, gpu/pairs.py:242-259, gpu/islands.py:273-286,
  *     gpu/toi_search.py:567-581, gpu/toi_event.py:732-743   the jax.custom_batching.custom_vmap batch rules that
  *     receive the whole batch of worlds and launch one kernel over it. A JAX FFI handler registered for
- *     "goib2d_step" calls goib2d_step() from exactly that seam (INTEGRATION.md shows the binding).
+ *     "goib2d_step" calls goib2d_step() from exactly that seam.
  *
  * Data contract. A batch of N worlds shares one Model (scene constants; uploaded once, goib2d_model_create) and
  * owns one State: GOIB2D_NUM_LEAVES arrays ("leaves"), each laid out (N, ...) row-major - the layout of the

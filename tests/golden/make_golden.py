@@ -1,6 +1,9 @@
 """Generate the golden vectors: the reference engine's own states, stepped by the reference's own Python code.
 
-    python tests/golden/make_golden.py [--jobs 8] [--only NAME ...]      (needs /root/reference; not on the GPU box)
+    python tests/golden/make_golden.py --reference PATH [--jobs 8] [--only NAME ...]
+
+PATH is a checkout of miwate/getting-over-it-rl (or the GOIB2D_REFERENCE environment variable); it is read, never
+written, and only this generator needs it.
 
 The reference (goi_jax/box2d) is JAX; jax is not installed here, so `tests/golden/jaxshim` stands in for it with
 numpy (one world at a time, JAX's float32/int32 dtype rules, `.at[]` updates, eager control flow). The reference's
@@ -19,6 +22,7 @@ built state.
 import argparse
 import json
 import multiprocessing as mp
+import os
 import sys
 import time
 import types
@@ -28,7 +32,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REFERENCE = Path("/root/reference")
+REFERENCE = Path(os.environ.get("GOIB2D_REFERENCE", "reference"))
 
 GAME_SCENES = ["free_fall", "box_on_ground", "box_stack", "polygons_at_angles", "polygon_circle", "revolute",
                "prismatic", "weld", "pile", "misc", "late_wake", "thin_plates", "limits_mid_run"]
@@ -61,6 +65,7 @@ def _jsonable(x):
 def setup_reference():
     """Import the reference engine with the numpy stand-in for jax, and stub the modules its scene files import
     that need the (unbuilt) Box2D oracle library."""
+    REFERENCE = Path(os.environ.get("GOIB2D_REFERENCE", "reference"))
     sys.path.insert(0, str(HERE / "jaxshim"))
     sys.path.insert(0, str(REFERENCE))
     sys.path.insert(0, str(REFERENCE / "tests" / "box2d"))
@@ -188,7 +193,10 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--jobs", type=int, default=8)
     ap.add_argument("--only", nargs="*")
+    ap.add_argument("--reference", default=None, help="checkout of the reference repository")
     args = ap.parse_args()
+    if args.reference:
+        os.environ["GOIB2D_REFERENCE"] = str(Path(args.reference).resolve())
     jobs = all_jobs()
     if args.only:
         jobs = [j for j in jobs if job_name(j) in args.only]
