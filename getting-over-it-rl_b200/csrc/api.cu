@@ -73,6 +73,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.rec = take(8 * c4);
     L.jr = take((int64_t)sizeof(gb::JRow) * (J > 0 ? J : 1));
     L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
+    L.adj_start = take(4 * (int64_t)(B + 1)), L.adj_cur = take(b4), L.adj = take(2 * 8 * (int64_t)(C > 0 ? C : 1));
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);
@@ -270,6 +271,22 @@ int goib2d_model_create(const goib2d_model_desc *d, goib2d_model **out) {
     UP(pair_a, P);
     UP(pair_b, P);
 #undef UP
+    if (!rc) {  // each body's joints, highest index first, with the body at the other end (the island walk's order)
+        std::vector<int32_t> jstart(B + 1, 0), jadj(2 * (size_t)(2 * J > 0 ? 2 * J : 1));
+        for (int j = 0; j < J; ++j) {
+            ++jstart[d->joint_a[j] + 1];
+            if (d->joint_b[j] != d->joint_a[j]) ++jstart[d->joint_b[j] + 1];
+        }
+        for (int b = 0; b < B; ++b) jstart[b + 1] += jstart[b];
+        std::vector<int32_t> pos(jstart.begin(), jstart.end() - 1);
+        for (int j = J - 1; j >= 0; --j) {
+            int a = d->joint_a[j], b = d->joint_b[j];
+            jadj[2 * pos[a]] = j, jadj[2 * pos[a] + 1] = b, ++pos[a];
+            if (b != a) jadj[2 * pos[b]] = j, jadj[2 * pos[b] + 1] = a, ++pos[b];
+        }
+        rc = upload(m->allocs, jstart.data(), jstart.size(), &g.jadj_start);
+        if (!rc) rc = upload(m->allocs, jadj.data(), jadj.size(), &g.jadj);
+    }
     const int32_t *d_ident = nullptr;
     if (!rc) rc = upload(m->allocs, ident.data(), (size_t)F, &d_ident);
     g.fixture_slot = d_ident, g.row_fixture = d_ident, g.compact = 0;

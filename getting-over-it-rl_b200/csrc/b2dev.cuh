@@ -153,7 +153,7 @@ static __device__ __constant__ float k_cos_c[10][2] = {
     {0x1.a01a02p-16f, -0x1.7f97fap-42f}, {-0x1.27e4fcp-22f, 0x1.10ec14p-47f}, {0x1.1eed8ep-29f, 0x1.ff1b14p-54f},
     {-0x1.93974ap-37f, -0x1.180f94p-62f}, {0x1.ae7f3ep-45f, 0x1.ccee08p-71f}, {-0x1.682786p-53f, -0x1.dcbeccp-80f}};
 
-static __device__ __noinline__ Rot rot_of(float x) {
+static __device__ __noinline__ Rot rot_of_ff(float x) {
     const float pio2_0 = 0x1.921fb6p+0f, pio2_1 = -0x1.777a5cp-25f, pio2_2 = -0x1.ee59dap-50f;
     const float two_over_pi = 0x1.45f306p-1f;
     float k = rintf(x * two_over_pi);
@@ -175,6 +175,36 @@ static __device__ __noinline__ Rot rot_of(float x) {
     float sn = q == 0 ? s : q == 1 ? c : q == 2 ? -s : -c;
     float cs = q == 0 ? c : q == 1 ? -s : q == 2 ? -c : s;
     return {cs, x == 0 ? x : sn};
+}
+
+// The same values, fast: sin and cos in double precision rounded once to float, which is the correct rounding of
+// sin(x) / cos(x) unless the double lies within ROT_TOL (relative) of a midpoint between two floats; those
+// arguments, and |x| > ROT_FAST_MAX where the float-float reduction above drifts from the true value, take rot_of_ff.
+// Checked equal to rot_of_ff, bit for bit, on every float32 argument (rot_check.cu runs the sweep; without the cutoff
+// the first difference is at |x| = 2^24).
+constexpr float ROT_FAST_MAX = 0x1p+16f;
+constexpr double ROT_TOL = 0x1p-36;
+GBD bool rounds_clear(double d, float f) {  // d is farther than ROT_TOL * |d| from both midpoints around f
+    double fd = (double)f;
+    double up = 0.5 * (fd + (double)nextafterf(f, INFINITY)), dn = 0.5 * (fd + (double)nextafterf(f, -INFINITY));
+    double tol = fabs(d) * ROT_TOL;
+    return fabs(d - up) > tol && fabs(d - dn) > tol;
+}
+GBD bool rot_fast(float x, Rot &q) {  // false: the argument needs rot_of_ff
+    if (!(fabsf(x) <= ROT_FAST_MAX)) return false;
+    if (x == 0.0f) {
+        q = {1.0f, x};
+        return true;
+    }
+    double sd, cd;
+    sincos((double)x, &sd, &cd);
+    float s = __double2float_rn(sd), c = __double2float_rn(cd);
+    q = {c, s};
+    return rounds_clear(sd, s) && rounds_clear(cd, c);
+}
+static __device__ __noinline__ Rot rot_of(float x) {
+    Rot q;
+    return rot_fast(x, q) ? q : rot_of_ff(x);
 }
 
 GBD Xf xf_from(V2 c, float a, V2 lc) {  // b2Body::SynchronizeTransform: q.Set(a); p = c - q lc

@@ -20,6 +20,8 @@ struct DevModel {
     const float *static_fat, *static_friction, *static_restitution;
     const int32_t *row_fixture;   // [F] fixture of each State.fixtures row (valid for rows < n_rows)
     int any_toi_body;             // some body is bullet or continuous at build
+    const int32_t *jadj_start;    // [B + 1] CSR over bodies of jadj
+    const int32_t *jadj;          // (joint, other body) pairs: each body's joints, highest index first
     // Static-fixture grid (compact models; built by goib2d_model_create). FindNewContacts asks it for the static
     // fixtures near each non-static fixture instead of scanning every candidate pair; the hits are sorted back into
     // candidate order, so the created contacts are the same as the full scan's.
@@ -99,6 +101,8 @@ struct Layout {
     int64_t solved;  // [C]
     // [J]
     int64_t jr, jorder, jisl, jflag;
+    // island graph: [B + 1] CSR start and [B] fill cursor over bodies, [2C] (contact slot, other body) pairs
+    int64_t adj_start, adj_cur, adj;
     // [ceil(P/32)]
     int64_t bitmap;
     int64_t hits;  // [max_hits] new-pair candidates of the grid path

@@ -25,7 +25,7 @@ struct Ctx {
     const StepParams &p;
     const DevModel &m;
     const goib2d_settings &s;
-    W w;
+    W &w;  // shared memory, one per warp: a per-thread copy would cost 32x its size in local memory
     char *scr;
     int lane;
     int status;
@@ -253,16 +253,42 @@ __device__ void collide(Ctx &x) {
     }
     for (int b = lane; b < B; b += 32) aw[b] = w.awake[b];
     __syncwarp();
-    if (lane == 0) {  // the walk newest first: visits and the wakes they cause
-        for (int k = 0; k < n_live; ++k) {
-            int s = order[k];
-            int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
-            bool visit = (aw[ba] && w.type[ba] != STATIC) || (aw[bb] && w.type[bb] != STATIC);
-            active[s] = visit;
-            bool wakes = over[s] ? ((man[s].count > 0) != (bool)w.touching[s]) : (w.count[s] > 0);
-            if (visit && wakes) aw[ba] = aw[bb] = 1;
+    // The walk newest first (pairs.py:60-90): a contact is visited when one of its bodies is awake and not static,
+    // and a visited contact whose touching state changes wakes both bodies for the contacts after it. Between two
+    // wakes of a non-static body nothing changes, so each round settles, in parallel, every contact up to the next
+    // such wake, which lane 0 then applies. Wakes of static bodies only reach their awake flag, at the end.
+    for (int k0 = 0;;) {
+        int first = n_live;
+        for (int base = k0; base < n_live; base += 32) {
+            int k = base + lane, s = -1;
+            bool visit = false, wakes = false, change = false;
+            if (k < n_live) {
+                s = order[k];
+                int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
+                bool sa = w.type[ba] == STATIC, sb = w.type[bb] == STATIC;
+                visit = (aw[ba] && !sa) || (aw[bb] && !sb);
+                wakes = over[s] ? ((man[s].count > 0) != (bool)w.touching[s]) : (w.count[s] > 0);
+                change = visit && wakes && ((!sa && !aw[ba]) || (!sb && !aw[bb]));
+            }
+            unsigned mk = __ballot_sync(FULL, change);
+            int f = mk ? base + __ffs(mk) - 1 : n_live;
+            if (s >= 0 && k <= f) active[s] = visit && wakes ? 2 : (int)visit;
+            if (mk) {
+                first = f;
+                break;
+            }
         }
+        __syncwarp();
+        if (first == n_live) break;
+        if (lane == 0) {
+            int s = order[first];
+            aw[m.fixture_body[w.fa[s]]] = 1, aw[m.fixture_body[w.fb[s]]] = 1;
+        }
+        __syncwarp();
+        k0 = first + 1;
     }
+    for (int s = lane; s < C; s += 32)  // wakes of static bodies (value 2: visited and waking)
+        if (active[s] == 2) aw[m.fixture_body[w.fa[s]]] = 1, aw[m.fixture_body[w.fb[s]]] = 1, active[s] = 1;
     __syncwarp();
     for (int s = lane; s < C; s += 32) {
         if (!active[s]) continue;
@@ -293,26 +319,81 @@ __device__ IslandOut find_islands(Ctx &x) {
     int *corder = sp<int>(x.scr, L.corder), *cisl = sp<int>(x.scr, L.cisl), *cflag = sp<int>(x.scr, L.cflag);
     int *jorder = sp<int>(x.scr, L.jorder), *jisl = sp<int>(x.scr, L.jisl), *jflag = sp<int>(x.scr, L.jflag);
     int *bisl = sp<int>(x.scr, L.bisl), *bflag = sp<int>(x.scr, L.bflag), *stack = sp<int>(x.scr, L.stack);
+    int *adj_start = sp<int>(x.scr, L.adj_start), *adj_cur = sp<int>(x.scr, L.adj_cur);
+    int2 *adj = sp<int2>(x.scr, L.adj);
     int n_live = list_order(x, order, lpos);
     for (int s = lane; s < C; s += 32) cisl[s] = -1, cflag[s] = 0;
     for (int j = lane; j < J; j += 32) jisl[j] = -1, jflag[j] = 0;
-    for (int b = lane; b < B; b += 32) bisl[b] = -1, bflag[b] = 0;
+    for (int b = lane; b < B; b += 32) bisl[b] = -1, bflag[b] = 0, adj_cur[b] = 0;
     __syncwarp();
+    // The contact graph the walk follows: the touching contacts in list order (edges) and, per non-static body, its
+    // edges in that order with the body at the other end (~body when that one is static). Walking a body's list is
+    // the reference's scan of every edge for those incident to the body, in the same order.
+    int n_edges = 0;
+    for (int base = 0; base < n_live; base += 32) {
+        int k = base + lane;
+        int s = k < n_live ? order[k] : -1;
+        bool t = s >= 0 && w.touching[s];
+        unsigned mk = __ballot_sync(FULL, t);
+        if (t) {
+            edges[n_edges + __popc(mk & ((1u << lane) - 1))] = s;
+            int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
+            if (w.type[ba] != STATIC) atomicAdd(&adj_cur[ba], 1);
+            if (w.type[bb] != STATIC) atomicAdd(&adj_cur[bb], 1);
+        }
+        n_edges += __popc(mk);
+    }
+    __syncwarp();
+    int run = 0;  // exclusive scan of the degrees
+    for (int base = 0; base < B; base += 32) {
+        int b = base + lane;
+        int d = b < B ? adj_cur[b] : 0, inc = d;
+        for (int o = 1; o < 32; o <<= 1) {
+            int t = __shfl_up_sync(FULL, inc, o);
+            if (lane >= o) inc += t;
+        }
+        if (b < B) adj_start[b] = run + inc - d, adj_cur[b] = 0;
+        run += __shfl_sync(FULL, inc, 31);
+    }
+    if (lane == 0) adj_start[B] = run;
+    __syncwarp();
+    for (int base = 0; base < n_edges; base += 32) {  // fill 32 edges at a time, in edge order within each list
+        int e = base + lane;
+        int s = -1, a = -1, b = -1, oa = 0, ob = 0;
+        if (e < n_edges) {
+            s = edges[e];
+            int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
+            bool sa = w.type[ba] == STATIC, sb = w.type[bb] == STATIC;
+            a = sa ? -1 : ba, b = sb || bb == ba ? -1 : bb;  // one entry for a contact within one body
+            oa = sb ? ~bb : bb, ob = sa ? ~ba : ba;           // the other end, seen from a and from b
+        }
+        int ra = 0, rb = 0;  // incidences of a (of b) on earlier lanes of this chunk
+        for (int j = 0; j < 32; ++j) {
+            int aj = __shfl_sync(FULL, a, j), bj = __shfl_sync(FULL, b, j);
+            if (j < lane) ra += (aj == a) + (bj == a), rb += (aj == b) + (bj == b);
+        }
+        if (a >= 0) adj[adj_start[a] + adj_cur[a] + ra] = make_int2(s, oa);
+        if (b >= 0) adj[adj_start[b] + adj_cur[b] + rb] = make_int2(s, ob);
+        __syncwarp();
+        if (a >= 0) atomicAdd(&adj_cur[a], 1);
+        if (b >= 0) atomicAdd(&adj_cur[b], 1);
+        __syncwarp();
+    }
     IslandOut out{0, 0, 0};
     if (lane == 0) {
-        int n_edges = 0;
-        for (int k = 0; k < n_live; ++k)
-            if (w.touching[order[k]]) edges[n_edges++] = order[k];
         int sp_ = 0, nc = 0, nj = 0, ni = 0;
+        int next_seed = B - 1;  // bodies above the last seed never qualify again: flags only get set, and only
+                                // bodies already flagged are woken
         for (;;) {
             if (sp_ == 0) {
                 int seed = -1;
-                for (int b = B - 1; b >= 0; --b)
+                for (int b = next_seed; b >= 0; --b)
                     if (w.active[b] && w.type[b] != STATIC && w.awake[b] && !bflag[b]) {
                         seed = b;
                         break;
                     }
                 if (seed < 0) break;
+                next_seed = seed - 1;
                 ++ni;
                 stack[sp_++] = seed;
                 bflag[seed] = 1;
@@ -320,21 +401,19 @@ __device__ IslandOut find_islands(Ctx &x) {
             }
             int b = stack[--sp_];
             int id = ni - 1;
-            for (int e = 0; e < n_edges; ++e) {
-                int s = edges[e];
-                int ca = m.fixture_body[w.fa[s]], cb = m.fixture_body[w.fb[s]];
-                if ((ca != b && cb != b) || cflag[s]) continue;
+            for (int q = adj_start[b], qe = adj_start[b + 1]; q < qe; ++q) {
+                int2 en = adj[q];
+                int s = en.x;
+                if (cflag[s]) continue;
                 corder[nc++] = s;
                 cisl[s] = id;
                 cflag[s] = 1;
-                int other = ca == b ? cb : ca;
-                if (!bflag[other] && w.type[other] != STATIC) stack[sp_++] = other, bflag[other] = 1;
+                int other = en.y;
+                if (other >= 0 && !bflag[other]) stack[sp_++] = other, bflag[other] = 1;
             }
-            for (int j = J - 1; j >= 0; --j) {
-                int ja = m.joint_a[j], jb = m.joint_b[j];
-                if ((ja != b && jb != b) || jflag[j]) continue;
-                int other = ja == b ? jb : ja;
-                if (!w.active[other]) continue;
+            for (int q = m.jadj_start[b], qe = m.jadj_start[b + 1]; q < qe; ++q) {
+                int j = m.jadj[2 * q], other = m.jadj[2 * q + 1];
+                if (jflag[j] || !w.active[other]) continue;
                 jorder[nj++] = j;
                 jisl[j] = id;
                 jflag[j] = 1;
@@ -566,41 +645,77 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
 }
 
 // ---------------------------------------------------------------- b2World::SolveTOI (toi.py:462-865)
+// Is the contact in `slot` a TOI candidate before sweep alignment (toi.py:500-520)? Sets its bodies.
+__device__ __forceinline__ bool toi_candidate(Ctx &x, int slot, int &A, int &Bb) {
+    const W &w = x.w;
+    bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
+    if (!base || w.t_flag[slot]) return false;
+    A = x.m.fixture_body[w.fa[slot]], Bb = x.m.fixture_body[w.fb[slot]];
+    bool actA = w.awake[A] && w.type[A] != STATIC, actB = w.awake[Bb] && w.type[Bb] != STATIC;
+    return (actA || actB) && toi_pair_rule(w, A, Bb, x.s.unity_toi);
+}
+
+// The sweeps a candidate's b2TimeOfImpact starts from: both bodies' (c0, a0) and the common alpha0.
+__device__ __forceinline__ void toi_record(const W &w, int A, int Bb, float common, float *r) {
+    r[0] = w.c0[2 * A], r[1] = w.c0[2 * A + 1], r[2] = w.a0[A];
+    r[3] = w.c0[2 * Bb], r[4] = w.c0[2 * Bb + 1], r[5] = w.a0[Bb], r[6] = common;
+}
+
 // one pass of the min-TOI search; returns found, sets *min_slot / *min_alpha (all lanes)
 __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
     const DevModel &m = x.m;
     W &w = x.w;
-    const int C = w.C, lane = x.lane;
+    const int lane = x.lane;
     const Layout &L = x.p.lay;
     int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *tneed = sp<int>(x.scr, L.tneed);
     float *rec = sp<float>(x.scr, L.rec);
     int n_live = list_order(x, order, lpos);
-    if (lane == 0) {  // sweep alignment in list order (toi.py:500-536)
-        for (int k = 0; k < n_live; ++k) {
-            int slot = order[k];
-            tneed[slot] = 0;
-            bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
-            if (!base || w.t_flag[slot]) continue;
-            int A = m.fixture_body[w.fa[slot]], Bb = m.fixture_body[w.fb[slot]];
-            bool actA = w.awake[A] && w.type[A] != STATIC, actB = w.awake[Bb] && w.type[Bb] != STATIC;
-            if (!(actA || actB) || !toi_pair_rule(w, A, Bb, x.s.unity_toi)) continue;
+    // Sweep alignment in list order (toi.py:500-536): a candidate whose bodies' sweeps sit at different alpha0
+    // advances the one behind, which every later candidate of that body sees. Between two advances nothing moves, so
+    // each round records, in parallel, every candidate up to the next advance, which lane 0 then performs.
+    for (int k0 = 0;;) {
+        int first = n_live;
+        for (int base = k0; base < n_live; base += 32) {
+            int k = base + lane, slot = -1, A = 0, Bb = 0;
+            bool cand = false;
+            float alA = 0.0f, alB = 0.0f;
+            if (k < n_live) {
+                slot = order[k];
+                cand = toi_candidate(x, slot, A, Bb);
+                if (cand) alA = w.t_alpha0[A], alB = w.t_alpha0[Bb];
+            }
+            unsigned mk = __ballot_sync(FULL, cand && alA != alB);
+            int f = mk ? base + __ffs(mk) - 1 : n_live;
+            if (slot >= 0 && k < f) {
+                tneed[slot] = cand;
+                if (cand) toi_record(w, A, Bb, alA, rec + 8 * slot);
+            }
+            if (mk) {
+                first = f;
+                break;
+            }
+        }
+        __syncwarp();
+        if (first == n_live) break;
+        if (lane == 0) {
+            int slot = order[first], A = 0, Bb = 0;
+            toi_candidate(x, slot, A, Bb);
             float alA = w.t_alpha0[A], alB = w.t_alpha0[Bb];
             float common = alA;
             if (alA < alB) {
                 sweep_advance(w.c0[2 * A], w.c0[2 * A + 1], w.a0[A], w.t_alpha0[A], w.c[2 * A], w.c[2 * A + 1],
                               w.a[A], alB);
                 common = alB;
-            } else if (alB < alA) {
+            } else {
                 sweep_advance(w.c0[2 * Bb], w.c0[2 * Bb + 1], w.a0[Bb], w.t_alpha0[Bb], w.c[2 * Bb],
                               w.c[2 * Bb + 1], w.a[Bb], alA);
             }
-            float *r = rec + 8 * slot;
-            r[0] = w.c0[2 * A], r[1] = w.c0[2 * A + 1], r[2] = w.a0[A];
-            r[3] = w.c0[2 * Bb], r[4] = w.c0[2 * Bb + 1], r[5] = w.a0[Bb], r[6] = common;
+            toi_record(w, A, Bb, common, rec + 8 * slot);
             tneed[slot] = 1;
         }
+        __syncwarp();
+        k0 = first + 1;
     }
-    __syncwarp();
     for (int k = lane; k < n_live; k += 32) {  // b2TimeOfImpact per queued contact
         int slot = order[k];
         if (!tneed[slot]) continue;
@@ -622,29 +737,30 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
         w.t_flag[slot] = 1;
     }
     __syncwarp();
-    int ms = 0;
+    // The minimum, first (or last) in list order among exact ties (toi.py:550-557), as warp reductions.
+    const bool oldest = x.s.toi_tie_oldest;
     float best = 1.0f;
-    bool found = false;
-    if (lane == 0) {  // the minimum, first (or last) in list order among exact ties (toi.py:550-557)
-        bool any = false;
-        for (int k = 0; k < n_live; ++k) {
-            int slot = order[k];
-            bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
-            if (base && w.t_flag[slot] && w.t_toi[slot] < 1.0f) any = true, best = fminf(best, w.t_toi[slot]);
-        }
-        int msp = x.s.toi_tie_oldest ? -1 : C;
-        for (int k = 0; k < n_live; ++k) {
-            int slot = order[k];
-            bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
-            if (!(base && w.t_flag[slot] && w.t_toi[slot] < 1.0f && w.t_toi[slot] == best)) continue;
-            if (x.s.toi_tie_oldest ? k > msp : k < msp) ms = slot, msp = k;
-        }
-        const float done_alpha = 1.0f - 10.0f * EPS;
-        found = any && !(done_alpha < best);
+    for (int k = lane; k < n_live; k += 32) {
+        int slot = order[k];
+        bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
+        if (base && w.t_flag[slot] && w.t_toi[slot] < 1.0f) best = fminf(best, w.t_toi[slot]);
     }
-    *min_slot = __shfl_sync(FULL, ms, 0);
-    *min_alpha = __shfl_sync(FULL, best, 0);
-    return __shfl_sync(FULL, (int)found, 0);
+    for (int o = 16; o > 0; o >>= 1) best = fminf(best, __shfl_xor_sync(FULL, best, o));
+    int pos = oldest ? -1 : n_live;
+    for (int k = lane; k < n_live; k += 32) {
+        int slot = order[k];
+        bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
+        if (base && w.t_flag[slot] && w.t_toi[slot] < 1.0f && w.t_toi[slot] == best) pos = oldest ? k : min(pos, k);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        int q = __shfl_xor_sync(FULL, pos, o);
+        pos = oldest ? max(pos, q) : min(pos, q);
+    }
+    const float done_alpha = 1.0f - 10.0f * EPS;
+    bool any = pos >= 0 && pos < n_live;
+    *min_slot = any ? order[pos] : 0;
+    *min_alpha = best;
+    return any && !(done_alpha < best);
 }
 
 // one TOI event (toi.py:604-716) with b2Island::SolveTOI (toi.py:719-799)
@@ -897,13 +1013,20 @@ __device__ void world_step(Ctx &x, float dt) {
 
 using namespace gb;
 
-// One warp per world; blockDim.x = 32 * worlds per block.
-extern "C" __global__ void __launch_bounds__(128) goib2d_step_kernel(const __grid_constant__ StepParams p) {
+// One warp per world; blockDim.x = 32 * worlds per block. GOIB2D_MIN_BLOCKS bounds the registers per thread so that
+// that many 128-thread blocks fit on an SM (65536 / (128 * blocks) registers).
+#ifndef GOIB2D_MIN_BLOCKS
+#define GOIB2D_MIN_BLOCKS 7
+#endif
+extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
+    goib2d_step_kernel(const __grid_constant__ StepParams p) {
     const int warp = threadIdx.x >> 5;
     const int64_t world = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
     if (world >= p.n_worlds) return;
-    Ctx x{p, p.m, p.s, {}, p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0, clock64()};
-    bind_world(x.w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
+    __shared__ W s_world[4];  // blockDim.x <= 128
+    if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
+    __syncwarp();
+    Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0, clock64()};
     for (int k = 0; k < p.n_steps; ++k) {
         if (p.actions && x.lane < p.n_action)  // action channels -> joint motor speeds
             x.w.motor_speed[p.action_joint[x.lane]] = p.action_scale[x.lane] * p.actions[world * p.n_action + x.lane];
