@@ -12,7 +12,9 @@
 
 #include "engine.cuh"
 
-extern "C" __global__ void goib2d_step_kernel(const __grid_constant__ gb::StepParams p);
+namespace gb {
+cudaError_t launch_steps(StepParams p, cudaStream_t stream);  // step.cu
+}
 
 namespace {
 
@@ -402,11 +404,8 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
         p.actions = actions, p.n_action = m->n_action, p.action_joint = m->action_joint;
         p.action_scale = m->action_scale;
     }
-    const int wpb = 4;  // worlds (warps) per block
-    int64_t blocks = (n_worlds + wpb - 1) / wpb;
-    if (blocks > 0x7fffffff) return fail(GOIB2D_ELIMIT, "too many worlds");
-    goib2d_step_kernel<<<(unsigned)blocks, 32 * wpb, 0, (cudaStream_t)stream>>>(p);
-    CUDA_TRY(cudaGetLastError());
+    if ((n_worlds + 3) / 4 > 0x7fffffff) return fail(GOIB2D_ELIMIT, "too many worlds");
+    CUDA_TRY(gb::launch_steps(p, (cudaStream_t)stream));
     return 0;
 }
 
@@ -497,10 +496,7 @@ int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int
         p.actions = actions, p.n_action = m->n_action, p.action_joint = m->action_joint;
         p.action_scale = m->action_scale;
     }
-    const int wpb = 4;
-    int64_t blocks = (n_worlds + wpb - 1) / wpb;
-    goib2d_step_kernel<<<(unsigned)blocks, 32 * wpb, 0, (cudaStream_t)stream>>>(p);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(gb::launch_steps(p, (cudaStream_t)stream));
     return 0;
 }
 

@@ -117,6 +117,7 @@ struct StepParams {
     int C, rows;
     int64_t n_worlds;
     int n_steps;
+    int step;  // index of the step a part kernel belongs to
     const float *actions;
     int n_action;
     const int32_t *action_joint;

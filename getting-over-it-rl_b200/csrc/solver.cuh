@@ -129,7 +129,7 @@ __device__ __forceinline__ V2 dvel(V2 vB, float wB, V2 rb, V2 vA, float wA, V2 r
 }
 
 // b2ContactSolver::SolveVelocityConstraints for one contact (contact_solver.py:194-279)
-__device__ __noinline__ void contact_solve_velocity(VCRow &c, const Bodies &bd) {
+__device__ __forceinline__ void contact_solve_velocity(VCRow &c, const Bodies &bd) {
     V2 vA{bd.vx[c.ia], bd.vy[c.ia]}, vB{bd.vx[c.ib], bd.vy[c.ib]};
     float wA = bd.vw[c.ia], wB = bd.vw[c.ib];
     const float mA = c.mA, mB = c.mB, iA = c.iA, iB = c.iB;
@@ -194,7 +194,7 @@ __device__ __noinline__ void contact_solve_velocity(VCRow &c, const Bodies &bd) 
 
 // b2ContactSolver::SolvePositionConstraints for one contact (contact_solver.py:307-354); masses passed so that
 // SolveTOI can zero those of the bodies that are not the TOI pair.
-__device__ __noinline__ float contact_solve_position(const VCRow &c, const Bodies &bd, float baumgarte, float slop,
+__device__ __forceinline__ float contact_solve_position(const VCRow &c, const Bodies &bd, float baumgarte, float slop,
                                                      float max_lin, float mA, float mB, float iA, float iB) {
     V2 cA{bd.cx[c.ia], bd.cy[c.ia]}, cB{bd.cx[c.ib], bd.cy[c.ib]};
     float aA = bd.ca[c.ia], aB = bd.ca[c.ib];
@@ -566,7 +566,7 @@ __device__ __forceinline__ void weld_velocity(JRow &r, V2 &vA, float &wA, V2 &vB
     }
 }
 
-__device__ __noinline__ void joint_solve_velocity(JRow &r, const Bodies &bd, bool v24) {  // joints.py:440-459
+__device__ __forceinline__ void joint_solve_velocity(JRow &r, const Bodies &bd, bool v24) {  // joints.py:440-459
     V2 vA{bd.vx[r.ia], bd.vy[r.ia]}, vB{bd.vx[r.ib], bd.vy[r.ib]};
     float wA = bd.vw[r.ia], wB = bd.vw[r.ib];
     if (r.type == REVOLUTE) {
@@ -604,7 +604,7 @@ __device__ __forceinline__ bool rev_point_position(const JRow &r, const Bodies &
     return pos_err <= s.linear_slop && ang_err <= s.angular_slop;
 }
 
-__device__ __noinline__ bool joint_solve_position(const JRow &r, const Bodies &bd, const goib2d_settings &s) {
+__device__ __forceinline__ bool joint_solve_position(const JRow &r, const Bodies &bd, const goib2d_settings &s) {
     V2 cA{bd.cx[r.ia], bd.cy[r.ia]}, cB{bd.cx[r.ib], bd.cy[r.ib]};
     float aA = bd.ca[r.ia], aB = bd.ca[r.ib];
     const float mA = r.mA, mB = r.mB, iA = r.iA, iB = r.iB;

@@ -1,4 +1,4 @@
-// goib2d: the batched b2World::Step kernel for sm_100a. One warp per world; K steps per launch.
+// goib2d: the batched b2World::Step for sm_100a. One warp per world; each step runs as four part kernels (step_part).
 //
 // Mapping. Each world's State is a row of every leaf (contiguous per world), so a warp reads and writes its own
 // world with unit-stride lane accesses. Data-parallel phases run one element per lane: the candidate-pair scan
@@ -8,6 +8,42 @@
 // exactly the reference's order (goi_jax/box2d/step.py, island.py, pairs.py, toi.py), so results are bit-identical
 // to it. Per-world working arrays live in a scratch arena (L1/L2-resident), laid out by scratch_layout().
 #include <cstdio>
+
+// Optional per-phase cycle counters for profiling builds (-DGOIB2D_PHASE_TIMERS): lane 0 of every warp adds the
+// clock64 cycles spent in each phase; goib2d_debug_phase_cycles() reads them. Compiled out otherwise.
+#ifdef GOIB2D_PHASE_TIMERS
+namespace gb {
+__device__ unsigned long long g_phase_cycles[16];
+#define GB_PHASE(x, i)                                                                       \
+    do {                                                                                     \
+        long long t1_ = clock64();                                                           \
+        if ((x).lane == 0) atomicAdd(&g_phase_cycles[i], (unsigned long long)(t1_ - (x).t0)); \
+        (x).t0 = t1_;                                                                        \
+    } while (0)
+// 0 events, 1 TOI position passes, 2 TOI solves, 3 searches, 4 max events, 5 TOI cycles, 6 outer iterations,
+// 7 push-backs, 8 root-finder steps, 9 GJK iterations, 10-13 TOI outcomes
+__device__ unsigned long long g_counts[16];
+// cycles in the TOI parts (0 sweep_xf, 1 GJK, 2 sep_init, 3 sep_find_min) and the island solver's calls (4 contact
+// velocity, 5 joint velocity, 6 contact position, 7 joint position; their counts at 8-11)
+__device__ unsigned long long g_toi_cycles[16];
+}  // namespace gb
+#define GB_COUNT(i, v) atomicAdd(&g_counts[i], (unsigned long long)(v))
+#define GB_TOI_T0() long long gb_t0_ = clock64()
+#define GB_TOI_T1(i) atomicAdd(&g_toi_cycles[i], (unsigned long long)(clock64() - gb_t0_))
+#else
+#define GB_PHASE(x, i) \
+    do {               \
+    } while (0)
+#define GB_COUNT(i, v) \
+    do {               \
+    } while (0)
+#define GB_TOI_T0() \
+    do {            \
+    } while (0)
+#define GB_TOI_T1(i) \
+    do {             \
+    } while (0)
+#endif
 
 #include "solver.cuh"
 #include "toi.cuh"
@@ -32,26 +68,6 @@ struct Ctx {
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
 };
 
-// Optional per-phase cycle counters for profiling builds (-DGOIB2D_PHASE_TIMERS): lane 0 of every warp adds the
-// clock64 cycles spent in each phase; goib2d_debug_phase_cycles() reads them. Compiled out otherwise.
-#ifdef GOIB2D_PHASE_TIMERS
-__device__ unsigned long long g_phase_cycles[16];
-#define GB_PHASE(x, i)                                                                       \
-    do {                                                                                     \
-        long long t1_ = clock64();                                                           \
-        if ((x).lane == 0) atomicAdd(&g_phase_cycles[i], (unsigned long long)(t1_ - (x).t0)); \
-        (x).t0 = t1_;                                                                        \
-    } while (0)
-__device__ unsigned long long g_counts[16];  // 0 events, 1 TOI position passes, 2 TOI solves, 3 searches, 4 max events
-#define GB_COUNT(i, v) atomicAdd(&g_counts[i], (unsigned long long)(v))
-#else
-#define GB_PHASE(x, i) \
-    do {               \
-    } while (0)
-#define GB_COUNT(i, v) \
-    do {               \
-    } while (0)
-#endif
 
 __device__ __forceinline__ void wake_body(W &w, int b) {  // b2Body::SetAwake(true)
     if (!w.awake[b]) {
@@ -521,9 +537,21 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
             for (int k = 0; k < isl.n_contacts; ++k) contact_warm_start(vc[k], bd);
         for (int k = 0; k < isl.n_joints; ++k) joint_warm_start(jr[k], bd, v24);
         for (int it = 0; it < s.velocity_iterations; ++it) {
-            for (int k = 0; k < isl.n_joints; ++k) joint_solve_velocity(jr[k], bd, v24);
-            for (int k = 0; k < isl.n_contacts; ++k) contact_solve_velocity(vc[k], bd);
+            for (int k = 0; k < isl.n_joints; ++k) {
+                GB_TOI_T0();
+                joint_solve_velocity(jr[k], bd, v24);
+                GB_TOI_T1(5);
+            }
+            for (int k = 0; k < isl.n_contacts; ++k) {
+                GB_TOI_T0();
+                contact_solve_velocity(vc[k], bd);
+                GB_TOI_T1(4);
+            }
         }
+#ifdef GOIB2D_PHASE_TIMERS
+        atomicAdd(&g_toi_cycles[8], (unsigned long long)isl.n_contacts * s.velocity_iterations);
+        atomicAdd(&g_toi_cycles[9], (unsigned long long)isl.n_joints * s.velocity_iterations);
+#endif
     }
     __syncwarp();
     GB_PHASE(x, 4);
@@ -638,7 +666,11 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
     for (int b = lane; b < B; b += 32) moved[b] = bisl[b] >= 0 && w.type[b] != STATIC;
     __syncwarp();
     GB_PHASE(x, 6);
-    synchronize_fixtures(x, moved, w.rows);
+}
+
+// the end of b2World::Solve: SynchronizeFixtures of the moved bodies, then FindNewContacts (step.py:185-194)
+__device__ void broadphase(Ctx &x) {
+    synchronize_fixtures(x, sp<int>(x.scr, x.p.lay.moved), x.w.rows);
     GB_PHASE(x, 7);
     find_new_contacts(x);
     GB_PHASE(x, 8);
@@ -986,27 +1018,61 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
 #endif
 }
 
-// b2World::Step (step.py:28-47)
-__device__ void world_step(Ctx &x, float dt) {
+// b2World::Step (step.py:28-47) in four parts, each a kernel of its own (the parts' code is large, and warps that
+// run the same part at the same time share the SM's instruction cache):
+//   0  the action channels, FindNewContacts for new fixtures, b2ContactManager::Collide
+//   1  islands and the island solver, sleep (b2World::Solve up to SynchronizeFixtures)
+//   2  SynchronizeFixtures and FindNewContacts
+//   3  SolveTOI, then the end of the step (inv_dt0, cleared forces; the status word after the last step)
+// Every value one part hands the next is in the State or the world's arena.
+template <int PART>
+__device__ __forceinline__ void step_part(const StepParams &p) {
+    const int warp = threadIdx.x >> 5;
+    const int64_t world = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    if (world >= p.n_worlds) return;
+    __shared__ W s_world[4];  // blockDim.x <= 128
+    if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
+    __syncwarp();
+    Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0, clock64()};
     W &w = x.w;
-    const goib2d_settings &s = x.s;
-    GB_PHASE(x, 11);
-    if (*w.new_fixture) find_new_contacts(x);
-    __syncwarp();
-    if (x.lane == 0) *w.new_fixture = 0;
-    const float inv_dt = dt > 0 ? 1.0f / dt : 0.0f;
-    const float dt_ratio = *w.inv_dt0 * dt;
-    __syncwarp();
-    GB_PHASE(x, 0);
-    collide(x);
-    GB_PHASE(x, 1);
-    solve(x, dt, dt_ratio);
-    if (s.continuous_physics) solve_toi(x, dt);
-    __syncwarp();
-    if (x.lane == 0 && dt > 0) *w.inv_dt0 = inv_dt;
-    if (s.auto_clear_forces)
-        for (int b = x.lane; b < w.B; b += 32) w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
-    __syncwarp();
+    const float dt = p.dt;
+    if (PART == 0) {
+        if (p.actions && x.lane < p.n_action)  // action channels -> joint motor speeds
+            w.motor_speed[p.action_joint[x.lane]] = p.action_scale[x.lane] * p.actions[world * p.n_action + x.lane];
+        __syncwarp();
+        GB_PHASE(x, 11);
+        if (*w.new_fixture) find_new_contacts(x);
+        __syncwarp();
+        if (x.lane == 0) *w.new_fixture = 0;
+        __syncwarp();
+        GB_PHASE(x, 0);
+        collide(x);
+        GB_PHASE(x, 1);
+    } else if (PART == 1) {
+        solve(x, dt, *w.inv_dt0 * dt);
+    } else if (PART == 2) {
+        broadphase(x);
+    } else {
+        if (x.s.continuous_physics) solve_toi(x, dt);
+        __syncwarp();
+        if (x.lane == 0 && dt > 0) *w.inv_dt0 = 1.0f / dt;
+        if (x.s.auto_clear_forces)
+            for (int b = x.lane; b < w.B; b += 32) w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
+        if (p.step == p.n_steps - 1) {
+            bool bad = false;  // non-finite body state
+            for (int b = x.lane; b < w.B; b += 32)
+                bad = bad || !isfinite(w.c[2 * b]) || !isfinite(w.c[2 * b + 1]) || !isfinite(w.a[b]) ||
+                      !isfinite(w.v[2 * b]) || !isfinite(w.v[2 * b + 1]) || !isfinite(w.w[b]);
+            if (__any_sync(FULL, bad)) x.status |= ST_NONFINITE;
+        }
+        __syncwarp();
+    }
+    if (x.lane == 0 && p.status) {
+        if (PART == 0 && p.step == 0)
+            p.status[world] = x.status;
+        else if (x.status)
+            p.status[world] |= x.status;
+    }
 }
 
 }  // namespace gb
@@ -1019,36 +1085,48 @@ using namespace gb;
 #define GOIB2D_MIN_BLOCKS 7
 #endif
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
-    goib2d_step_kernel(const __grid_constant__ StepParams p) {
-    const int warp = threadIdx.x >> 5;
-    const int64_t world = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
-    if (world >= p.n_worlds) return;
-    __shared__ W s_world[4];  // blockDim.x <= 128
-    if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
-    __syncwarp();
-    Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0, clock64()};
-    for (int k = 0; k < p.n_steps; ++k) {
-        if (p.actions && x.lane < p.n_action)  // action channels -> joint motor speeds
-            x.w.motor_speed[p.action_joint[x.lane]] = p.action_scale[x.lane] * p.actions[world * p.n_action + x.lane];
-        __syncwarp();
-        world_step(x, p.dt);
-    }
-    bool bad = false;  // non-finite body state
-    for (int b = x.lane; b < x.w.B; b += 32)
-        bad = bad || !isfinite(x.w.c[2 * b]) || !isfinite(x.w.c[2 * b + 1]) || !isfinite(x.w.a[b]) ||
-              !isfinite(x.w.v[2 * b]) || !isfinite(x.w.v[2 * b + 1]) || !isfinite(x.w.w[b]);
-    if (__any_sync(FULL, bad)) x.status |= ST_NONFINITE;
-    if (x.lane == 0 && p.status) p.status[world] = x.status;
+    goib2d_collide_kernel(const __grid_constant__ StepParams p) {
+    step_part<0>(p);
 }
+extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
+    goib2d_solve_kernel(const __grid_constant__ StepParams p) {
+    step_part<1>(p);
+}
+extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
+    goib2d_broadphase_kernel(const __grid_constant__ StepParams p) {
+    step_part<2>(p);
+}
+extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
+    goib2d_toi_kernel(const __grid_constant__ StepParams p) {
+    step_part<3>(p);
+}
+
+namespace gb {
+// p.n_steps steps of p.n_worlds worlds: the four part kernels per step, in order on one stream
+cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
+    const int wpb = 4;  // worlds (warps) per block
+    const unsigned blocks = (unsigned)((p.n_worlds + wpb - 1) / wpb);
+    for (int k = 0; k < p.n_steps; ++k) {
+        p.step = k;
+        goib2d_collide_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        goib2d_solve_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        goib2d_toi_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+    }
+    return cudaGetLastError();
+}
+}  // namespace gb
 
 #ifdef GOIB2D_PHASE_TIMERS
 extern "C" int goib2d_debug_phase_cycles(unsigned long long *out, int reset) {
     if (cudaMemcpyFromSymbol(out, g_phase_cycles, sizeof(g_phase_cycles)) != cudaSuccess) return -2;
     if (cudaMemcpyFromSymbol(out + 16, g_counts, sizeof(g_counts)) != cudaSuccess) return -2;
+    if (cudaMemcpyFromSymbol(out + 32, g_toi_cycles, sizeof(g_toi_cycles)) != cudaSuccess) return -2;
     if (reset) {
         unsigned long long z[16] = {0};
         cudaMemcpyToSymbol(g_phase_cycles, z, sizeof(z));
         cudaMemcpyToSymbol(g_counts, z, sizeof(z));
+        cudaMemcpyToSymbol(g_toi_cycles, z, sizeof(g_toi_cycles));
     }
     return 0;
 }

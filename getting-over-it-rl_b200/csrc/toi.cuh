@@ -4,6 +4,18 @@
 #pragma once
 #include "narrow.cuh"
 
+#ifndef GB_COUNT
+#define GB_COUNT(i, v) \
+    do {               \
+    } while (0)
+#define GB_TOI_T0() \
+    do {            \
+    } while (0)
+#define GB_TOI_T1(i) \
+    do {             \
+    } while (0)
+#endif
+
 namespace gb {
 
 enum { E_UNKNOWN = 0, E_FAILED = 1, E_OVERLAPPED = 2, E_TOUCHING = 3, E_SEPARATED = 4 };
@@ -62,30 +74,30 @@ __device__ __forceinline__ SV make_vertex(const Proxy &pA, Xf xfA, int iA, const
     v.a = 0.0f, v.iA = iA, v.iB = iB;
     return v;
 }
-__device__ __forceinline__ float simplex_metric(const SV *s, int count) {
-    if (count == 2) return length(sub(s[0].w, s[1].w));
-    if (count == 3) return cross(sub(s[1].w, s[0].w), sub(s[2].w, s[0].w));
+__device__ __forceinline__ float simplex_metric(const SV &s0, const SV &s1, const SV &s2, int count) {
+    if (count == 2) return length(sub(s0.w, s1.w));
+    if (count == 3) return cross(sub(s1.w, s0.w), sub(s2.w, s0.w));
     return 0.0f;
 }
 
-__device__ void gjk_solve2(SV *s, int &count) {  // toi.py:160-175
-    V2 w1 = s[0].w, w2 = s[1].w;
+__device__ __forceinline__ void gjk_solve2(SV &s0, SV &s1, int &count) {  // toi.py:160-175
+    V2 w1 = s0.w, w2 = s1.w;
     V2 e12 = sub(w2, w1);
     float d12_2 = -dot(w1, e12), d12_1 = dot(w2, e12);
     if (d12_2 <= 0) {
-        s[0].a = 1.0f, count = 1;
+        s0.a = 1.0f, count = 1;
         return;
     }
     if (d12_1 <= 0) {
-        s[1].a = 1.0f, s[0] = s[1], count = 1;
+        s1.a = 1.0f, s0 = s1, count = 1;
         return;
     }
     float inv = 1.0f / (d12_1 + d12_2);
-    s[0].a = d12_1 * inv, s[1].a = d12_2 * inv, count = 2;
+    s0.a = d12_1 * inv, s1.a = d12_2 * inv, count = 2;
 }
 
-__device__ void gjk_solve3(SV *s, int &count) {  // toi.py:178-227
-    V2 w1 = s[0].w, w2 = s[1].w, w3 = s[2].w;
+__device__ __forceinline__ void gjk_solve3(SV &s0, SV &s1, SV &s2, int &count) {  // toi.py:178-227
+    V2 w1 = s0.w, w2 = s1.w, w3 = s2.w;
     V2 e12 = sub(w2, w1);
     float d12_1 = dot(w2, e12), d12_2 = -dot(w1, e12);
     V2 e13 = sub(w3, w1);
@@ -95,81 +107,92 @@ __device__ void gjk_solve3(SV *s, int &count) {  // toi.py:178-227
     float n123 = cross(e12, e13);
     float d123_1 = n123 * cross(w2, w3), d123_2 = n123 * cross(w3, w1), d123_3 = n123 * cross(w1, w2);
     if (d12_2 <= 0 && d13_2 <= 0) {
-        s[0].a = 1.0f, count = 1;
+        s0.a = 1.0f, count = 1;
     } else if (d12_1 > 0 && d12_2 > 0 && d123_3 <= 0) {
         float inv = 1.0f / (d12_1 + d12_2);
-        s[0].a = d12_1 * inv, s[1].a = d12_2 * inv, count = 2;
+        s0.a = d12_1 * inv, s1.a = d12_2 * inv, count = 2;
     } else if (d13_1 > 0 && d13_2 > 0 && d123_2 <= 0) {
         float inv = 1.0f / (d13_1 + d13_2);
-        s[0].a = d13_1 * inv, s[2].a = d13_2 * inv, s[1] = s[2], count = 2;
+        s0.a = d13_1 * inv, s2.a = d13_2 * inv, s1 = s2, count = 2;
     } else if (d12_1 <= 0 && d23_2 <= 0) {
-        s[1].a = 1.0f, s[0] = s[1], count = 1;
+        s1.a = 1.0f, s0 = s1, count = 1;
     } else if (d13_1 <= 0 && d23_1 <= 0) {
-        s[2].a = 1.0f, s[0] = s[2], count = 1;
+        s2.a = 1.0f, s0 = s2, count = 1;
     } else if (d23_1 > 0 && d23_2 > 0 && d123_1 <= 0) {
         float inv = 1.0f / (d23_1 + d23_2);
-        s[1].a = d23_1 * inv, s[2].a = d23_2 * inv, s[0] = s[2], count = 2;
+        s1.a = d23_1 * inv, s2.a = d23_2 * inv, s0 = s2, count = 2;
     } else {
         float inv = 1.0f / ((d123_1 + d123_2) + d123_3);
-        s[0].a = d123_1 * inv, s[1].a = d123_2 * inv, s[2].a = d123_3 * inv, count = 3;
+        s0.a = d123_1 * inv, s1.a = d123_2 * inv, s2.a = d123_3 * inv, count = 3;
     }
 }
 
 // b2Distance, useRadii = false (toi.py:230-294)
+// The simplex lives in three named vertices (s0, s1, s2), not an indexed array, so that it stays in registers.
 __device__ __noinline__ float gjk_distance(Cache &cache, const Proxy &pA, Xf xfA, const Proxy &pB, Xf xfB) {
-    SV s[3];
-    for (int j = 0; j < 3; ++j) s[j] = SV{{0, 0}, {0, 0}, {0, 0}, 0.0f, 0, 0};
-    for (int j = 0; j < cache.count; ++j) s[j] = make_vertex(pA, xfA, cache.iA[j], pB, xfB, cache.iB[j]);
-    int count = cache.count;
-    float metric2 = simplex_metric(s, count);
+    const SV zero{{0, 0}, {0, 0}, {0, 0}, 0.0f, 0, 0};
+    SV s0 = zero, s1 = zero, s2 = zero;
+    const int cc = cache.count;
+    if (cc > 0) s0 = make_vertex(pA, xfA, cache.iA[0], pB, xfB, cache.iB[0]);
+    if (cc > 1) s1 = make_vertex(pA, xfA, cache.iA[1], pB, xfB, cache.iB[1]);
+    if (cc > 2) s2 = make_vertex(pA, xfA, cache.iA[2], pB, xfB, cache.iB[2]);
+    int count = cc;
+    float metric2 = simplex_metric(s0, s1, s2, count);
     if (count > 1 && (metric2 < 0.5f * cache.metric || 2.0f * cache.metric < metric2 || metric2 < EPS)) count = 0;
     if (count == 0) {
-        s[0] = make_vertex(pA, xfA, 0, pB, xfB, 0);
-        s[0].a = 1.0f;
+        s0 = make_vertex(pA, xfA, 0, pB, xfB, 0);
+        s0.a = 1.0f;
         count = 1;
     }
     for (int it = 0; it < 20;) {
-        int save_count = count, saveA[3], saveB[3];
-        for (int j = 0; j < 3; ++j) saveA[j] = s[j].iA, saveB[j] = s[j].iB;
+        const int save_count = count;
+        const int sa0 = s0.iA, sa1 = s1.iA, sa2 = s2.iA, sb0 = s0.iB, sb1 = s1.iB, sb2 = s2.iB;
         if (count == 2)
-            gjk_solve2(s, count);
+            gjk_solve2(s0, s1, count);
         else if (count == 3)
-            gjk_solve3(s, count);
+            gjk_solve3(s0, s1, s2, count);
         if (count == 3) break;
         V2 d;
         if (count == 1) {
-            d = neg(s[0].w);
+            d = neg(s0.w);
         } else {
-            V2 e12 = sub(s[1].w, s[0].w);
-            float sgn = cross(e12, neg(s[0].w));
+            V2 e12 = sub(s1.w, s0.w);
+            float sgn = cross(e12, neg(s0.w));
             d = sgn > 0 ? cross_sv(1.0f, e12) : cross_vs(e12, 1.0f);
         }
         if (dot(d, d) < EPS * EPS) break;
         int iA = pA.support(rot_t(xfA.q, neg(d)));
         int iB = pB.support(rot_t(xfB.q, d));
         SV v = make_vertex(pA, xfA, iA, pB, xfB, iB);
-        v.a = s[count].a;  // the tentative vertex's weight is not set
-        s[count] = v;
+        if (count == 1) {  // the new vertex goes to slot `count`; its weight is left as the slot had it
+            v.a = s1.a;
+            s1 = v;
+        } else {
+            v.a = s2.a;
+            s2 = v;
+        }
         ++it;
-        bool dup = false;
-        for (int j = 0; j < save_count; ++j) dup = dup || (saveA[j] == iA && saveB[j] == iB);
+        GB_COUNT(9, 1);
+        bool dup = (save_count > 0 && sa0 == iA && sb0 == iB) || (save_count > 1 && sa1 == iA && sb1 == iB) ||
+                   (save_count > 2 && sa2 == iA && sb2 == iB);
         if (dup) break;
         ++count;
     }
     V2 pa, pb;
     if (count == 1) {
-        pa = s[0].wA, pb = s[0].wB;
+        pa = s0.wA, pb = s0.wB;
     } else if (count == 2) {
-        pa = {s[0].a * s[0].wA.x + s[1].a * s[1].wA.x, s[0].a * s[0].wA.y + s[1].a * s[1].wA.y};
-        pb = {s[0].a * s[0].wB.x + s[1].a * s[1].wB.x, s[0].a * s[0].wB.y + s[1].a * s[1].wB.y};
+        pa = {s0.a * s0.wA.x + s1.a * s1.wA.x, s0.a * s0.wA.y + s1.a * s1.wA.y};
+        pb = {s0.a * s0.wB.x + s1.a * s1.wB.x, s0.a * s0.wB.y + s1.a * s1.wB.y};
     } else {
-        V2 p2{s[0].a * s[0].wA.x + s[1].a * s[1].wA.x, s[0].a * s[0].wA.y + s[1].a * s[1].wA.y};
-        pa = {p2.x + s[2].a * s[2].wA.x, p2.y + s[2].a * s[2].wA.y};
+        V2 p2{s0.a * s0.wA.x + s1.a * s1.wA.x, s0.a * s0.wA.y + s1.a * s1.wA.y};
+        pa = {p2.x + s2.a * s2.wA.x, p2.y + s2.a * s2.wA.y};
         pb = pa;
     }
     cache.count = count;
-    for (int j = 0; j < 3; ++j) cache.iA[j] = s[j].iA, cache.iB[j] = s[j].iB;
-    cache.metric = simplex_metric(s, count);
+    cache.iA[0] = s0.iA, cache.iA[1] = s1.iA, cache.iA[2] = s2.iA;
+    cache.iB[0] = s0.iB, cache.iB[1] = s1.iB, cache.iB[2] = s2.iB;
+    cache.metric = simplex_metric(s0, s1, s2, count);
     return length(sub(pa, pb));
 }
 
@@ -248,23 +271,54 @@ __device__ __noinline__ int time_of_impact(const Proxy &pA, Sweep swA, const Pro
     cache.count = 0, cache.metric = 0.0f;
     for (int j = 0; j < 3; ++j) cache.iA[j] = cache.iB[j] = 0;
     for (int iter = 0;;) {
-        Xf xfA = sweep_xf(swA, t1), xfB = sweep_xf(swB, t1);
-        float dist = gjk_distance(cache, pA, xfA, pB, xfB);
+        Xf xfA, xfB;
+        float dist;
+        {
+            GB_TOI_T0();
+            xfA = sweep_xf(swA, t1), xfB = sweep_xf(swB, t1);
+            GB_TOI_T1(0);
+        }
+        {
+            GB_TOI_T0();
+            dist = gjk_distance(cache, pA, xfA, pB, xfB);
+            GB_TOI_T1(1);
+        }
+        GB_COUNT(6, 1);
         if (dist <= 0.0f) {
             *t_out = 0.0f;
+            GB_COUNT(13, 1);
             return E_OVERLAPPED;
         }
         if (dist < target + tol) {
             *t_out = t1;
+            GB_COUNT(11, 1);
             return E_TOUCHING;
         }
-        SepFn f = sep_init(cache, pA, xfA, pB, xfB);
+        SepFn f;
+        {
+            GB_TOI_T0();
+            f = sep_init(cache, pA, xfA, pB, xfB);
+            GB_TOI_T1(2);
+        }
         float t2 = 1.0f;
         for (int push = 0;;) {
             int iA, iB;
-            float s2 = sep_find_min(f, pA, sweep_xf(swA, t2), pB, sweep_xf(swB, t2), iA, iB);
+            Xf xa2, xb2;
+            float s2;
+            {
+                GB_TOI_T0();
+                xa2 = sweep_xf(swA, t2), xb2 = sweep_xf(swB, t2);
+                GB_TOI_T1(0);
+            }
+            {
+                GB_TOI_T0();
+                s2 = sep_find_min(f, pA, xa2, pB, xb2, iA, iB);
+                GB_TOI_T1(3);
+            }
+            GB_COUNT(7, 1);
             if (s2 > target + tol) {
                 *t_out = 1.0f;
+                GB_COUNT(10, 1);
                 return E_SEPARATED;
             }
             if (s2 > target - tol) {
@@ -274,16 +328,19 @@ __device__ __noinline__ int time_of_impact(const Proxy &pA, Sweep swA, const Pro
             float s1 = sep_eval(f, pA, sweep_xf(swA, t1), iA, pB, sweep_xf(swB, t1), iB);
             if (s1 < target - tol) {
                 *t_out = t1;
+                GB_COUNT(12, 1);
                 return E_FAILED;
             }
             if (s1 <= target + tol) {
                 *t_out = t1;
+                GB_COUNT(11, 1);
                 return E_TOUCHING;
             }
             float a1 = t1, a2 = t2;
             for (int cnt = 0;;) {
                 float t = (cnt & 1) ? a1 + ((target - s1) * (a2 - a1)) / (s2 - s1) : 0.5f * (a1 + a2);
                 ++cnt;
+                GB_COUNT(8, 1);
                 float s = sep_eval(f, pA, sweep_xf(swA, t), iA, pB, sweep_xf(swB, t), iB);
                 if (babs(s - target) < tol) {
                     t2 = t;
@@ -301,6 +358,7 @@ __device__ __noinline__ int time_of_impact(const Proxy &pA, Sweep swA, const Pro
         ++iter;
         if (iter == 20) {
             *t_out = t1;
+            GB_COUNT(12, 1);
             return E_FAILED;
         }
     }
