@@ -74,10 +74,20 @@ GBD V2 solve22(float a11, float a12, float a21, float a22, float bx, float by) {
     float det = inv_or_zero(a11 * a22 - a12 * a21);
     return {det * (a22 * bx - a12 * by), det * (a11 * by - a21 * bx)};
 }
+// The same solves with the inverse determinant given: a constraint whose K stays fixed over the velocity iterations
+// computes it once (same operands, so the same float as the solves above compute on every call).
+GBD float det22_inv(float a11, float a12, float a21, float a22) { return inv_or_zero(a11 * a22 - a12 * a21); }
+GBD V2 solve22d(float a11, float a12, float a21, float a22, float bx, float by, float det) {
+    return {det * (a22 * bx - a12 * by), det * (a11 * by - a21 * bx)};
+}
 GBD V3 cross3(V3 a, V3 b) { return {a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x}; }
 GBD float dot3(V3 a, V3 b) { return (a.x * b.x + a.y * b.y) + a.z * b.z; }
 GBD V3 solve33(V3 ex, V3 ey, V3 ez, V3 b) {  // math2d.py:178-182
     float det = inv_or_zero(dot3(ex, cross3(ey, ez)));
+    return {det * dot3(b, cross3(ey, ez)), det * dot3(ex, cross3(b, ez)), det * dot3(ex, cross3(ey, b))};
+}
+GBD float det33_inv(V3 ex, V3 ey, V3 ez) { return inv_or_zero(dot3(ex, cross3(ey, ez))); }
+GBD V3 solve33d(V3 ex, V3 ey, V3 ez, V3 b, float det) {
     return {det * dot3(b, cross3(ey, ez)), det * dot3(ex, cross3(b, ez)), det * dot3(ex, cross3(ey, b))};
 }
 GBD void inverse22_of33(V3 ex, V3 ey, V3 &ox, V3 &oy, V3 &oz) {  // math2d.py:185-190
@@ -177,18 +187,45 @@ static __device__ __noinline__ Rot rot_of_ff(float x) {
     return {cs, x == 0 ? x : sn};
 }
 
-// The same values, fast: sin and cos in double precision rounded once to float, which is the correct rounding of
-// sin(x) / cos(x) unless the double lies within ROT_TOL (relative) of a midpoint between two floats; those
-// arguments, and |x| > ROT_FAST_MAX where the float-float reduction above drifts from the true value, take rot_of_ff.
-// Checked equal to rot_of_ff, bit for bit, on every float32 argument (rot_check.cu runs the sweep; without the cutoff
-// the first difference is at |x| = 2^24).
+// The same values, fast: sin and cos in double precision (sincos_short, below) rounded once to float, which is the
+// correct rounding of sin(x) / cos(x) unless the double lies within 2^-36 (relative) of a midpoint between two
+// floats; those arguments, and |x| > ROT_FAST_MAX, take rot_of_ff. Checked equal to rot_of_ff, bit for bit, on every
+// float32 argument (rot_check.cu runs the sweep; with CUDA's double sincos in place of sincos_short and no cutoff,
+// the first difference is at |x| = 2^24, where the float-float reduction drifts from the true value).
 constexpr float ROT_FAST_MAX = 0x1p+16f;
-constexpr double ROT_TOL = 0x1p-36;
-GBD bool rounds_clear(double d, float f) {  // d is farther than ROT_TOL * |d| from both midpoints around f
-    double fd = (double)f;
-    double up = 0.5 * (fd + (double)nextafterf(f, INFINITY)), dn = 0.5 * (fd + (double)nextafterf(f, -INFINITY));
-    double tol = fabs(d) * ROT_TOL;
-    return fabs(d - up) > tol && fabs(d - dn) > tol;
+// Rounding a normal double to float looks only at the 29 bits it drops: the double is |low29 - 2^28| of its own
+// ulps from the float midpoint that decides the rounding. ROT_CLEAR such ulps is 2^-36 of |d| at least.
+constexpr long long ROT_CLEAR = 1LL << 17;
+GBD bool rounds_clear(double d) {  // false also for doubles below the normal float range
+    long long b = __double_as_longlong(d);
+    long long low = b & 0x1FFFFFFFLL, dist = low - 0x10000000LL;
+    return ((b >> 52) & 0x7FF) > 1023 - 126 && (dist > ROT_CLEAR || dist < -ROT_CLEAR);
+}
+// sin and cos in double for |x| <= ROT_FAST_MAX, short latency: Cody-Waite reduction by pi/2 in two parts (PIO2_HI
+// has 35 significant bits, so k * PIO2_HI is exact for |k| < 2^17, and x - k * PIO2_HI is exact by Sterbenz), then
+// the Taylor series of sin to r^13 and of cos to r^14 on |r| <= pi/4, Horner in r^2 with fused multiply-adds.
+// Truncation below 2^-44 relative, reduction error below 2^-70: far inside the rounding test's 2^-36. The constants are pi/2 split
+// from a 78-digit Machin-formula value of pi, and 1/n!.
+GBD void sincos_short(double x, double &sn, double &cs) {
+    const double TWO_OVER_PI = 0x1.45f306dc9c883p-1, PIO2_HI = 0x1.921fb54440000p+0, PIO2_LO = 0x1.68c234c4c6629p-39;
+    double k = rint(x * TWO_OVER_PI);
+    double r = fma(-k, PIO2_LO, x - k * PIO2_HI);
+    double r2 = r * r;
+    double ps = fma(r2, 1.0 / 6227020800.0, -1.0 / 39916800.0);
+    ps = fma(r2, ps, 1.0 / 362880.0);
+    ps = fma(r2, ps, -1.0 / 5040.0);
+    ps = fma(r2, ps, 1.0 / 120.0);
+    ps = fma(r2, ps, -1.0 / 6.0);
+    double pc = fma(r2, -1.0 / 87178291200.0, 1.0 / 479001600.0);
+    pc = fma(r2, pc, -1.0 / 3628800.0);
+    pc = fma(r2, pc, 1.0 / 40320.0);
+    pc = fma(r2, pc, -1.0 / 720.0);
+    pc = fma(r2, pc, 1.0 / 24.0);
+    pc = fma(r2, pc, -0.5);
+    double s = fma(r * r2, ps, r), c = fma(r2, pc, 1.0);
+    int q = (int)k & 3;
+    sn = q == 0 ? s : q == 1 ? c : q == 2 ? -s : -c;
+    cs = q == 0 ? c : q == 1 ? -s : q == 2 ? -c : s;
 }
 GBD bool rot_fast(float x, Rot &q) {  // false: the argument needs rot_of_ff
     if (!(fabsf(x) <= ROT_FAST_MAX)) return false;
@@ -197,10 +234,10 @@ GBD bool rot_fast(float x, Rot &q) {  // false: the argument needs rot_of_ff
         return true;
     }
     double sd, cd;
-    sincos((double)x, &sd, &cd);
+    sincos_short((double)x, sd, cd);
     float s = __double2float_rn(sd), c = __double2float_rn(cd);
     q = {c, s};
-    return rounds_clear(sd, s) && rounds_clear(cd, c);
+    return rounds_clear(sd) && rounds_clear(cd);
 }
 static __device__ __noinline__ Rot rot_of(float x) {
     Rot q;

@@ -77,6 +77,7 @@ struct alignas(16) JRow {
     V2 lx, ly;
     float imp[5];
     float mimp;
+    float d33, d22;  // inverse determinants of K and of its upper-left 2x2 block (fixed over the velocity iterations)
 };
 
 // A narrow-phase result (collide.py:5-7).

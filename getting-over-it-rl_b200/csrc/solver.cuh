@@ -354,6 +354,8 @@ __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int ji
     } else {
         r.imp[0] = SC(ix), r.imp[1] = SC(iy), r.imp[2] = SC(iz), r.imp[3] = 0.0f, r.imp[4] = 0.0f;
     }
+    r.d33 = det33_inv(r.Kx, r.Ky, r.Kz);
+    r.d22 = det22_inv(r.Kx.x, r.Ky.x, r.Kx.y, r.Ky.y);
     r.mimp = SC(mimp);
 #undef SC
     r.inv_dt = dt > 0 ? 1.0f / dt : 0.0f;
@@ -423,11 +425,12 @@ __device__ __forceinline__ void rev_velocity(JRow &r, V2 &vA, float &wA, V2 &vB,
     bool lim = r.enable_limit && st != INACTIVE_LIMIT && !fixed;
     if (lim) {
         float c2 = wB - wA;
-        V3 sv = solve33(ex, ey, ez, V3{c1.x, c1.y, c2});
+        V3 sv = solve33d(ex, ey, ez, V3{c1.x, c1.y, c2}, r.d33);
         float jx = -sv.x, jy = -sv.y, jz = -sv.z;
         float new_z = iz + jz;
         bool redo = (st == AT_LOWER && new_z < 0) || (st == AT_UPPER && new_z > 0);
-        V2 rr = solve22(ex.x, ey.x, ex.y, ey.y, -c1.x + iz * ez.x, -c1.y + iz * ez.y);
+        V2 rr{0.0f, 0.0f};
+        if (redo) rr = solve22d(ex.x, ey.x, ex.y, ey.y, -c1.x + iz * ez.x, -c1.y + iz * ez.y, r.d22);
         float lx = redo ? rr.x : jx, ly = redo ? rr.y : jy, lz = redo ? -iz : jz;
         float nix = redo ? ix + rr.x : ix + jx, niy = redo ? iy + rr.y : iy + jy, niz = redo ? 0.0f : iz + jz;
         vA = {vA.x - mA * lx, vA.y - mA * ly};
@@ -436,7 +439,7 @@ __device__ __forceinline__ void rev_velocity(JRow &r, V2 &vA, float &wA, V2 &vB,
         wB = wB + iB * (cross(r.rB, V2{lx, ly}) + lz);
         r.imp[0] = nix, r.imp[1] = niy, r.imp[2] = niz;
     } else {
-        V2 p = solve22(ex.x, ey.x, ex.y, ey.y, -c1.x, -c1.y);
+        V2 p = solve22d(ex.x, ey.x, ex.y, ey.y, -c1.x, -c1.y, r.d22);
         vA = {vA.x - mA * p.x, vA.y - mA * p.y};
         wA = wA - iA * cross(r.rA, p);
         vB = {vB.x + mB * p.x, vB.y + mB * p.y};
@@ -474,7 +477,7 @@ __device__ __forceinline__ void rev24_velocity(JRow &r, V2 &vA, float &wA, V2 &v
         if (lim) wA = wA + iA * impulse, wB = wB - iB * impulse, r.imp[4] = nup;
     }
     V2 c1 = dvel(vB, wB, r.rB, vA, wA, r.rA);
-    V2 p = solve22(ex.x, ey.x, ex.y, ey.y, -c1.x, -c1.y);
+    V2 p = solve22d(ex.x, ey.x, ex.y, ey.y, -c1.x, -c1.y, r.d22);
     vA = {vA.x - mA * p.x, vA.y - mA * p.y};
     wA = wA - iA * cross(r.rA, p);
     vB = {vB.x + mB * p.x, vB.y + mB * p.y};
@@ -511,12 +514,12 @@ __device__ __forceinline__ void pri_velocity(JRow &r, V2 &vA, float &wA, V2 &vB,
     float Px, Py, LA, LB;
     if (lim) {
         float c2 = (dot(ax, sub(vB, vA)) + a2 * wB) - a1 * wA;
-        V3 df = solve33(ex, ey, ez, V3{-c1x, -c1y, -c2});
+        V3 df = solve33d(ex, ey, ez, V3{-c1x, -c1y, -c2}, r.d33);
         float nz_ = iz + df.z;
         nz_ = st == AT_LOWER ? bmax(nz_, 0.0f) : st == AT_UPPER ? bmin(nz_, 0.0f) : nz_;
         float bx = -c1x - (nz_ - iz) * ez.x;
         float by = -c1y - (nz_ - iz) * ez.y;
-        V2 f = solve22(ex.x, ey.x, ex.y, ey.y, bx, by);
+        V2 f = solve22d(ex.x, ey.x, ex.y, ey.y, bx, by, r.d22);
         float fx = f.x + ix, fy = f.y + iy;
         float dfx = fx - ix, dfy = fy - iy, dfz = nz_ - iz;
         Px = dfx * pe.x + dfz * ax.x;
@@ -525,7 +528,7 @@ __device__ __forceinline__ void pri_velocity(JRow &r, V2 &vA, float &wA, V2 &vB,
         LB = (dfx * s2 + dfy) + dfz * a2;
         r.imp[0] = fx, r.imp[1] = fy, r.imp[2] = nz_;
     } else {
-        V2 g = solve22(ex.x, ey.x, ex.y, ey.y, -c1x, -c1y);
+        V2 g = solve22d(ex.x, ey.x, ex.y, ey.y, -c1x, -c1y, r.d22);
         Px = g.x * pe.x, Py = g.x * pe.y;
         LA = g.x * s1 + g.y;
         LB = g.x * s2 + g.y;
