@@ -75,6 +75,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.rec = take(8 * c4);
     L.jr = take((int64_t)sizeof(gb::JRow) * (J > 0 ? J : 1));
     L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
+    L.isl = take(16);
     L.adj_start = take(4 * (int64_t)(B + 1)), L.adj_cur = take(b4), L.adj = take(2 * 8 * (int64_t)(C > 0 ? C : 1));
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves

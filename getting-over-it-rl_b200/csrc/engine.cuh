@@ -102,6 +102,7 @@ struct Layout {
     int64_t solved;  // [C]
     // [J]
     int64_t jr, jorder, jisl, jflag;
+    int64_t isl;  // [3] island counts: contacts, joints, islands
     // island graph: [B + 1] CSR start and [B] fill cursor over bodies, [2C] (contact slot, other body) pairs
     int64_t adj_start, adj_cur, adj;
     // [ceil(P/32)]

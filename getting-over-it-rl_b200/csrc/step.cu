@@ -1,4 +1,4 @@
-// goib2d: the batched b2World::Step for sm_100a. One warp per world; each step runs as four part kernels (step_part).
+// goib2d: the batched b2World::Step for sm_100a. One warp per world; each step runs as a sequence of part kernels.
 //
 // Mapping. Each world's State is a row of every leaf (contiguous per world), so a warp reads and writes its own
 // world with unit-stride lane accesses. Data-parallel phases run one element per lane: the candidate-pair scan
@@ -492,7 +492,7 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
     const DevModel &m = x.m;
     const goib2d_settings &s = x.s;
     W &w = x.w;
-    const int B = w.B, C = w.C, J = w.J, lane = x.lane;
+    const int B = w.B, lane = x.lane;
     const Layout &L = x.p.lay;
     IslandOut isl = find_islands(x);
     GB_PHASE(x, 2);
@@ -531,45 +531,64 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
     for (int k = lane; k < isl.n_joints; k += 32) prepare_joint(m, w, jorder[k], bd, s, dt, dt_ratio, warm, jr[k]);
     __syncwarp();
     GB_PHASE(x, 3);
-    const bool v24 = s.revolute_v24;
-    if (lane == 0) {
-        if (warm)
-            for (int k = 0; k < isl.n_contacts; ++k) contact_warm_start(vc[k], bd);
-        for (int k = 0; k < isl.n_joints; ++k) joint_warm_start(jr[k], bd, v24);
-        for (int it = 0; it < s.velocity_iterations; ++it) {
-            for (int k = 0; k < isl.n_joints; ++k) {
-                GB_TOI_T0();
-                joint_solve_velocity(jr[k], bd, v24);
-                GB_TOI_T1(5);
-            }
-            for (int k = 0; k < isl.n_contacts; ++k) {
-                GB_TOI_T0();
-                contact_solve_velocity(vc[k], bd);
-                GB_TOI_T1(4);
-            }
-        }
-#ifdef GOIB2D_PHASE_TIMERS
-        atomicAdd(&g_toi_cycles[8], (unsigned long long)isl.n_contacts * s.velocity_iterations);
-        atomicAdd(&g_toi_cycles[9], (unsigned long long)isl.n_joints * s.velocity_iterations);
-#endif
+    if (lane == 0) {  // the island counts, for the constraint sweeps (solve_constraints)
+        int *cnt = sp<int>(x.scr, L.isl);
+        cnt[0] = isl.n_contacts, cnt[1] = isl.n_joints, cnt[2] = isl.n_islands;
     }
     __syncwarp();
-    GB_PHASE(x, 4);
-    for (int k = lane; k < isl.n_contacts; k += 32) {  // StoreImpulses (contact_solver.py:293-304)
+    GB_PHASE(x, 3);
+}
+
+// The island constraint sweeps of one world (step.py:101-140, 197-251), run by ONE thread: warm start, the
+// velocity iterations, StoreImpulses, position integration and the position iterations with per-island early
+// exit. These loops are sequential within a world, so a warp runs 32 worlds' sweeps side by side (one per lane)
+// rather than one world's on a single lane. Reads the rows solve() prepared in the world's arena.
+__device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t world) {
+    const Layout &L = p.lay;
+    const goib2d_settings &s = p.s;
+    char *scr = p.scratch + world * L.stride;
+    const int B = p.m.B, C = p.C, J = p.m.J;
+    const int *cnt = sp<int>(scr, L.isl);
+    const int n_contacts = cnt[0], n_joints = cnt[1], n_islands = cnt[2];
+    int *bisl = sp<int>(scr, L.bisl), *cisl = sp<int>(scr, L.cisl), *jisl = sp<int>(scr, L.jisl);
+    int *done = sp<int>(scr, L.done), *jok = sp<int>(scr, L.jok);
+    float *minsep = sp<float>(scr, L.minsep);
+    VCRow *vc = sp<VCRow>(scr, L.vc);
+    JRow *jr = sp<JRow>(scr, L.jr);
+    const Bodies bd{sp<float>(scr, L.vx), sp<float>(scr, L.vy), sp<float>(scr, L.vw), sp<float>(scr, L.cx),
+                    sp<float>(scr, L.cy), sp<float>(scr, L.ca), sp<float>(scr, L.qc), sp<float>(scr, L.qs),
+                    sp<float>(scr, L.qa)};
+    const bool warm = s.warm_starting, v24 = s.revolute_v24;
+    if (warm)
+        for (int k = 0; k < n_contacts; ++k) contact_warm_start(vc[k], bd);
+    for (int k = 0; k < n_joints; ++k) joint_warm_start(jr[k], bd, v24);
+    for (int it = 0; it < s.velocity_iterations; ++it) {
+        for (int k = 0; k < n_joints; ++k) joint_solve_velocity(jr[k], bd, v24);
+        for (int k = 0; k < n_contacts; ++k) contact_solve_velocity(vc[k], bd);
+    }
+    float *normal_impulse = (float *)p.L.p[GOIB2D_C_NORMAL_IMPULSE] + world * 2 * C;
+    float *tangent_impulse = (float *)p.L.p[GOIB2D_C_TANGENT_IMPULSE] + world * 2 * C;
+    for (int k = 0; k < n_contacts; ++k) {  // StoreImpulses (contact_solver.py:293-304)
         const VCRow &c = vc[k];
         for (int j = 0; j < c.count; ++j)
-            w.normal_impulse[2 * c.slot + j] = c.ni[j], w.tangent_impulse[2 * c.slot + j] = c.ti[j];
+            normal_impulse[2 * c.slot + j] = c.ni[j], tangent_impulse[2 * c.slot + j] = c.ti[j];
     }
-    for (int k = lane; k < isl.n_joints; k += 32) {  // joints.py:609-622
+    float *lower_impulse = (float *)p.L.p[GOIB2D_J_LOWER_IMPULSE] + world * J;
+    float *upper_impulse = (float *)p.L.p[GOIB2D_J_UPPER_IMPULSE] + world * J;
+    float *impulse = (float *)p.L.p[GOIB2D_J_IMPULSE] + world * 3 * J;
+    float *motor_impulse = (float *)p.L.p[GOIB2D_J_MOTOR_IMPULSE] + world * J;
+    int32_t *limit_state = (int32_t *)p.L.p[GOIB2D_J_LIMIT_STATE] + world * J;
+    for (int k = 0; k < n_joints; ++k) {  // joints.py:609-622
         const JRow &r = jr[k];
-        if (v24) w.lower_impulse[r.jid] = r.imp[3], w.upper_impulse[r.jid] = r.imp[4];
-        for (int i = 0; i < 3; ++i) w.impulse[3 * r.jid + i] = r.imp[i];
-        w.motor_impulse[r.jid] = r.mimp;
-        w.limit_state[r.jid] = r.limit_state;
+        if (v24) lower_impulse[r.jid] = r.imp[3], upper_impulse[r.jid] = r.imp[4];
+        for (int i = 0; i < 3; ++i) impulse[3 * r.jid + i] = r.imp[i];
+        motor_impulse[r.jid] = r.mimp;
+        limit_state[r.jid] = r.limit_state;
     }
+    const float h = p.dt;
     const float max_t = s.clamps_per_second ? s.max_translation * h : s.max_translation;
     const float max_r = s.clamps_per_second ? s.max_rotation * h : s.max_rotation;
-    for (int b = lane; b < B; b += 32) {  // integrate positions (step.py:120-135)
+    for (int b = 0; b < B; ++b) {  // integrate positions (step.py:120-135)
         if (bisl[b] < 0) continue;
         float vx = bd.vx[b], vy = bd.vy[b], ww = bd.vw[b];
         float tx = h * vx, ty = h * vy;
@@ -582,35 +601,43 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
         bd.cx[b] = bd.cx[b] + h * vx, bd.cy[b] = bd.cy[b] + h * vy, bd.ca[b] = bd.ca[b] + h * ww;
         bd.vx[b] = vx, bd.vy[b] = vy, bd.vw[b] = ww;
     }
-    for (int i = lane; i < B; i += 32) done[i] = i >= isl.n_islands;
-    __syncwarp();
-    if (lane == 0) {  // position iterations with per-island early exit (step.py:197-251)
-        for (int it = 0; it < s.position_iterations; ++it) {
-            bool all = true;
-            for (int i = 0; i < isl.n_islands; ++i) all = all && done[i];
-            if (all) break;
-            for (int i = 0; i < isl.n_islands; ++i) minsep[i] = 0.0f, jok[i] = 1;
-            for (int k = 0; k < isl.n_contacts; ++k) {
-                const VCRow &c = vc[k];
-                int i = cisl[c.slot];
-                if (done[i]) continue;
-                float ms = contact_solve_position(c, bd, s.baumgarte, s.linear_slop, s.max_linear_correction, c.mA,
-                                                  c.mB, c.iA, c.iB);
-                minsep[i] = bmin(minsep[i], ms);
-            }
-            for (int k = 0; k < isl.n_joints; ++k) {
-                const JRow &r = jr[k];
-                int i = jisl[r.jid];
-                if (done[i]) continue;
-                bool ok = joint_solve_position(r, bd, s);
-                jok[i] = jok[i] && ok;
-            }
-            for (int i = 0; i < isl.n_islands; ++i)
-                if (minsep[i] >= -3.0f * s.linear_slop && jok[i]) done[i] = 1;
+    for (int i = 0; i < B; ++i) done[i] = i >= n_islands;
+    for (int it = 0; it < s.position_iterations; ++it) {  // per-island early exit (step.py:197-251)
+        bool all = true;
+        for (int i = 0; i < n_islands; ++i) all = all && done[i];
+        if (all) break;
+        for (int i = 0; i < n_islands; ++i) minsep[i] = 0.0f, jok[i] = 1;
+        for (int k = 0; k < n_contacts; ++k) {
+            const VCRow &c = vc[k];
+            int i = cisl[c.slot];
+            if (done[i]) continue;
+            float ms = contact_solve_position(c, bd, s.baumgarte, s.linear_slop, s.max_linear_correction, c.mA, c.mB,
+                                              c.iA, c.iB);
+            minsep[i] = bmin(minsep[i], ms);
         }
+        for (int k = 0; k < n_joints; ++k) {
+            const JRow &r = jr[k];
+            int i = jisl[r.jid];
+            if (done[i]) continue;
+            bool ok = joint_solve_position(r, bd, s);
+            jok[i] = jok[i] && ok;
+        }
+        for (int i = 0; i < n_islands; ++i)
+            if (minsep[i] >= -3.0f * s.linear_slop && jok[i]) done[i] = 1;
     }
-    __syncwarp();
-    GB_PHASE(x, 5);
+}
+
+// b2World::Solve after the sweeps (step.py:141-194): write back, sleep, the moved bodies
+__device__ void solve_finish(Ctx &x, float dt) {
+    const DevModel &m = x.m;
+    const goib2d_settings &s = x.s;
+    W &w = x.w;
+    const int B = w.B, C = w.C, J = w.J, lane = x.lane;
+    const Layout &L = x.p.lay;
+    const float h = dt;
+    int *bisl = sp<int>(x.scr, L.bisl), *cisl = sp<int>(x.scr, L.cisl), *jisl = sp<int>(x.scr, L.jisl);
+    int *done = sp<int>(x.scr, L.done), *moved = sp<int>(x.scr, L.moved);
+    Bodies bd = bodies_of(x);
     for (int b = lane; b < B; b += 32) {  // write back + SynchronizeTransform (step.py:141-151)
         if (bisl[b] < 0) continue;
         w.c[2 * b] = bd.cx[b], w.c[2 * b + 1] = bd.cy[b], w.a[b] = bd.ca[b];
@@ -811,6 +838,9 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     VCRow *vc = sp<VCRow>(x.scr, L.vc);
     Bodies bd = bodies_of(x);
     const int A = m.fixture_body[w.fa[min_slot]], Bb = m.fixture_body[w.fb[min_slot]];
+#ifdef GOIB2D_PHASE_TIMERS
+    long long ev_t0 = clock64();
+#endif
     for (int b = lane; b < B; b += 32) {  // every body advanced to min_alpha, and its transform there
         float *d = adv + 8 * b;
         d[0] = w.c0[2 * b], d[1] = w.c0[2 * b + 1], d[2] = w.a0[b], d[3] = w.t_alpha0[b];
@@ -897,6 +927,10 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         __syncwarp();
         return;
     }
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[12], (unsigned long long)(clock64() - ev_t0));
+    ev_t0 = clock64();
+#endif
     // b2Island::SolveTOI: position passes moving only the TOI pair, then velocity passes, then integration
     for (int b = lane; b < B; b += 32) {
         bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
@@ -967,6 +1001,10 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         }
     }
     __syncwarp();
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[13], (unsigned long long)(clock64() - ev_t0));
+    ev_t0 = clock64();
+#endif
     synchronize_fixtures(x, moved, w.rows);
     for (int s_ = lane; s_ < C; s_ += 32) {
         if (moved[m.fixture_body[w.fa[s_]]] || moved[m.fixture_body[w.fb[s_]]]) w.t_flag[s_] = 0;  // every slot
@@ -980,6 +1018,9 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     }
     if (lane == 0) *w.t_events += 1;
     __syncwarp();
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[14], (unsigned long long)(clock64() - ev_t0));
+#endif
 }
 
 __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
@@ -1018,12 +1059,15 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
 #endif
 }
 
-// b2World::Step (step.py:28-47) in four parts, each a kernel of its own (the parts' code is large, and warps that
-// run the same part at the same time share the SM's instruction cache):
+// b2World::Step (step.py:28-47) in parts, each a kernel of its own (the parts' code is large, and warps that run
+// the same part at the same time share the SM's instruction cache). One warp per world:
 //   0  the action channels, FindNewContacts for new fixtures, b2ContactManager::Collide
-//   1  islands and the island solver, sleep (b2World::Solve up to SynchronizeFixtures)
-//   2  SynchronizeFixtures and FindNewContacts
-//   3  SolveTOI, then the end of the step (inv_dt0, cleared forces; the status word after the last step)
+//   1  b2World::Solve up to SynchronizeFixtures: islands, velocity integration, the constraint rows (solve), the
+//      constraint sweeps on lane 0 (solve_constraints), write back and sleep (solve_finish)
+//   2, 3  the same as 1 without the sweeps, before and after them (solve; solve_finish): for large batches the
+//      sweeps run between the two one world per thread (goib2d_constraints_kernel)
+//   4  SynchronizeFixtures and FindNewContacts
+//   5  SolveTOI, then the end of the step (inv_dt0, cleared forces; the status word after the last step)
 // Every value one part hands the next is in the State or the world's arena.
 template <int PART>
 __device__ __forceinline__ void step_part(const StepParams &p) {
@@ -1048,9 +1092,17 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
         GB_PHASE(x, 0);
         collide(x);
         GB_PHASE(x, 1);
-    } else if (PART == 1) {
+    } else if (PART == 1) {  // the whole of b2World::Solve, the sweeps on lane 0
         solve(x, dt, *w.inv_dt0 * dt);
+        if (x.lane == 0) solve_constraints(p, world);
+        __syncwarp();
+        GB_PHASE(x, 5);
+        solve_finish(x, dt);
     } else if (PART == 2) {
+        solve(x, dt, *w.inv_dt0 * dt);
+    } else if (PART == 3) {
+        solve_finish(x, dt);
+    } else if (PART == 4) {
         broadphase(x);
     } else {
         if (x.s.continuous_physics) solve_toi(x, dt);
@@ -1093,23 +1145,46 @@ extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     step_part<1>(p);
 }
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
-    goib2d_broadphase_kernel(const __grid_constant__ StepParams p) {
+    goib2d_solve_rows_kernel(const __grid_constant__ StepParams p) {
     step_part<2>(p);
+}
+// one world per THREAD (solve_constraints)
+extern "C" __global__ void __launch_bounds__(32) goib2d_constraints_kernel(const __grid_constant__ StepParams p) {
+    const int64_t world = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (world < p.n_worlds) solve_constraints(p, world);
+}
+extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
+    goib2d_finish_kernel(const __grid_constant__ StepParams p) {
+    step_part<3>(p);
+}
+extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
+    goib2d_broadphase_kernel(const __grid_constant__ StepParams p) {
+    step_part<4>(p);
 }
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_toi_kernel(const __grid_constant__ StepParams p) {
-    step_part<3>(p);
+    step_part<5>(p);
 }
 
 namespace gb {
-// p.n_steps steps of p.n_worlds worlds: the four part kernels per step, in order on one stream
+// From this many worlds the constraint sweeps run one world per thread: 32 worlds' sweeps share a warp's issue
+// slots, which pays once the batch fills the SMs with warps of sweeps; below it a warp per world keeps more warps in
+// flight per SM. (Both run the same code, in the same order within a world.)
+constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = 16384;
+// p.n_steps steps of p.n_worlds worlds: the part kernels per step, in order on one stream
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     const int wpb = 4;  // worlds (warps) per block
     const unsigned blocks = (unsigned)((p.n_worlds + wpb - 1) / wpb);
     for (int k = 0; k < p.n_steps; ++k) {
         p.step = k;
         goib2d_collide_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
-        goib2d_solve_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        if (p.n_worlds < THREAD_SWEEPS_MIN_WORLDS) {
+            goib2d_solve_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        } else {
+            goib2d_solve_rows_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+            goib2d_constraints_kernel<<<(unsigned)((p.n_worlds + 31) / 32), 32, 0, stream>>>(p);
+            goib2d_finish_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        }
         goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         goib2d_toi_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
     }

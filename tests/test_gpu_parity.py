@@ -79,6 +79,25 @@ def test_gpu_matches_oracle_on_workloads(api, cfg, n, steps):
     assert ((eng.status() & 0b1011) == 0).all()  # no overflow, no non-finite state, no table limit
 
 
+@pytest.mark.parametrize("cfg,steps", [("c1", 12), ("c4", 6)])
+def test_large_batches_match_oracle(api, cfg, steps):
+    """A batch large enough that the constraint sweeps run one world per thread (16384 worlds and up) equals the
+    oracle on worlds taken from both ends of the batch."""
+    from goib2d import configs
+    from goib2d.world import map_state
+    n = 16384
+    sc, model, host = configs.batch(cfg, n)
+    dev = api.to_device(host)
+    eng = api.engine_for(model, host.bodies.type.shape[1])
+    eng.step_(dev, sc.settings, configs.DT, n_steps=steps)
+    got = api.to_host(dev)
+    pick = np.r_[0:96, n - 96:n]
+    want = oracle_lib.step(model, map_state(lambda x: np.ascontiguousarray(np.asarray(x)[pick]), host), sc.settings,
+                           configs.DT, steps, threads=8)
+    assert_states_equal(map_state(lambda x: np.asarray(x)[pick], got), want, f"{cfg} n={n}")
+    assert ((eng.status() & 0b1011) == 0).all()
+
+
 def test_actions_drive_joint_motors(api):
     """The action channels set joints.motor_speed before each step, as the oracle does."""
     from goib2d import configs
