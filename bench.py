@@ -155,7 +155,7 @@ def main():
         return
     import torch
     import torch.distributed as dist
-    from goib2d import api, configs, shard
+    from goib2d import api, configs, native, shard
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world_size > 1:
@@ -253,10 +253,15 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-                         "algorithmic_bytes_per_world_step": bytes_ws},
+                         "algorithmic_bytes_per_world_step": bytes_ws,
+                         "kernel": "one step's launch group (goib2d_collide_kernel, goib2d_solve_kernel, "
+                                   "goib2d_toi_kernel), timed as one unit by the per-step CUDA events",
+                         "traffic_source": f"profiles/traffic_{args.config}.json (ncu dram bytes of the launch group)"
+                                           if traffic is not None else None},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": n * na * 4 * world_size,
                     "d2h_bytes_per_step": n * 2 * 4 * world_size, "steps": Ke},
-            "gpu_launches": K, "clocks": clk, "wall_s_timed": wall, "nonfinite_worlds": nonfinite,
+            "gpu_launches": K * native.load().goib2d_kernels_per_step(n), "clocks": clk, "wall_s_timed": wall,
+            "nonfinite_worlds": nonfinite,
             "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     eng.close()

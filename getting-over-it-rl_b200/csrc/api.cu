@@ -14,6 +14,7 @@
 
 namespace gb {
 cudaError_t launch_steps(StepParams p, cudaStream_t stream);  // step.cu
+int kernels_per_step(int64_t n_worlds);                       // step.cu
 }
 
 namespace {
@@ -203,6 +204,8 @@ struct goib2d_model {
 extern "C" {
 
 int goib2d_version(void) { return GOIB2D_ABI_VERSION; }
+
+int goib2d_kernels_per_step(int64_t n_worlds) { return gb::kernels_per_step(n_worlds); }
 
 const char *goib2d_last_error(void) { return g_err.c_str(); }
 

@@ -119,7 +119,9 @@ struct StepParams {
     int C, rows;
     int64_t n_worlds;
     int n_steps;
-    int step;  // index of the step a part kernel belongs to
+    int step;        // index of the step a part kernel belongs to
+    int64_t world0;  // a part kernel's launch covers worlds world0 .. world_end - 1
+    int64_t world_end;
     const float *actions;
     int n_action;
     const int32_t *action_joint;

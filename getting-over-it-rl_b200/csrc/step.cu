@@ -1062,18 +1062,17 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
 // b2World::Step (step.py:28-47) in parts, each a kernel of its own (the parts' code is large, and warps that run
 // the same part at the same time share the SM's instruction cache). One warp per world:
 //   0  the action channels, FindNewContacts for new fixtures, b2ContactManager::Collide
-//   1  b2World::Solve up to SynchronizeFixtures: islands, velocity integration, the constraint rows (solve), the
-//      constraint sweeps on lane 0 (solve_constraints), write back and sleep (solve_finish)
-//   2, 3  the same as 1 without the sweeps, before and after them (solve; solve_finish): for large batches the
-//      sweeps run between the two one world per thread (goib2d_constraints_kernel)
-//   4  SynchronizeFixtures and FindNewContacts
+//   1  b2World::Solve: islands, velocity integration, the constraint rows (solve), the constraint sweeps on lane 0
+//      (solve_constraints), write back and sleep (solve_finish), SynchronizeFixtures and FindNewContacts
+//   2, 3, 4  part 1 in pieces for large batches: solve; solve_finish; SynchronizeFixtures and FindNewContacts, with
+//      the sweeps between the first two run one world per thread (goib2d_constraints_kernel)
 //   5  SolveTOI, then the end of the step (inv_dt0, cleared forces; the status word after the last step)
 // Every value one part hands the next is in the State or the world's arena.
 template <int PART>
 __device__ __forceinline__ void step_part(const StepParams &p) {
     const int warp = threadIdx.x >> 5;
-    const int64_t world = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
-    if (world >= p.n_worlds) return;
+    const int64_t world = p.world0 + (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    if (world >= p.world_end) return;
     __shared__ W s_world[4];  // blockDim.x <= 128
     if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
@@ -1098,6 +1097,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
         __syncwarp();
         GB_PHASE(x, 5);
         solve_finish(x, dt);
+        broadphase(x);
     } else if (PART == 2) {
         solve(x, dt, *w.inv_dt0 * dt);
     } else if (PART == 3) {
@@ -1150,8 +1150,8 @@ extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
 }
 // one world per THREAD (solve_constraints)
 extern "C" __global__ void __launch_bounds__(32) goib2d_constraints_kernel(const __grid_constant__ StepParams p) {
-    const int64_t world = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (world < p.n_worlds) solve_constraints(p, world);
+    const int64_t world = p.world0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (world < p.world_end) solve_constraints(p, world);
 }
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_finish_kernel(const __grid_constant__ StepParams p) {
@@ -1171,21 +1171,26 @@ namespace gb {
 // slots, which pays once the batch fills the SMs with warps of sweeps; below it a warp per world keeps more warps in
 // flight per SM. (Both run the same code, in the same order within a world.)
 constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = 16384;
-// p.n_steps steps of p.n_worlds worlds: the part kernels per step, in order on one stream
+// p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: per step the collide part, the solve
+// part (the fused kernel, or for large batches rows / thread sweeps / finish and the broadphase part), the TOI part
+int kernels_per_step(int64_t n_worlds) { return n_worlds < THREAD_SWEEPS_MIN_WORLDS ? 3 : 6; }
+
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     const int wpb = 4;  // worlds (warps) per block
-    const unsigned blocks = (unsigned)((p.n_worlds + wpb - 1) / wpb);
+    p.world0 = 0, p.world_end = p.n_worlds;
+    const int64_t n = p.n_worlds;
+    const unsigned blocks = (unsigned)((n + wpb - 1) / wpb);
     for (int k = 0; k < p.n_steps; ++k) {
         p.step = k;
         goib2d_collide_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
-        if (p.n_worlds < THREAD_SWEEPS_MIN_WORLDS) {
+        if (n < THREAD_SWEEPS_MIN_WORLDS) {
             goib2d_solve_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         } else {
             goib2d_solve_rows_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
-            goib2d_constraints_kernel<<<(unsigned)((p.n_worlds + 31) / 32), 32, 0, stream>>>(p);
+            goib2d_constraints_kernel<<<(unsigned)((n + 31) / 32), 32, 0, stream>>>(p);
             goib2d_finish_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+            goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         }
-        goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         goib2d_toi_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
     }
     return cudaGetLastError();

@@ -49,6 +49,8 @@ class Engine:
         self.handle = h
         self.device = torch.cuda.current_device()
         self.n_action = 0
+        self._bound = None     # (State, its first leaf's address, checked pointer table): see _bind
+        self._settings = None  # (Settings, its C struct)
         if len(action_joints):
             self.set_action_map(action_joints, action_scale)
 
@@ -59,8 +61,13 @@ class Engine:
                                                           s.ctypes.data_as(native._f)))
         self.n_action = len(j)
 
-    def step_(self, state, settings, dt, n_steps=1, actions=None, stream=None):
-        """Step every world of a batched device State n_steps times, in place; returns the State."""
+    def _bind(self, state):
+        """The checked leaf pointer table of a device State, cached for the last State object stepped (a State is
+        immutable, so the same object has the same leaves; the first leaf's address guards against storage
+        changes)."""
+        c = self._bound
+        if c is not None and c[0] is state and c[1] == state.bodies.type.data_ptr():
+            return c[2]
         leaves = state_leaves(state)
         first = leaves[0]
         if not (isinstance(first, torch.Tensor) and first.is_cuda):
@@ -69,13 +76,20 @@ class Engine:
         if state.bodies.type.shape[1] != self.n_bodies or state.joints.motor_speed.shape[1] != len(self.model.joint_type):
             raise ValueError(f"State has {state.bodies.type.shape[1]} bodies / {state.joints.motor_speed.shape[1]} joints,"
                              f" the Model {self.n_bodies} / {len(self.model.joint_type)}")
-        C_ = state.contacts.pair.shape[1]
-        rows = state.fixtures.friction.shape[1]
         for t in leaves:
             if not t.is_contiguous() or t.device != first.device:
                 raise ValueError("State leaves must be contiguous tensors on one device")
-        ptrs = (C.c_void_p * len(leaves))(*[t.data_ptr() for t in leaves])
-        ss = settings_struct(settings)
+        bound = (n, state.contacts.pair.shape[1], state.fixtures.friction.shape[1], first.device,
+                 (C.c_void_p * len(leaves))(*[t.data_ptr() for t in leaves]))
+        self._bound = (state, state.bodies.type.data_ptr(), bound)
+        return bound
+
+    def step_(self, state, settings, dt, n_steps=1, actions=None, stream=None):
+        """Step every world of a batched device State n_steps times, in place; returns the State."""
+        n, C_, rows, device, ptrs = self._bind(state)
+        if self._settings is None or self._settings[0] is not settings:
+            self._settings = (settings, settings_struct(settings))
+        ss = self._settings[1]
         act = None
         if actions is not None:
             if not (isinstance(actions, torch.Tensor) and actions.is_cuda and actions.dtype == torch.float32):
@@ -84,7 +98,7 @@ class Engine:
                 raise ValueError(f"actions must be contiguous ({n}, {self.n_action})")
             act = actions.data_ptr()
         if stream is None:
-            stream = torch.cuda.current_stream(first.device).cuda_stream
+            stream = torch.cuda.current_stream(device).cuda_stream
         native.check(self.lib.goib2d_step(self.handle, C.addressof(ss), C.c_float(float(dt)), C_, rows, n,
                                           int(n_steps), ptrs, act, stream))
         return state

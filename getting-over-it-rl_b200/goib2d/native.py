@@ -147,6 +147,7 @@ def load():
         "goib2d_status_copy": (C.c_int, [vp, _i, C.c_int64]),
         "goib2d_step_noalloc": (C.c_int, [vp, vp, C.c_float, C.c_int32, C.c_int32, C.c_int64, C.c_int32,
                                           C.POINTER(vp), vp, vp]),
+        "goib2d_kernels_per_step": (C.c_int, [C.c_int64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

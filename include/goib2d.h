@@ -132,6 +132,11 @@ int goib2d_status(goib2d_model *model, const int32_t **device_status, int64_t *n
 /* The same status words copied to host memory (n <= the last step's n_worlds); synchronises the device. */
 int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
 
+/* Kernel launches one goib2d_step step makes for a batch of n_worlds worlds: 3, or 6 for batches of 16384 worlds
+ * and more (their constraint sweeps run one world per thread). For launch accounting and profilers; no counterpart
+ * in the reference engine. */
+int goib2d_kernels_per_step(int64_t n_worlds);
+
 /* Bytes of the static scratch arena used by goib2d_step_noalloc (on every device that loads the library). */
 #define GOIB2D_NOALLOC_SCRATCH_BYTES (32u << 20)
 
