@@ -235,15 +235,22 @@ int goib2d_model_create(const goib2d_model_desc *d, goib2d_model **out) {
     for (int f = 0; f < F; ++f) {
         if (d->fixture_body[f] < 0 || d->fixture_body[f] >= B) return fail(GOIB2D_EINVAL, "fixture %d body", f);
         if (d->count[f] < 1 || d->count[f] > gb::MAXV) return fail(GOIB2D_EINVAL, "fixture %d vertex count", f);
-        if (d->shape_type[f] != gb::CIRCLE && d->shape_type[f] != gb::POLYGON)
-            return fail(GOIB2D_EINVAL, "fixture %d shape type %d (circle and polygon only)", f, d->shape_type[f]);
+        if (d->shape_type[f] != gb::CIRCLE && d->shape_type[f] != gb::POLYGON && d->shape_type[f] != gb::EDGE)
+            return fail(GOIB2D_EINVAL, "fixture %d shape type %d (circle, edge or polygon)", f, d->shape_type[f]);
+        if (d->shape_type[f] == gb::EDGE && d->count[f] != 2)
+            return fail(GOIB2D_EINVAL, "edge fixture %d has vertex count %d (2)", f, d->count[f]);
     }
     for (int j = 0; j < J; ++j)
         if (d->joint_a[j] < 0 || d->joint_a[j] >= B || d->joint_b[j] < 0 || d->joint_b[j] >= B)
             return fail(GOIB2D_EINVAL, "joint %d bodies", j);
-    for (int p = 0; p < P; ++p)
+    for (int p = 0; p < P; ++p) {
         if (d->pair_a[p] < 0 || d->pair_a[p] >= F || d->pair_b[p] < 0 || d->pair_b[p] >= F)
             return fail(GOIB2D_EINVAL, "pair %d fixtures", p);
+        if (d->shape_type[d->pair_b[p]] == gb::EDGE ||
+            (d->shape_type[d->pair_a[p]] == gb::CIRCLE && d->shape_type[d->pair_b[p]] == gb::POLYGON))
+            return fail(GOIB2D_EINVAL, "pair %d: an edge pair lists the edge first, a polygon-circle pair the polygon "
+                        "(and two edges never collide)", p);
+    }
     auto *m = new goib2d_model();
     int rc = 0;
     cudaGetDevice(&m->device);
@@ -276,6 +283,7 @@ int goib2d_model_create(const goib2d_model_desc *d, goib2d_model **out) {
     UP(reference_angle, J);
     UP(pair_a, P);
     UP(pair_b, P);
+    UP(edge_ghost, F);  // zeros when NULL
 #undef UP
     if (!rc) {  // each body's joints, highest index first, with the body at the other end (the island walk's order)
         std::vector<int32_t> jstart(B + 1, 0), jadj(2 * (size_t)(2 * J > 0 ? 2 * J : 1));

@@ -19,7 +19,7 @@ enum { STATIC = 0, KINEMATIC = 1, DYNAMIC = 2 };
 enum { REVOLUTE = 1, PRISMATIC = 2, WELD = 8 };
 enum { INACTIVE_LIMIT = 0, AT_LOWER = 1, AT_UPPER = 2, EQUAL_LIMITS = 3 };
 enum { CIRCLES = 0, FACE_A = 1, FACE_B = 2 };
-enum { CIRCLE = 0, POLYGON = 2 };
+enum { CIRCLE = 0, EDGE = 1, POLYGON = 2 };
 
 struct V2 {
     float x, y;

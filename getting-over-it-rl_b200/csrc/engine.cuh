@@ -17,6 +17,7 @@ struct DevModel {
     const float *local_anchor_a, *local_anchor_b, *local_axis_a, *local_yaxis_a, *reference_angle;
     const int32_t *pair_a, *pair_b;
     const int32_t *fixture_slot;  // [F] row of each fixture (identity for the full layout), -1 static
+    const int32_t *edge_ghost;    // [F] ghost-vertex flags of edge fixtures (0 elsewhere)
     const float *static_fat, *static_friction, *static_restitution;
     const int32_t *row_fixture;   // [F] fixture of each State.fixtures row (valid for rows < n_rows)
     int any_toi_body;             // some body is bullet or continuous at build

@@ -272,14 +272,223 @@ __device__ void collide_circles(const Poly &pa, Xf xfa, const Poly &pb, Xf xfb, 
     out.id[0] = out.id[1] = 0;
 }
 
-// b2Contact::Evaluate dispatch (collide.py:189-207)
-__device__ __noinline__ void evaluate(const DevModel &m, int fa, int fb, Xf xfa, Xf xfb, float slop, Man &out) {
+// ---------------------------------------------------------------- edges (no counterpart in the reference engine)
+// Box2D 2.3.1's method for edge shapes, in this engine's own code: a segment v1-v2 of an edge fixture, with the
+// optional ghost vertices v0 (before v1) and v3 (after v2) of a chain. The ghost vertices decide which side of a
+// shared chain vertex owns a contact, so that a shape sliding along a chain is not caught by its inner vertices.
+struct Edge {
+    V2 v0, v1, v2, v3;
+    bool has0, has3;
+    float radius;
+};
+__device__ __forceinline__ Edge edge_of(const DevModel &m, int f) {
+    const float *v = m.verts + 16 * f;
+    int g = m.edge_ghost[f];
+    return {{v[4], v[5]}, {v[0], v[1]}, {v[2], v[3]}, {v[6], v[7]}, (g & 1) != 0, (g & 2) != 0, m.radius[f]};
+}
+
+__device__ __forceinline__ void man_empty(Man &out, int mtype) {
+    out.mtype = mtype, out.count = 0;
+    out.ln = out.lp = out.pt[0] = out.pt[1] = V2{0.0f, 0.0f};
+    out.id[0] = out.id[1] = 0;
+}
+
+// b2CollideEdgeAndCircle: the circle centre's Voronoi region of the segment (vertex v1, vertex v2 or the face); a
+// vertex region owned by the neighbouring edge (the centre lies beyond the shared vertex along that edge) gives no
+// contact here.
+__device__ void collide_edge_circle(const Edge &e, Xf xfa, const Poly &cb, Xf xfb, Man &out) {
+    V2 q = xf_mul_t(xfa, xf_mul(xfb, cb.vert(0)));  // the centre in the edge's frame
+    V2 a = e.v1, b = e.v2, ab = sub(b, a);
+    float u = dot(ab, sub(b, q)), v = dot(ab, sub(q, a));
+    float radius = e.radius + cb.radius;
+    man_empty(out, CIRCLES);
+    out.pt[0] = out.pt[1] = cb.vert(0);
+    if (v <= 0.0f) {  // vertex v1
+        V2 d = sub(q, a);
+        if (dot(d, d) > radius * radius) return;
+        if (e.has0 && dot(sub(a, e.v0), sub(a, q)) > 0.0f) return;
+        out.count = 1, out.lp = a, out.id[0] = feature_key(0, 0, E_VERTEX, E_VERTEX);
+        return;
+    }
+    if (u <= 0.0f) {  // vertex v2
+        V2 d = sub(q, b);
+        if (dot(d, d) > radius * radius) return;
+        if (e.has3 && dot(sub(e.v3, b), sub(q, b)) > 0.0f) return;
+        out.count = 1, out.lp = b, out.id[0] = feature_key(1, 0, E_VERTEX, E_VERTEX);
+        return;
+    }
+    float inv = 1.0f / dot(ab, ab);
+    V2 p{inv * (u * a.x + v * b.x), inv * (u * a.y + v * b.y)};  // the closest point of the face
+    V2 d = sub(q, p);
+    if (dot(d, d) > radius * radius) return;
+    V2 n{-ab.y, ab.x};
+    if (dot(n, sub(q, a)) < 0.0f) n = neg(n);
+    out.mtype = FACE_A, out.count = 1, out.ln = normalize(n), out.lp = a;
+    out.id[0] = feature_key(0, 0, E_FACE, E_VERTEX);
+}
+
+// The polygon's area centroid (b2PolygonShape::m_centroid), fan of triangles from the origin.
+__device__ __forceinline__ V2 poly_centroid(const Poly &p) {
+    float area = 0.0f, cx = 0.0f, cy = 0.0f;
+    const float third = 1.0f / 3.0f;
+    for (int i = 0; i < p.count; ++i) {
+        V2 p2 = p.vert(i), p3 = p.vert(i + 1 < p.count ? i + 1 : 0);
+        float tri = 0.5f * cross(p2, p3);
+        area = area + tri;
+        cx = cx + tri * third * (p2.x + p3.x);
+        cy = cy + tri * third * (p2.y + p3.y);
+    }
+    float inv = 1.0f / area;
+    return {cx * inv, cy * inv};
+}
+
+// Which side of the edge the polygon is on (front) and the range of contact normals the edge admits there: a
+// normal must lie between `lower` and `upper`. With a ghost vertex, the range reaches the neighbouring edge's
+// normal across a convex vertex and stops at this edge's across a concave one; without, the free end turns the
+// range all the way round to the opposite side.
+struct EdgeRange {
+    bool front;
+    V2 normal, lower, upper;
+};
+__device__ EdgeRange edge_range(const Edge &e, V2 c) {
+    V2 e1 = normalize(sub(e.v2, e.v1));
+    V2 n1{e1.y, -e1.x};
+    float o1 = dot(n1, sub(c, e.v1));
+    V2 n0{0.0f, 0.0f}, n2{0.0f, 0.0f};
+    float o0 = 0.0f, o2 = 0.0f;
+    bool cv1 = false, cv2 = false;
+    if (e.has0) {
+        V2 e0 = normalize(sub(e.v1, e.v0));
+        n0 = {e0.y, -e0.x}, cv1 = cross(e0, e1) >= 0.0f, o0 = dot(n0, sub(c, e.v0));
+    }
+    if (e.has3) {
+        V2 e2 = normalize(sub(e.v3, e.v2));
+        n2 = {e2.y, -e2.x}, cv2 = cross(e1, e2) > 0.0f, o2 = dot(n2, sub(c, e.v2));
+    }
+    const V2 m1 = neg(n1);
+    EdgeRange r;
+    if (e.has0 && e.has3) {
+        if (cv1 && cv2) {
+            r.front = o0 >= 0.0f || o1 >= 0.0f || o2 >= 0.0f;
+            r.lower = r.front ? n0 : m1, r.upper = r.front ? n2 : m1;
+        } else if (cv1) {
+            r.front = o0 >= 0.0f || (o1 >= 0.0f && o2 >= 0.0f);
+            r.lower = r.front ? n0 : neg(n2), r.upper = r.front ? n1 : m1;
+        } else if (cv2) {
+            r.front = o2 >= 0.0f || (o0 >= 0.0f && o1 >= 0.0f);
+            r.lower = r.front ? n1 : m1, r.upper = r.front ? n2 : neg(n0);
+        } else {
+            r.front = o0 >= 0.0f && o1 >= 0.0f && o2 >= 0.0f;
+            r.lower = r.front ? n1 : neg(n2), r.upper = r.front ? n1 : neg(n0);
+        }
+    } else if (e.has0) {
+        if (cv1) {
+            r.front = o0 >= 0.0f || o1 >= 0.0f;
+            r.lower = r.front ? n0 : n1, r.upper = m1;
+        } else {
+            r.front = o0 >= 0.0f && o1 >= 0.0f;
+            r.lower = n1, r.upper = r.front ? m1 : neg(n0);
+        }
+    } else if (e.has3) {
+        if (cv2) {
+            r.front = o1 >= 0.0f || o2 >= 0.0f;
+            r.lower = m1, r.upper = r.front ? n2 : n1;
+        } else {
+            r.front = o1 >= 0.0f && o2 >= 0.0f;
+            r.lower = r.front ? m1 : neg(n2), r.upper = n1;
+        }
+    } else {
+        r.front = o1 >= 0.0f;
+        r.lower = r.front ? m1 : n1, r.upper = r.front ? m1 : n1;
+    }
+    r.normal = r.front ? n1 : m1;
+    return r;
+}
+
+// b2CollideEdgeAndPolygon: the polygon in the edge's frame; the edge's own axis against the polygon's face axes
+// restricted to the admissible normal range (angular_slop of slack), the polygon axis preferred only when clearly
+// deeper (0.98 x the edge separation + 0.001); the incident feature clipped to the reference face's side planes.
+__device__ void collide_edge_polygon(const Edge &e, Xf xfa, const Poly &pb, Xf xfb, float angular_slop, Man &out) {
+    const Rot q{xfa.q.c * xfb.q.c + xfa.q.s * xfb.q.s, xfa.q.c * xfb.q.s - xfa.q.s * xfb.q.c};
+    const Xf xf{rot_t(xfa.q, sub(xfb.p, xfa.p)), q};  // polygon frame -> edge frame
+    const int n = pb.count;
+    auto PV = [&](int i) { return xf_mul(xf, pb.vert(i)); };
+    auto PN = [&](int i) { return rot(xf.q, pb.norm(i)); };
+    man_empty(out, FACE_A);
+    const EdgeRange rg = edge_range(e, xf_mul(xf, poly_centroid(pb)));
+    const float radius = e.radius + pb.radius;
+    float sep_e = MAXF;  // the edge's axis
+    for (int i = 0; i < n; ++i) sep_e = bmin(sep_e, dot(rg.normal, sub(PV(i), e.v1)));
+    if (sep_e > radius) return;
+    int pidx = -1;  // the polygon's axes
+    float psep = -MAXF;
+    const V2 perp{-rg.normal.y, rg.normal.x};
+    for (int i = 0; i < n; ++i) {
+        V2 nn = neg(PN(i)), v = PV(i);
+        float s = bmin(dot(nn, sub(v, e.v1)), dot(nn, sub(v, e.v2)));
+        if (s > radius) {  // a separating axis
+            pidx = i, psep = s;
+            break;
+        }
+        V2 lim = dot(nn, perp) >= 0.0f ? rg.upper : rg.lower;
+        if (dot(sub(nn, lim), rg.normal) < -angular_slop) continue;
+        if (s > psep) pidx = i, psep = s;
+    }
+    if (pidx >= 0 && psep > radius) return;
+    const bool on_b = pidx >= 0 && psep > 0.98f * sep_e + 0.001f;
+    ClipV ie[2];
+    int r1, r2;
+    V2 rv1, rv2, rn;
+    if (!on_b) {  // the edge is the reference face; the polygon edge most anti-parallel to it is incident
+        int best = 0;
+        float bv = dot(rg.normal, PN(0));
+        for (int i = 1; i < n; ++i) {
+            float val = dot(rg.normal, PN(i));
+            if (val < bv) bv = val, best = i;
+        }
+        int i2 = best + 1 < n ? best + 1 : 0;
+        ie[0] = {PV(best), 0, best, E_FACE, E_VERTEX};
+        ie[1] = {PV(i2), 0, i2, E_FACE, E_VERTEX};
+        r1 = rg.front ? 0 : 1, r2 = rg.front ? 1 : 0;
+        rv1 = rg.front ? e.v1 : e.v2, rv2 = rg.front ? e.v2 : e.v1;
+        rn = rg.normal;  // n1 in front, -n1 behind
+    } else {  // a polygon face is the reference; the segment is incident
+        ie[0] = {e.v1, 0, pidx, E_VERTEX, E_FACE};
+        ie[1] = {e.v2, 0, pidx, E_VERTEX, E_FACE};
+        r1 = pidx, r2 = pidx + 1 < n ? pidx + 1 : 0;
+        rv1 = PV(r1), rv2 = PV(r2), rn = PN(r1);
+    }
+    const V2 sn1{rn.y, -rn.x}, sn2 = neg(sn1);
+    ClipV c1[2], c2[2];
+    if (clip2(ie, sn1, dot(sn1, rv1), r1, c1) < 2) return;
+    if (clip2(c1, sn2, dot(sn2, rv2), r2, c2) < 2) return;
+    out.mtype = on_b ? FACE_B : FACE_A;
+    out.ln = on_b ? pb.norm(r1) : rn;
+    out.lp = on_b ? pb.vert(r1) : rv1;
+    int count = 0;
+    for (int k = 0; k < 2; ++k) {
+        const ClipV &c = c2[k];
+        if (dot(rn, sub(c.v, rv1)) > radius) continue;
+        out.pt[count] = on_b ? c.v : xf_mul_t(xf, c.v);
+        out.id[count] = on_b ? feature_key(c.ib, c.ia, c.tb, c.ta) : feature_key(c.ia, c.ib, c.ta, c.tb);
+        ++count;
+    }
+    out.count = count;
+}
+
+// b2Contact::Evaluate dispatch (collide.py:189-207; edge pairs put the edge first, as b2Contact::Create does)
+__device__ __noinline__ void evaluate(const DevModel &m, int fa, int fb, Xf xfa, Xf xfb, float slop, float angular_slop,
+                                      Man &out) {
     Poly pa = poly_of(m, fa), pb = poly_of(m, fb);
     int ta = m.shape_type[fa], tb = m.shape_type[fb];
     if (ta == POLYGON && tb == POLYGON)
         collide_polygons(pa, xfa, pb, xfb, slop, out);
     else if (ta == POLYGON && tb == CIRCLE)
         collide_polygon_circle(pa, xfa, pb, xfb, out);
+    else if (ta == EDGE && tb == CIRCLE)
+        collide_edge_circle(edge_of(m, fa), xfa, pb, xfb, out);
+    else if (ta == EDGE && tb == POLYGON)
+        collide_edge_polygon(edge_of(m, fa), xfa, pb, xfb, angular_slop, out);
     else
         collide_circles(pa, xfa, pb, xfb, out);
 }

@@ -265,7 +265,7 @@ __device__ void collide(Ctx &x) {
         if (w.pair[s] < 0) continue;
         int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
         over[s] = overlap(fixture_fat(m, w, w.fa[s]), fixture_fat(m, w, w.fb[s]));
-        evaluate(m, w.fa[s], w.fb[s], w.bxf(ba), w.bxf(bb), x.s.linear_slop, man[s]);
+        evaluate(m, w.fa[s], w.fb[s], w.bxf(ba), w.bxf(bb), x.s.linear_slop, x.s.angular_slop, man[s]);
     }
     for (int b = lane; b < B; b += 32) aw[b] = w.awake[b];
     __syncwarp();
@@ -857,7 +857,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         if (ba != A && bb != A && ba != Bb && bb != Bb) continue;
         const float *da = adv + 8 * ba, *db = adv + 8 * bb;
         evaluate(m, w.fa[s_], w.fb[s_], Xf{{da[4], da[5]}, {da[6], da[7]}}, Xf{{db[4], db[5]}, {db[6], db[7]}},
-                 s.linear_slop, man[s_]);
+                 s.linear_slop, s.angular_slop, man[s_]);
     }
     __syncwarp();
     int n_isl = 0;

@@ -81,6 +81,8 @@ class Scene:
     n_worlds: int
     static_polys: list = field(default_factory=list)  # (verts (k,2), friction)
     static_boxes: list = field(default_factory=list)  # (half (2,), centre (2,), angle, friction)
+    static_chains: list = field(default_factory=list)  # (vertices (k,2), friction): open chains of edges
+    static_edges: list = field(default_factory=list)  # ((v1, v2), friction): lone edges, no ghost vertices
     level_calls: list = field(default_factory=list)  # extra builder calls for the level (anchors)
     dyn: dict = field(default_factory=dict)  # per-world arrays, first axis = world
     builder: object = None  # fn(defn, scene, i) adding the dynamic part of world i
@@ -95,6 +97,10 @@ class Scene:
             defn.add_polygon(g, verts, friction=fr)
         for half, ctr, ang, fr in self.static_boxes:
             defn.add_box(g, tuple(half), tuple(ctr), ang, friction=fr)
+        for verts, fr in self.static_chains:
+            defn.add_chain(g, verts, friction=fr)
+        for (v1, v2), fr in self.static_edges:
+            defn.add_edge(g, v1, v2, friction=fr)
         self.builder(defn, self, i)
         return defn
 
@@ -122,12 +128,21 @@ def _c0_bodies(defn, sc, i):
         defn.add_box(b, (0.25, 0.25), friction=0.6)
 
 
-def c0(seed=0, n=256):
+def _terrain_chain(heights, x0, dx):
+    return np.array([(x0 + i * dx, heights[i]) for i in range(len(heights))], F32)
+
+
+def c0(seed=0, n=256, terrain="quads"):
+    """terrain "quads": the polygon-terrain variant (static quads down to a floor, parity pinned to the reference);
+    "chain": BASELINE's own level, one chain of edges (this engine's edge shapes; no reference to pin)."""
     rng = np.random.default_rng(seed)
     h = rng.uniform(-0.5, 0.5, 128).astype(F32)
     x0, dx = -32.0, 0.5
-    sc = Scene("c0_box_drop", _settings(False), 64, 600, n)
-    sc.static_polys = _terrain_quads(h, x0, dx, -2.0, 0.6)
+    sc = Scene("c0_box_drop" if terrain == "quads" else "c0_box_drop_chain", _settings(False), 64, 600, n)
+    if terrain == "quads":
+        sc.static_polys = _terrain_quads(h, x0, dx, -2.0, 0.6)
+    else:
+        sc.static_chains = [(_terrain_chain(h, x0, dx), 0.6)]
     sc.dyn = _per_world(seed, n, lambda r: dict(x=r.uniform(x0 + 1, x0 + 127 * dx - 1, 8).astype(F32),
                                                y=r.uniform(2, 6, 8).astype(F32),
                                                angle=r.uniform(0, 2 * np.pi, 8).astype(F32)))
@@ -163,12 +178,12 @@ def _c1_bodies(defn, sc, i):
     _rig(defn, sc, i, float(d["x"][i]), float(d["y"][i]), float(d["angle"][i]))
 
 
-def _level_c1(rng, friction=0.7):
+def _level_c1(rng, friction=0.7, terrain="quads"):
     steps = rng.normal(0, 0.15, 2000)
     h = np.concatenate([[0.0], np.cumsum(steps)]).astype(F32)
     x0, dx = -250.0, 0.25
     floor = float(h.min()) - 1.0
-    polys = _terrain_quads(h, x0, dx, floor, friction)
+    polys = _terrain_quads(h, x0, dx, floor, friction) if terrain == "quads" else []
     rocks = []
     for _ in range(60):
         k = int(rng.integers(3, 9))
@@ -194,11 +209,15 @@ def _rig_start(h, x0, dx, rocks, r):
     return dict(x=F32(x), y=F32(y), angle=F32(ang), w0=F32(r.uniform(-2, 2)))
 
 
-def c1(seed=0, n=4096):
+def c1(seed=0, n=4096, terrain="quads"):
+    """terrain "quads": the polygon-terrain variant; "chain": BASELINE's 2000-segment edge chain (own edge shapes,
+    no reference to pin). The same level, rocks and rig starts either way."""
     rng = np.random.default_rng(seed)
-    h, x0, dx, polys, rocks = _level_c1(rng)
-    sc = Scene("c1_rig", _settings(True), 48, 1000, n)
+    h, x0, dx, polys, rocks = _level_c1(rng, terrain=terrain)
+    sc = Scene("c1_rig" if terrain == "quads" else "c1_rig_chain", _settings(True), 48, 1000, n)
     sc.static_polys = polys
+    if terrain != "quads":
+        sc.static_chains = [(_terrain_chain(h, x0, dx), 0.7)]
     sc.dyn = _per_world(seed, n, lambda r: _rig_start(h, x0, dx, rocks, r))
     sc.builder = _c1_bodies
     sc.level = (h, x0, dx)
@@ -278,17 +297,23 @@ def _c3_bodies(defn, sc, i):
         defn.add_circle(b, 0.05, friction=0.2)
 
 
-def c3(seed=0, n=8192):
+def c3(seed=0, n=8192, terrain="quads"):
+    """terrain "quads": the 64 zero-thickness targets as 0.02 m boxes; "chain": as edge shapes (own, unpinned)."""
     rng = np.random.default_rng(seed)
-    sc = Scene("c3_toi", _settings(True), 256, 300, n)
+    sc = Scene("c3_toi" if terrain == "quads" else "c3_toi_edges", _settings(True), 256, 300, n)
     boxes = [((10.0, 0.01), (0.0, -10.0), 0.0, 0.3), ((10.0, 0.01), (0.0, 10.0), 0.0, 0.3),
              ((0.01, 10.0), (-10.0, 0.0), 0.0, 0.3), ((0.01, 10.0), (10.0, 0.0), 0.0, 0.3)]
     for _ in range(12):
         boxes.append(((float(rng.uniform(0.5, 2.0)), 0.01), (float(rng.uniform(-8, 8)), float(rng.uniform(-8, 8))),
                       float(rng.uniform(0, np.pi)), 0.3))
-    for _ in range(64):  # zero-thickness edges as 0.02 m thick boxes
-        boxes.append(((float(rng.uniform(0.25, 1.5)), 0.01), (float(rng.uniform(-9, 9)), float(rng.uniform(-9, 9))),
-                      float(rng.uniform(0, np.pi)), 0.3))
+    for _ in range(64):  # zero-thickness edges: 0.02 m thick boxes, or edge shapes
+        half, cx, cy = float(rng.uniform(0.25, 1.5)), float(rng.uniform(-9, 9)), float(rng.uniform(-9, 9))
+        ang = float(rng.uniform(0, np.pi))
+        if terrain == "quads":
+            boxes.append(((half, 0.01), (cx, cy), ang, 0.3))
+        else:
+            ca, sa = math.cos(ang) * half, math.sin(ang) * half
+            sc.static_edges.append((((cx - ca, cy - sa), (cx + ca, cy + sa)), 0.3))
     sc.static_boxes = boxes
     def draw(r):
         speed, th = r.uniform(50, 200, 32), r.uniform(0, 2 * np.pi, 32)
@@ -318,9 +343,9 @@ def _c4_bodies(defn, sc, i):
         prev = link
 
 
-def c4(seed=0, n=65536):
-    sc = c1(seed, n)
-    sc.name, sc.capacity, sc.steps = "c4_scale", 64, 10000
+def c4(seed=0, n=65536, terrain="quads"):
+    sc = c1(seed, n, terrain)
+    sc.name, sc.capacity, sc.steps = "c4_scale" if terrain == "quads" else "c4_scale_chain", 64, 10000
     sc.builder = _c4_bodies
     h, x0, dx = sc.level
     ix = int((20.0 - x0) / dx)
@@ -332,6 +357,19 @@ _FIRST = [0]
 
 DEFAULT_N = {"c0": 256, "c1": 4096, "c2": 1024, "c3": 8192, "c4": 65536}
 CONFIGS = {"c0": c0, "c1": c1, "c2": c2, "c3": c3, "c4": c4}
+# BASELINE's own levels with edge shapes (chains, lone edges): this engine's edge colliders, parity unpinned
+
+
+def _edge_variant(base):
+    def fn(seed=0, n=None):
+        return CONFIGS[base](seed, DEFAULT_N[base] if n is None else n, "chain")
+    return fn
+
+
+for _k in ("c0", "c1", "c3", "c4"):
+    CONFIGS[_k + "e"] = _edge_variant(_k)
+    DEFAULT_N[_k + "e"] = DEFAULT_N[_k]
+del _k
 
 
 def scene(name, seed=0, n=None, first=0):
@@ -357,7 +395,7 @@ def batch(name, n, seed=0, compact=True, first=0):
     sc = scene(name, seed, n, first)
     full = sc.world_def(0)
     model, st0 = full.build(sc.capacity)
-    n_static = len(sc.static_polys) + len(sc.static_boxes)
+    n_static = sum(1 for f in full.fixtures if f["body"] == 0)  # the level: fixtures of the ground body
     geom = full.fixture_geometry()
     per = []
     for i in range(n):

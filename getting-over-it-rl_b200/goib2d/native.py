@@ -25,7 +25,7 @@ class ModelDesc(C.Structure):
                 ("normals", _f), ("joint_type", _i), ("joint_a", _i), ("joint_b", _i), ("local_anchor_a", _f),
                 ("local_anchor_b", _f), ("local_axis_a", _f), ("local_yaxis_a", _f), ("reference_angle", _f),
                 ("pair_a", _i), ("pair_b", _i), ("toi_bodies", _u), ("fixture_slot", _i), ("static_fat", _f),
-                ("static_friction", _f), ("static_restitution", _f)]
+                ("static_friction", _f), ("static_restitution", _f), ("edge_ghost", _i)]
 
 
 _MODEL_FIELDS = (("fixture_body", np.int32, _i), ("shape_type", np.int32, _i), ("count", np.int32, _i),
@@ -35,7 +35,8 @@ _MODEL_FIELDS = (("fixture_body", np.int32, _i), ("shape_type", np.int32, _i), (
                  ("local_axis_a", np.float32, _f), ("local_yaxis_a", np.float32, _f),
                  ("reference_angle", np.float32, _f), ("pair_a", np.int32, _i), ("pair_b", np.int32, _i),
                  ("toi_bodies", np.uint8, _u), ("fixture_slot", np.int32, _i), ("static_fat", np.float32, _f),
-                 ("static_friction", np.float32, _f), ("static_restitution", np.float32, _f))
+                 ("static_friction", np.float32, _f), ("static_restitution", np.float32, _f),
+                 ("edge_ghost", np.int32, _i))
 
 
 class PackedModel:

@@ -11,7 +11,8 @@ import numpy as np
 from .settings import AABB_EXTENSION, AABB_MULTIPLIER, EPSILON, MAX_POLYGON_VERTICES
 
 F32 = np.float32
-CIRCLE, POLYGON = 0, 2  # b2Shape::Type; edge (1) and chain (3) are not in the reference engine
+CIRCLE, EDGE, POLYGON = 0, 1, 2  # b2Shape::Type. Edges are this engine's own addition (the reference engine has
+# neither edges nor chains); a chain is built as a run of edge fixtures with ghost vertices (WorldDef.add_chain).
 
 
 def host_sin_cos(a):
@@ -160,5 +161,5 @@ def fatten(lx, ly, ux, uy):
     return (lx - e).astype(F32), (ly - e).astype(F32), (ux + e).astype(F32), (uy + e).astype(F32)
 
 
-__all__ = ["CIRCLE", "POLYGON", "AABB_MULTIPLIER", "box", "polygon_set", "polygon_raw", "pad", "fixture_aabbs",
+__all__ = ["CIRCLE", "EDGE", "POLYGON", "AABB_MULTIPLIER", "box", "polygon_set", "polygon_raw", "pad", "fixture_aabbs",
            "fatten", "host_sin_cos", "normalize", "edge_normals"]

@@ -55,6 +55,8 @@ class Model(NamedTuple):
     scan_cand: np.ndarray = None
     scan_row: np.ndarray = None
     scan_box: np.ndarray = None
+    # Edge fixtures (this engine's addition): bit 0 / bit 1 set when verts[f, 2] / verts[f, 3] is a ghost vertex
+    edge_ghost: np.ndarray = None  # i32[F]
 
 
 class Bodies(NamedTuple):
@@ -285,13 +287,48 @@ class WorldDef:
         b["v"] = np.array([F32(b["v"][0] + F32(-w * dy)), F32(b["v"][1] + F32(w * dx))], F32)
 
     def _add_fixture(self, body, shape_type, verts, normals, radius, friction, restitution, sensor, layer,
-                     category, mask, group):
+                     category, mask, group, count=None, ghost=0):
         vv, nn = shapes.pad(verts, normals)
-        self.fixtures.append(dict(body=body, shape_type=shape_type, verts=vv, normals=nn, count=len(verts),
+        self.fixtures.append(dict(body=body, shape_type=shape_type, verts=vv, normals=nn,
+                                  count=len(verts) if count is None else count, ghost=int(ghost),
                                   radius=F32(radius), friction=F32(friction), restitution=F32(restitution),
                                   sensor=bool(sensor), layer=int(layer) & 31, category=category, mask=mask,
                                   group=group))
         return len(self.fixtures) - 1
+
+    def add_edge(self, body, v1, v2, v0=None, v3=None, *, friction=0.2, restitution=0.0, sensor=False, layer=0,
+                 category=1, mask=0xFFFF, group=0):
+        """b2EdgeShape: the segment v1-v2 with the optional ghost vertices v0 (before v1) and v3 (after v2), skin
+        radius b2_polygonRadius. Massless; collides with circles and polygons, not with other edges. No counterpart in
+        the reference engine."""
+        p1, p2 = (F32(v1[0]), F32(v1[1])), (F32(v2[0]), F32(v2[1]))
+        g0 = (F32(0), F32(0)) if v0 is None else (F32(v0[0]), F32(v0[1]))
+        g3 = (F32(0), F32(0)) if v3 is None else (F32(v3[0]), F32(v3[1]))
+        nx, ny = shapes.normalize(F32(p2[1] - p1[1]), F32(-(p2[0] - p1[0])))
+        verts = np.array([p1, p2, g0, g3], F32)
+        normals = np.array([(nx, ny), (-nx, -ny), (0, 0), (0, 0)], F32)
+        ghost = (0 if v0 is None else 1) | (0 if v3 is None else 2)
+        return self._add_fixture(body, shapes.EDGE, verts, normals, self.settings.polygon_radius, friction,
+                                 restitution, sensor, layer, category, mask, group, count=2, ghost=ghost)
+
+    def add_chain(self, body, vertices, loop=False, prev_vertex=None, next_vertex=None, **kw):
+        """b2ChainShape as its child edges, one edge fixture per segment in order, each with its neighbours' ends
+        as ghost vertices (b2ChainShape::GetChildEdge). loop=True closes the chain (b2ChainShape::CreateLoop); an open
+        chain takes prev_vertex / next_vertex as its end ghosts when given. Returns the fixture indices."""
+        v = [(float(p[0]), float(p[1])) for p in np.asarray(vertices, np.float64).reshape(-1, 2)]
+        if loop:
+            if len(v) < 3:
+                raise ValueError("a chain loop needs 3 vertices or more")
+            prev_vertex, next_vertex = v[-1], v[1]
+            v = v + [v[0]]
+        elif len(v) < 2:
+            raise ValueError("a chain needs 2 vertices or more")
+        out = []
+        for i in range(len(v) - 1):
+            v0 = v[i - 1] if i > 0 else prev_vertex
+            v3 = v[i + 2] if i + 2 < len(v) else next_vertex
+            out.append(self.add_edge(body, v[i], v[i + 1], v0, v3, **kw))
+        return out
 
     def add_polygon(self, body, vertices, radius=None, raw=False, *, friction=0.2, restitution=0.0, density=0.0,
                     sensor=False, layer=0, category=1, mask=0xFFFF, group=0):
@@ -348,6 +385,7 @@ class WorldDef:
         world.py:308-329)."""
         no_collide = {frozenset((j["a"], j["b"])) for j in self.joints if not j["collide"]}
         fx, out = self.fixtures, []
+        E = shapes.EDGE
         for i in range(len(fx)):
             fi = fx[i]
             ti = self.bodies[fi["body"]]["type"]
@@ -355,14 +393,17 @@ class WorldDef:
                 fk = fx[k]
                 if fi["body"] == fk["body"] or fi["sensor"] or fk["sensor"]:
                     continue
+                if fi["shape_type"] == E and fk["shape_type"] == E:  # no edge-edge collider
+                    continue
                 if ti == STATIC and self.bodies[fk["body"]]["type"] == STATIC:
                     continue
                 if frozenset((fi["body"], fk["body"])) in no_collide:
                     continue
                 if not _filter_ok(fi, fk, self.layer_masks):
                     continue
-                out.append((k, i) if (fi["shape_type"] == shapes.CIRCLE and fk["shape_type"] == shapes.POLYGON)
-                           else (i, k))
+                first_k = ((fi["shape_type"] == shapes.CIRCLE and fk["shape_type"] == shapes.POLYGON) or
+                           fk["shape_type"] == E)  # b2Contact::Create's primary order: polygon > circle, edge first
+                out.append((k, i) if first_k else (i, k))
         return out
 
     def body_arrays(self):
@@ -388,9 +429,12 @@ class WorldDef:
 
         def col(key, dt, shape=()):
             return np.array([x[key] for x in fs], dt).reshape((F,) + shape)
-        return dict(fixture_body=col("body", I32), shape_type=col("shape_type", I32), radius=col("radius", F32),
+        geom = dict(fixture_body=col("body", I32), shape_type=col("shape_type", I32), radius=col("radius", F32),
                     count=col("count", I32), verts=col("verts", F32, (MAX_POLYGON_VERTICES, 2)),
                     normals=col("normals", F32, (MAX_POLYGON_VERTICES, 2)))
+        if any(f["shape_type"] == shapes.EDGE for f in fs):
+            geom["edge_ghost"] = col("ghost", I32)
+        return geom
 
     def fixture_arrays(self, bodies, geom=None):
         """Fixtures (friction, restitution, fat AABB at the bodies' transforms) for the given Bodies."""

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define GOIB2D_ABI_VERSION 1
+#define GOIB2D_ABI_VERSION 2
 
 #define GOIB2D_OK 0
 #define GOIB2D_EINVAL (-1)   /* bad argument (null pointer, size out of range, inconsistent layout) */
@@ -49,7 +49,10 @@ typedef struct goib2d_settings {
 
 /* The scene constants of goi_jax/box2d/world.py:30-67 (Model), as host arrays. fixture_slot == NULL: full fixture
  * layout (State.fixtures has one row per fixture); otherwise the compact layout (reference world.py:437-472): rows
- * only for fixtures of non-static bodies, static_* hold the static fixtures' values. */
+ * only for fixtures of non-static bodies, static_* hold the static fixtures' values.
+ * shape_type: 0 circle (verts[0] the centre), 2 polygon (count vertices and normals), 1 edge (no counterpart in the
+ * reference engine): count 2, verts[0] and verts[1] the segment, verts[2] and verts[3] the ghost vertices before and
+ * after it (a chain is a run of edges whose ghost vertices are their neighbours' ends), present per edge_ghost. */
 typedef struct goib2d_model_desc {
     int32_t n_bodies, n_fixtures, n_joints, n_pairs;
     const int32_t *fixture_body, *shape_type, *count;   /* [F] */
@@ -64,6 +67,7 @@ typedef struct goib2d_model_desc {
     const int32_t *fixture_slot;                        /* [F] or NULL */
     const float *static_fat;                            /* [F][4] (compact layout) */
     const float *static_friction, *static_restitution;  /* [F]    (compact layout) */
+    const int32_t *edge_ghost;  /* [F] edges: bit 0 verts[2] is a ghost vertex, bit 1 verts[3]; NULL = none */
 } goib2d_model_desc;
 
 /* State leaves, in order (goib2d/world.py STATE_LEAVES). */

@@ -28,7 +28,7 @@ enum { STATIC = 0, KINEMATIC = 1, DYNAMIC = 2 };
 enum { REVOLUTE = 1, PRISMATIC = 2, WELD = 8 };
 enum { INACTIVE_LIMIT = 0, AT_LOWER = 1, AT_UPPER = 2, EQUAL_LIMITS = 3 };
 enum { CIRCLES = 0, FACE_A = 1, FACE_B = 2 };
-enum { CIRCLE = 0, POLYGON = 2 };
+enum { CIRCLE = 0, EDGE = 1, POLYGON = 2 };
 
 struct V2 {
     float x, y;
@@ -190,7 +190,9 @@ struct Manifold {
     V2 local_normal, local_point, point[2];
     int32_t id[2];
 };
-void evaluate(const Model &m, int fa, int fb, Xf xfa, Xf xfb, float linear_slop, Manifold *out);
+// Contact manifold of a candidate pair (b2Contact::Evaluate); edges (shape type 1) have no counterpart in the
+// reference engine: they follow the same method as the device code, Box2D 2.3.1's ghost-vertex colliders.
+void evaluate(const Model &m, int fa, int fb, Xf xfa, Xf xfb, float linear_slop, float angular_slop, Manifold *out);
 
 // Pieces shared by the step and SolveTOI
 void find_new_contacts(const Model &m, World &w);

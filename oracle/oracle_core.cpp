@@ -400,16 +400,228 @@ void collide_circles(const Poly &pa, Xf xfa, const Poly &pb, Xf xfb, Manifold *o
     out->point[0] = out->point[1] = pb.vert(0);
     out->id[0] = out->id[1] = 0;
 }
+
+// ---- edges (no counterpart in the reference engine). An edge fixture: count 2, the segment in verts[0..1], the
+// ghost vertices of its chain in verts[2] (before) and verts[3] (after), flagged by edge_ghost bits 0 and 1.
+struct EdgeShape {
+    V2 g0, a, b, g3;
+    bool has_g0, has_g3;
+    float radius;
+};
+EdgeShape edge_shape(const Model &m, int f) {
+    const float *v = m.d->verts + 16 * f;
+    int flags = m.d->edge_ghost ? m.d->edge_ghost[f] : 0;
+    return {{v[4], v[5]}, {v[0], v[1]}, {v[2], v[3]}, {v[6], v[7]}, (flags & 1) != 0, (flags & 2) != 0,
+            m.d->radius[f]};
+}
+inline float lesser(float a, float b) { return a < b ? a : b; }
+void no_points(Manifold *out, int mtype) {
+    out->mtype = mtype, out->count = 0;
+    out->local_normal = out->local_point = out->point[0] = out->point[1] = V2{0.0f, 0.0f};
+    out->id[0] = out->id[1] = 0;
+}
+
+// edge against circle: the circle centre's region of the segment (end a, end b or the face between); an end whose
+// region belongs to the neighbouring edge of the chain yields nothing here
+void collide_edge_circle(const EdgeShape &e, Xf xfa, const Poly &c, Xf xfb, Manifold *out) {
+    const V2 centre = xf_mul_t(xfa, xf_mul(xfb, c.vert(0)));
+    const V2 seg = sub(e.b, e.a);
+    const float to_b = dot(seg, sub(e.b, centre)), from_a = dot(seg, sub(centre, e.a));
+    const float r = e.radius + c.radius;
+    no_points(out, CIRCLES);
+    out->point[0] = out->point[1] = c.vert(0);
+    if (from_a <= 0.0f) {
+        V2 d = sub(centre, e.a);
+        if (dot(d, d) > r * r) return;
+        if (e.has_g0 && dot(sub(e.a, e.g0), sub(e.a, centre)) > 0.0f) return;  // the previous edge's region
+        out->count = 1, out->local_point = e.a, out->id[0] = feature_key(0, 0, E_VERTEX, E_VERTEX);
+        return;
+    }
+    if (to_b <= 0.0f) {
+        V2 d = sub(centre, e.b);
+        if (dot(d, d) > r * r) return;
+        if (e.has_g3 && dot(sub(e.g3, e.b), sub(centre, e.b)) > 0.0f) return;  // the next edge's region
+        out->count = 1, out->local_point = e.b, out->id[0] = feature_key(1, 0, E_VERTEX, E_VERTEX);
+        return;
+    }
+    const float inv_len2 = 1.0f / dot(seg, seg);
+    const V2 foot{inv_len2 * (to_b * e.a.x + from_a * e.b.x), inv_len2 * (to_b * e.a.y + from_a * e.b.y)};
+    const V2 d = sub(centre, foot);
+    if (dot(d, d) > r * r) return;
+    V2 n{-seg.y, seg.x};
+    if (dot(n, sub(centre, e.a)) < 0.0f) n = neg(n);
+    out->mtype = FACE_A, out->count = 1, out->local_normal = normalize(n), out->local_point = e.a;
+    out->id[0] = feature_key(0, 0, E_FACE, E_VERTEX);
+}
+
+V2 area_centroid(const Poly &p) {  // triangles fanned from the origin
+    float area = 0.0f, sx = 0.0f, sy = 0.0f;
+    const float third = 1.0f / 3.0f;
+    for (int i = 0; i < p.count; ++i) {
+        const V2 u = p.vert(i), w = p.vert((i + 1) % p.count);
+        const float t = 0.5f * cross(u, w);
+        area = area + t;
+        sx = sx + t * third * (u.x + w.x);
+        sy = sy + t * third * (u.y + w.y);
+    }
+    const float inv = 1.0f / area;
+    return {sx * inv, sy * inv};
+}
+
+// the side of the edge the polygon's centroid c is on, and the admissible contact normals [lo, hi] there
+struct NormalRange {
+    bool front;
+    V2 normal, lo, hi;
+};
+NormalRange normal_range(const EdgeShape &e, V2 c) {
+    const V2 d1 = normalize(sub(e.b, e.a));
+    const V2 n1{d1.y, -d1.x}, m1 = neg(n1);
+    const float off1 = dot(n1, sub(c, e.a));
+    V2 n0{0.0f, 0.0f}, n2{0.0f, 0.0f};
+    float off0 = 0.0f, off2 = 0.0f;
+    bool convex_a = false, convex_b = false;
+    if (e.has_g0) {
+        const V2 d0 = normalize(sub(e.a, e.g0));
+        n0 = V2{d0.y, -d0.x};
+        convex_a = cross(d0, d1) >= 0.0f;
+        off0 = dot(n0, sub(c, e.g0));
+    }
+    if (e.has_g3) {
+        const V2 d2 = normalize(sub(e.g3, e.b));
+        n2 = V2{d2.y, -d2.x};
+        convex_b = cross(d1, d2) > 0.0f;
+        off2 = dot(n2, sub(c, e.b));
+    }
+    const bool f0 = off0 >= 0.0f, f1 = off1 >= 0.0f, f2 = off2 >= 0.0f;
+    NormalRange r{};
+    if (e.has_g0 && e.has_g3) {
+        if (convex_a && convex_b) {
+            r.front = f0 || f1 || f2;
+            r.lo = r.front ? n0 : m1;
+            r.hi = r.front ? n2 : m1;
+        } else if (convex_a) {
+            r.front = f0 || (f1 && f2);
+            r.lo = r.front ? n0 : neg(n2);
+            r.hi = r.front ? n1 : m1;
+        } else if (convex_b) {
+            r.front = f2 || (f0 && f1);
+            r.lo = r.front ? n1 : m1;
+            r.hi = r.front ? n2 : neg(n0);
+        } else {
+            r.front = f0 && f1 && f2;
+            r.lo = r.front ? n1 : neg(n2);
+            r.hi = r.front ? n1 : neg(n0);
+        }
+    } else if (e.has_g0) {
+        if (convex_a) {
+            r.front = f0 || f1;
+            r.lo = r.front ? n0 : n1;
+            r.hi = m1;
+        } else {
+            r.front = f0 && f1;
+            r.lo = n1;
+            r.hi = r.front ? m1 : neg(n0);
+        }
+    } else if (e.has_g3) {
+        if (convex_b) {
+            r.front = f1 || f2;
+            r.lo = m1;
+            r.hi = r.front ? n2 : n1;
+        } else {
+            r.front = f1 && f2;
+            r.lo = r.front ? m1 : neg(n2);
+            r.hi = n1;
+        }
+    } else {
+        r.front = f1;
+        r.lo = r.front ? m1 : n1;
+        r.hi = r.front ? m1 : n1;
+    }
+    r.normal = r.front ? n1 : m1;
+    return r;
+}
+
+// edge against polygon: separating axes (the edge's normal; the polygon's face normals inside the admissible range),
+// the reference face (the polygon's only if clearly deeper: 0.98 x + 0.001), the incident feature clipped to it
+void collide_edge_polygon(const EdgeShape &e, Xf xfa, const Poly &p, Xf xfb, float angular_slop, Manifold *out) {
+    const Rot q{xfa.q.c * xfb.q.c + xfa.q.s * xfb.q.s, xfa.q.c * xfb.q.s - xfa.q.s * xfb.q.c};
+    const Xf rel{rot_t(xfa.q, sub(xfb.p, xfa.p)), q};  // the polygon's frame seen from the edge's
+    const int k = p.count;
+    no_points(out, FACE_A);
+    const NormalRange nr = normal_range(e, xf_mul(rel, area_centroid(p)));
+    const float r = e.radius + p.radius;
+    float edge_sep = MAXF;
+    for (int i = 0; i < k; ++i) edge_sep = lesser(edge_sep, dot(nr.normal, sub(xf_mul(rel, p.vert(i)), e.a)));
+    if (edge_sep > r) return;
+    int face = -1;
+    float face_sep = -MAXF;
+    const V2 perp{-nr.normal.y, nr.normal.x};
+    for (int i = 0; i < k; ++i) {
+        const V2 nn = neg(rot(rel.q, p.norm(i)));
+        const V2 vi = xf_mul(rel, p.vert(i));
+        const float sep = lesser(dot(nn, sub(vi, e.a)), dot(nn, sub(vi, e.b)));
+        if (sep > r) {
+            face = i, face_sep = sep;
+            break;
+        }
+        const V2 limit = dot(nn, perp) >= 0.0f ? nr.hi : nr.lo;
+        if (dot(sub(nn, limit), nr.normal) < -angular_slop) continue;
+        if (sep > face_sep) face = i, face_sep = sep;
+    }
+    if (face >= 0 && face_sep > r) return;
+    const bool poly_ref = face >= 0 && face_sep > 0.98f * edge_sep + 0.001f;
+    ClipV inc[2];
+    int ia, ib;
+    V2 ref_a, ref_b, ref_n;
+    if (poly_ref) {
+        inc[0] = ClipV{e.a, 0, face, E_VERTEX, E_FACE};
+        inc[1] = ClipV{e.b, 0, face, E_VERTEX, E_FACE};
+        ia = face, ib = (face + 1) % k;
+        ref_a = xf_mul(rel, p.vert(ia)), ref_b = xf_mul(rel, p.vert(ib)), ref_n = rot(rel.q, p.norm(ia));
+    } else {
+        int low = 0;
+        float low_dot = dot(nr.normal, rot(rel.q, p.norm(0)));
+        for (int i = 1; i < k; ++i) {
+            const float dv = dot(nr.normal, rot(rel.q, p.norm(i)));
+            if (dv < low_dot) low_dot = dv, low = i;
+        }
+        const int nxt = (low + 1) % k;
+        inc[0] = ClipV{xf_mul(rel, p.vert(low)), 0, low, E_FACE, E_VERTEX};
+        inc[1] = ClipV{xf_mul(rel, p.vert(nxt)), 0, nxt, E_FACE, E_VERTEX};
+        ia = nr.front ? 0 : 1, ib = nr.front ? 1 : 0;
+        ref_a = nr.front ? e.a : e.b, ref_b = nr.front ? e.b : e.a, ref_n = nr.normal;
+    }
+    const V2 side1{ref_n.y, -ref_n.x}, side2 = neg(side1);
+    ClipV once[2], twice[2];
+    if (clip(inc, side1, dot(side1, ref_a), ia, once) < 2) return;
+    if (clip(once, side2, dot(side2, ref_b), ib, twice) < 2) return;
+    out->mtype = poly_ref ? FACE_B : FACE_A;
+    out->local_normal = poly_ref ? p.norm(ia) : ref_n;
+    out->local_point = poly_ref ? p.vert(ia) : ref_a;
+    int n = 0;
+    for (int j = 0; j < 2; ++j) {
+        const ClipV &cv = twice[j];
+        if (dot(ref_n, sub(cv.v, ref_a)) > r) continue;
+        out->point[n] = poly_ref ? cv.v : xf_mul_t(rel, cv.v);
+        out->id[n] = poly_ref ? feature_key(cv.ib, cv.ia, cv.tb, cv.ta) : feature_key(cv.ia, cv.ib, cv.ta, cv.tb);
+        ++n;
+    }
+    out->count = n;
+}
 }  // namespace
 
-void evaluate(const Model &m, int fa, int fb, Xf xfa, Xf xfb, float linear_slop, Manifold *out) {
-    // collide.py:189-207
+void evaluate(const Model &m, int fa, int fb, Xf xfa, Xf xfb, float linear_slop, float angular_slop, Manifold *out) {
+    // collide.py:189-207, plus the edge pairs (edge first, as b2Contact::Create orders them)
     Poly pa = poly_of(m, fa), pb = poly_of(m, fb);
     int ta = m.d->shape_type[fa], tb = m.d->shape_type[fb];
     if (ta == POLYGON && tb == POLYGON)
         collide_polygons(pa, xfa, pb, xfb, linear_slop, out);
     else if (ta == POLYGON && tb == CIRCLE)
         collide_polygon_circle(pa, xfa, pb, xfb, out);
+    else if (ta == EDGE && tb == CIRCLE)
+        collide_edge_circle(edge_shape(m, fa), xfa, pb, xfb, out);
+    else if (ta == EDGE && tb == POLYGON)
+        collide_edge_polygon(edge_shape(m, fa), xfa, pb, xfb, angular_slop, out);
     else
         collide_circles(pa, xfa, pb, xfb, out);
 }

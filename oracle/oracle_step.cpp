@@ -78,7 +78,7 @@ static void collide(const Model &m, World &w, const goib2d_settings &s) {
     for (int s_ : order) {
         int ba = fbody[w.fa[s_]], bb = fbody[w.fb[s_]];
         over[s_] = overlap(fixture_fat(m, w, w.fa[s_]), fixture_fat(m, w, w.fb[s_]));
-        evaluate(m, w.fa[s_], w.fb[s_], w.bxf(ba), w.bxf(bb), s.linear_slop, &man[s_]);
+        evaluate(m, w.fa[s_], w.fb[s_], w.bxf(ba), w.bxf(bb), s.linear_slop, s.angular_slop, &man[s_]);
     }
     for (int s_ : order) {
         int ba = fbody[w.fa[s_]], bb = fbody[w.fb[s_]];

@@ -460,7 +460,7 @@ void event(const Model &m, World &w, const goib2d_settings &s, float dt, int min
     }
     auto man_of = [&](int slot, Manifold *mn) {
         int ba = fbody[w.fa[slot]], bb = fbody[w.fb[slot]];
-        evaluate(m, w.fa[slot], w.fb[slot], axf[ba], axf[bb], s.linear_slop, mn);
+        evaluate(m, w.fa[slot], w.fb[slot], axf[ba], axf[bb], s.linear_slop, s.angular_slop, mn);
     };
     std::vector<uint8_t> flip_b(B, 0), in_isl_other(B, 0), touched_other(B, 0), newbody(B, 0);
     Manifold mmin;

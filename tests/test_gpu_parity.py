@@ -79,6 +79,39 @@ def test_gpu_matches_oracle_on_workloads(api, cfg, n, steps):
     assert ((eng.status() & 0b1011) == 0).all()  # no overflow, no non-finite state, no table limit
 
 
+@pytest.mark.parametrize("name,n,steps", [("circle_on_edge", 8, 120), ("box_on_chain", 16, 120),
+                                          ("box_on_edges", 16, 120), ("slope_chain", 32, 200),
+                                          ("bullet_at_edge", 8, 30)])
+def test_gpu_matches_oracle_on_edge_scenes(api, name, n, steps):
+    """Edge and chain shapes (this engine's own; no reference states exist): perturbed batches on the GPU equal
+    the oracle's restatement of the same method, bit for bit."""
+    import edge_scenes
+    from goib2d.world import map_state
+    model, st = edge_scenes.build(name, 64)
+    settings = edge_scenes.SCENES[name]().settings
+    host = map_state(lambda x: np.ascontiguousarray(np.repeat(np.asarray(x)[None], n, 0)), st)
+    rng = np.random.default_rng(7)
+    dyn = (host.bodies.type == 2)[..., None]
+    host.bodies.v[...] = np.where(dyn, host.bodies.v + rng.normal(0, 0.4, host.bodies.v.shape), host.bodies.v)
+    dev = api.to_device(host)
+    api.step_(model, dev, settings, edge_scenes.DT, n_steps=steps)
+    want = oracle_lib.step(model, host, settings, edge_scenes.DT, steps, threads=8)
+    assert_states_equal(api.to_host(dev), want, name)
+
+
+@pytest.mark.parametrize("cfg,n,steps", [("c0e", 64, 60), ("c1e", 256, 40), ("c3e", 128, 20)])
+def test_gpu_matches_oracle_on_edge_workloads(api, cfg, n, steps):
+    """BASELINE's own levels with edge shapes (chain terrain, lone edge targets) equal the oracle world for world."""
+    from goib2d import configs
+    sc, model, host = configs.batch(cfg, n)
+    dev = api.to_device(host)
+    eng = api.engine_for(model, host.bodies.type.shape[1])
+    eng.step_(dev, sc.settings, configs.DT, n_steps=steps)
+    want = oracle_lib.step(model, host, sc.settings, configs.DT, steps, threads=8)
+    assert_states_equal(api.to_host(dev), want, cfg)
+    assert ((eng.status() & 0b1011) == 0).all()
+
+
 @pytest.mark.parametrize("cfg,steps", [("c1", 12), ("c4", 6)])
 def test_large_batches_match_oracle(api, cfg, steps):
     """A batch large enough that the constraint sweeps run one world per thread (16384 worlds and up) equals the
@@ -133,4 +166,4 @@ def test_errors_are_reported_not_trapped(api):
         api.step_(g.model, bad, g.settings, g.dt)
     empty = api.to_device(g.state(0, batch=0))
     api.step_(g.model, empty, g.settings, g.dt)
-    assert native.load().goib2d_version() == 1
+    assert native.load().goib2d_version() == 2
