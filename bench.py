@@ -36,7 +36,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c1", choices=("c0", "c1", "c2", "c3", "c4"))
+    ap.add_argument("--config", default="c1", choices=("c0", "c1", "c2", "c3", "c4", "c0e", "c1e", "c3e", "c4e"))
     ap.add_argument("--worlds", type=int, default=None, help="worlds per GPU (default: the config's N)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--seed", type=int, default=0)
@@ -93,6 +93,19 @@ class Clocks:
                 "reasons": reasons, "samples": len(sm)}
 
 
+WORKLOADS = {
+    "c0": "c0_box_drop (BASELINE configs[0], polygon-terrain variant)",
+    "c1": "c1_rig (BASELINE configs[1], polygon-terrain variant)",
+    "c2": "c2_stress (BASELINE configs[2])",
+    "c3": "c3_toi (BASELINE configs[3], 0.02 m boxes for the zero-thickness edges)",
+    "c4": "c4_scale (BASELINE configs[4], polygon-terrain variant)",
+    "c0e": "c0_box_drop_chain (BASELINE configs[0], its chain terrain; edge shapes, parity unpinned)",
+    "c1e": "c1_rig_chain (BASELINE configs[1], its 2000-segment chain; edge shapes, parity unpinned)",
+    "c3e": "c3_toi_edges (BASELINE configs[3], zero-thickness edge targets; parity unpinned)",
+    "c4e": "c4_scale_chain (BASELINE configs[4], chain terrain; parity unpinned)",
+}
+
+
 def measured_peak():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -137,7 +150,7 @@ def run_reference(args, rank):
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * n / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded, goib2d/configs.py)", "impl": "reference",
-            "config": {"workload": f"{sc.name} (BASELINE configs[1], polygon-terrain variant)",
+            "config": {"workload": WORKLOADS.get(args.config, sc.name),
                        "worlds": n, "dt": float(configs.DT), "iterations": "8/3", "continuous_physics": True},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's JAX engine is not installed here; its algorithm runs as the bit-identical C++ "
@@ -172,8 +185,18 @@ def main():
     acts = torch.from_numpy(acts_host).to(dev) if na else None
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
+    # BASELINE c4: every world resets to its seeded initial state when the pot (body 1) falls below y = -5
+    resets = args.config.startswith("c4")
+    init_state = api.to_device(host, dev) if resets else None
+    reset_count = torch.zeros(n, dtype=torch.int32, device=dev) if resets else None
+
+    def world_step(a):
+        eng.step_(state, sc.settings, configs.DT, 1, a)
+        if resets:
+            eng.reset_below(state, init_state, 1, -5.0, reset_count)
+
     for k in range(Wm):
-        eng.step_(state, sc.settings, configs.DT, 1, acts[k] if na else None)
+        world_step(acts[k] if na else None)
     torch.cuda.synchronize(dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
@@ -186,7 +209,7 @@ def main():
     for k in range(K):
         flush.fill_(float(k))
         starts[k].record(stream)
-        eng.step_(state, sc.settings, configs.DT, 1, acts[Wm + k] if na else None)
+        world_step(acts[Wm + k] if na else None)
         ends[k].record(stream)
     torch.cuda.synchronize(dev)
     wall = time.perf_counter() - wall0
@@ -215,7 +238,7 @@ def main():
     for k in range(Ke):
         if na:
             a_dev.copy_(a_pin[k], non_blocking=True)
-        eng.step_(state, sc.settings, configs.DT, 1, a_dev if na else None)
+        world_step(a_dev if na else None)
         obs_pin.copy_(state.bodies.c[:, 1], non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize(dev)
@@ -244,7 +267,8 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": K, "warmup": Wm,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded worlds, goib2d/configs.py)",
-            "config": {"workload": f"{sc.name} (BASELINE configs[1], polygon-terrain variant)",
+            "config": {"workload": WORKLOADS.get(args.config, sc.name),
+                       "reset_on_fall": "pot below y = -5 -> the world's seeded initial state" if resets else None,
                        "worlds_per_gpu": n, "global_worlds": n * world_size, "dt": float(configs.DT),
                        "iterations": "8/3", "continuous_physics": True, "contact_capacity": sc.capacity,
                        "bodies": int(host.bodies.type.shape[1]), "fixtures": int(model.fixture_body.shape[0]),
@@ -254,13 +278,15 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                          "algorithmic_bytes_per_world_step": bytes_ws,
-                         "kernel": "one step's launch group (goib2d_collide_kernel, goib2d_solve_kernel, "
-                                   "goib2d_toi_kernel), timed as one unit by the per-step CUDA events",
+                         "kernel": (f"one step's launch group ({native.load().goib2d_kernels_per_step(n)} part "
+                                    f"kernels{' + the reset kernel' if resets else ''}), timed as one unit by the "
+                                    "per-step CUDA events"),
                          "traffic_source": f"profiles/traffic_{args.config}.json (ncu dram bytes of the launch group)"
                                            if traffic is not None else None},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": n * na * 4 * world_size,
                     "d2h_bytes_per_step": n * 2 * 4 * world_size, "steps": Ke},
-            "gpu_launches": K * native.load().goib2d_kernels_per_step(n), "clocks": clk, "wall_s_timed": wall,
+            "gpu_launches": K * (native.load().goib2d_kernels_per_step(n) + int(resets)), "clocks": clk,
+            "wall_s_timed": wall,
             "nonfinite_worlds": nonfinite,
             "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)

@@ -15,6 +15,9 @@
 namespace gb {
 cudaError_t launch_steps(StepParams p, cudaStream_t stream);  // step.cu
 int kernels_per_step(int64_t n_worlds);                       // step.cu
+cudaError_t launch_reset(const EnvParams &p, cudaStream_t s);    // env.cuh (compiled in step.cu)
+cudaError_t launch_observe(const EnvParams &p, cudaStream_t s);  // env.cuh
+cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s);  // env.cuh
 }
 
 namespace {
@@ -509,6 +512,94 @@ int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int
         p.action_scale = m->action_scale;
     }
     CUDA_TRY(gb::launch_steps(p, (cudaStream_t)stream));
+    return 0;
+}
+
+// ---- env helpers (env.cuh)
+namespace {
+// the Model layout a call's fixture_rows selects (as goib2d_step does)
+int pick_layout(goib2d_model *m, int32_t rows, const gb::DevModel **dm) {
+    if (rows == m->full.F)
+        *dm = &m->full;
+    else if (m->has_compact && rows == m->n_rows_compact)
+        *dm = &m->compact;
+    else
+        return fail(GOIB2D_EINVAL, "fixture rows %d match neither the full (%d) nor the compact (%d) layout", rows,
+                    m->full.F, m->has_compact ? m->n_rows_compact : -1);
+    return 0;
+}
+int env_params(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves, gb::EnvParams &p) {
+    if (!m || !leaves) return fail(GOIB2D_EINVAL, "null argument");
+    if (C < 0 || n_worlds < 0) return fail(GOIB2D_EINVAL, "negative size");
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != m->device) return fail(GOIB2D_EINVAL, "model lives on device %d, current device is %d", m->device, dev);
+    const gb::DevModel *dm = nullptr;
+    int rc = pick_layout(m, rows, &dm);
+    if (rc) return rc;
+    p = gb::EnvParams{};
+    p.m = *dm;
+    p.n_worlds = n_worlds, p.B = dm->B, p.rows = rows;
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) {
+        if (!leaves[i] && goib2d_leaf_elems(i, dm->B, rows, dm->J, C) > 0 && n_worlds > 0)
+            return fail(GOIB2D_EINVAL, "leaf %d is null", i);
+        p.L.p[i] = leaves[i];
+        p.leaf_bytes[i] = (int32_t)(goib2d_leaf_elems(i, dm->B, rows, dm->J, C) * (LEAVES[i].dtype == 2 ? 1 : 4));
+    }
+    return 0;
+}
+}  // namespace
+
+int goib2d_reset_masked(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves,
+                        void *const *init_leaves, const uint8_t *mask, void *stream) {
+    gb::EnvParams p;
+    int rc = env_params(m, C, rows, n_worlds, leaves, p);
+    if (rc) return rc;
+    if (!init_leaves || (!mask && n_worlds > 0)) return fail(GOIB2D_EINVAL, "null argument");
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.I.p[i] = init_leaves[i];
+    p.mask = mask;
+    CUDA_TRY(gb::launch_reset(p, (cudaStream_t)stream));
+    return 0;
+}
+
+int goib2d_reset_below(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves,
+                       void *const *init_leaves, int32_t body, float y_min, int32_t *reset_count, void *stream) {
+    gb::EnvParams p;
+    int rc = env_params(m, C, rows, n_worlds, leaves, p);
+    if (rc) return rc;
+    if (!init_leaves) return fail(GOIB2D_EINVAL, "null argument");
+    if (body < 0 || body >= p.B) return fail(GOIB2D_EINVAL, "body %d out of range", body);
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.I.p[i] = init_leaves[i];
+    p.body = body, p.y_min = y_min, p.reset_count = reset_count;
+    CUDA_TRY(gb::launch_reset(p, (cudaStream_t)stream));
+    return 0;
+}
+
+int goib2d_observe(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves, int32_t n_bodies,
+                   const int32_t *bodies, float *out, void *stream) {
+    gb::EnvParams p;
+    int rc = env_params(m, C, rows, n_worlds, leaves, p);
+    if (rc) return rc;
+    if (n_bodies < 0 || n_bodies > 16) return fail(GOIB2D_ELIMIT, "%d observed bodies (16 at most)", n_bodies);
+    if ((n_bodies && !bodies) || (!out && n_worlds && n_bodies)) return fail(GOIB2D_EINVAL, "null argument");
+    for (int k = 0; k < n_bodies; ++k) {
+        if (bodies[k] < 0 || bodies[k] >= p.B) return fail(GOIB2D_EINVAL, "body %d out of range", bodies[k]);
+        p.obs_body[k] = bodies[k];
+    }
+    p.n_obs = n_bodies, p.out = out;
+    CUDA_TRY(gb::launch_observe(p, (cudaStream_t)stream));
+    return 0;
+}
+
+int goib2d_raycast(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves, int32_t body,
+                   int32_t n_rays, float max_length, float *out, void *stream) {
+    gb::EnvParams p;
+    int rc = env_params(m, C, rows, n_worlds, leaves, p);
+    if (rc) return rc;
+    if (body < 0 || body >= p.B) return fail(GOIB2D_EINVAL, "body %d out of range", body);
+    if (n_rays < 0 || (!out && n_worlds && n_rays)) return fail(GOIB2D_EINVAL, "bad ray arguments");
+    p.body = body, p.n_rays = n_rays, p.max_length = max_length, p.out = out;
+    CUDA_TRY(gb::launch_raycast(p, (cudaStream_t)stream));
     return 0;
 }
 

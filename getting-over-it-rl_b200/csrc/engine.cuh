@@ -132,6 +132,25 @@ struct StepParams {
     int32_t *status;
 };
 
+// Parameters of the env kernels (env.cu): resets, observations, ray casts.
+struct EnvParams {
+    DevModel m;
+    Leaves L;     // the batch's State
+    Leaves I;     // a State of the same shape holding each world's initial state (resets)
+    int32_t leaf_bytes[GOIB2D_NUM_LEAVES];  // bytes of one world's row of each leaf
+    int64_t n_worlds;
+    int B, rows;
+    const uint8_t *mask;  // reset where mask[w] != 0 ...
+    int body;             // ... or where bodies.c[w][body].y < y_min
+    float y_min;
+    int32_t *reset_count;  // optional per-world counters
+    int n_obs;
+    int32_t obs_body[16];
+    float *out;
+    int n_rays;
+    float max_length;
+};
+
 // Status bits (include/goib2d.h goib2d_status)
 enum { ST_OVERFLOW = 1, ST_NONFINITE = 2, ST_CAP = 4, ST_LIMIT = 8 };
 

@@ -45,6 +45,7 @@ __device__ unsigned long long g_toi_cycles[16];
     } while (0)
 #endif
 
+#include "env.cuh"
 #include "solver.cuh"
 #include "toi.cuh"
 

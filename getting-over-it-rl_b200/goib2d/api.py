@@ -103,6 +103,52 @@ class Engine:
                                           int(n_steps), ptrs, act, stream))
         return state
 
+    # ---- env helpers (goib2d_reset_*, goib2d_observe, goib2d_raycast): device tensors in and out, on the State's
+    # current stream; no counterpart in the reference engine.
+
+    def _stream(self, device):
+        return torch.cuda.current_stream(device).cuda_stream
+
+    def reset_masked(self, state, init_state, mask):
+        """Worlds with mask[w] set (bool/uint8 cuda tensor (N,)) get every leaf's row from init_state (a device
+        State of the same shape: each world's initial state)."""
+        n, C_, rows, device, ptrs = self._bind(state)
+        init = (C.c_void_p * len(ptrs))(*[t.data_ptr() for t in state_leaves(init_state)])
+        m = mask.to(torch.uint8).contiguous()
+        native.check(self.lib.goib2d_reset_masked(self.handle, C_, rows, n, ptrs, init, m.data_ptr(),
+                                                  self._stream(device)))
+        return state
+
+    def reset_below(self, state, init_state, body, y_min, counts=None):
+        """BASELINE c4's reset-on-fall: the worlds whose `body` has c.y < y_min are reset to init_state; counts
+        (int32 cuda tensor (N,), optional) counts the resets per world."""
+        n, C_, rows, device, ptrs = self._bind(state)
+        init = (C.c_void_p * len(ptrs))(*[t.data_ptr() for t in state_leaves(init_state)])
+        cp = counts.data_ptr() if counts is not None else None
+        native.check(self.lib.goib2d_reset_below(self.handle, C_, rows, n, ptrs, init, int(body), C.c_float(y_min),
+                                                 cp, self._stream(device)))
+        return state
+
+    def observe(self, state, bodies, out=None):
+        """(N, len(bodies), 6) float32: c.x, c.y, angle, v.x, v.y, w of the given bodies."""
+        n, C_, rows, device, ptrs = self._bind(state)
+        b = np.ascontiguousarray(bodies, np.int32)
+        if out is None:
+            out = torch.empty((n, len(b), 6), dtype=torch.float32, device=device)
+        native.check(self.lib.goib2d_observe(self.handle, C_, rows, n, ptrs, len(b), b.ctypes.data_as(native._i),
+                                             out.data_ptr(), self._stream(device)))
+        return out
+
+    def raycast(self, state, body, n_rays, max_length, out=None):
+        """(N, n_rays) float32: nearest hit fraction of ray k from `body`'s centre of mass at angle 2 pi k / n_rays
+        over the static level (1 = no hit within max_length)."""
+        n, C_, rows, device, ptrs = self._bind(state)
+        if out is None:
+            out = torch.empty((n, n_rays), dtype=torch.float32, device=device)
+        native.check(self.lib.goib2d_raycast(self.handle, C_, rows, n, ptrs, int(body), int(n_rays),
+                                             C.c_float(max_length), out.data_ptr(), self._stream(device)))
+        return out
+
     def status(self):
         """Per-world status words of the last step, copied to the host (numpy int32; see goib2d_status)."""
         n = C.c_int64()

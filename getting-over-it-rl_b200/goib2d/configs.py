@@ -196,13 +196,16 @@ def _level_c1(rng, friction=0.7, terrain="quads"):
     return h, x0, dx, polys, rocks
 
 
-def _rig_start(h, x0, dx, rocks, r):
+def _rig_start(h, x0, dx, rocks, r, min_ground=None):
     """The pot resting just above the terrain under it, away from every rock; the hammer above the pot (pointing
-    up and to either side), as the character starts in the game."""
+    up and to either side), as the character starts in the game. min_ground: only where the ground under the pot is
+    above it (c4, whose reset-on-fall rule is pot y < -5)."""
     while True:
         x = r.uniform(x0 + 10, x0 + 2000 * dx - 10)
         i0, i1 = int((x - 0.8 - x0) / dx), int((x + 0.8 - x0) / dx) + 1
         y = float(h[i0:i1 + 1].max()) + 0.62
+        if min_ground is not None and float(h[i0:i1 + 1].min()) < min_ground:
+            continue
         if all((x - px) ** 2 + (y - py) ** 2 > (rr + 2.8) ** 2 for px, py, rr in rocks):
             break
     ang = r.uniform(0.2 * np.pi, 0.8 * np.pi)
@@ -345,6 +348,9 @@ def _c4_bodies(defn, sc, i):
 
 def c4(seed=0, n=65536, terrain="quads"):
     sc = c1(seed, n, terrain)
+    h, x0, dx = sc.level
+    rocks = _level_c1(np.random.default_rng(seed), terrain=terrain)[4]
+    sc.dyn = _per_world(seed, n, lambda r: _rig_start(h, x0, dx, rocks, r, min_ground=-3.0))
     sc.name, sc.capacity, sc.steps = "c4_scale" if terrain == "quads" else "c4_scale_chain", 64, 10000
     sc.builder = _c4_bodies
     h, x0, dx = sc.level

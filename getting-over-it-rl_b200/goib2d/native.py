@@ -149,6 +149,12 @@ def load():
         "goib2d_step_noalloc": (C.c_int, [vp, vp, C.c_float, C.c_int32, C.c_int32, C.c_int64, C.c_int32,
                                           C.POINTER(vp), vp, vp]),
         "goib2d_kernels_per_step": (C.c_int, [C.c_int64]),
+        "goib2d_reset_masked": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp), vp, vp]),
+        "goib2d_reset_below": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp),
+                                         C.c_int32, C.c_float, vp, vp]),
+        "goib2d_observe": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.c_int32, _i, vp, vp]),
+        "goib2d_raycast": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.c_int32, C.c_int32,
+                                     C.c_float, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

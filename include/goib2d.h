@@ -141,6 +141,31 @@ int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
  * in the reference engine. */
 int goib2d_kernels_per_step(int64_t n_worlds);
 
+/* ---- Env helpers around the step (no counterpart in the reference engine, whose RL env is outside it). Same
+ * contact_capacity / fixture_rows / leaves conventions as goib2d_step; asynchronous on `stream`. */
+
+/* Reset world w (every leaf's row) to init_leaves' row w where mask[w] != 0 (device uint8 [n_worlds]). init_leaves:
+ * a State of the same shape holding each world's initial state. */
+int goib2d_reset_masked(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
+                        void *const *leaves, void *const *init_leaves, const uint8_t *mask, void *stream);
+
+/* The same reset for the worlds whose body `body` has its centre of mass below y_min (bodies.c[w][body].y < y_min):
+ * BASELINE c4's reset-on-fall. reset_count: NULL, or device int32 [n_worlds] incremented per reset world. */
+int goib2d_reset_below(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
+                       void *const *leaves, void *const *init_leaves, int32_t body, float y_min, int32_t *reset_count,
+                       void *stream);
+
+/* Observations: out (device float32 [n_worlds][n_bodies][6]) = c.x, c.y, angle, v.x, v.y, w of bodies[k] (host
+ * int32 [n_bodies], at most 16). */
+int goib2d_observe(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
+                   void *const *leaves, int32_t n_bodies, const int32_t *bodies, float *out, void *stream);
+
+/* Ray casts against the static level: ray k of world w leaves body `body`'s centre of mass in direction
+ * 2 pi k / n_rays (world frame) for max_length; out (device float32 [n_worlds][n_rays]) = the nearest hit fraction
+ * over the fixtures of static bodies (b2RayCastOutput::fraction; 1 = no hit). */
+int goib2d_raycast(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
+                   void *const *leaves, int32_t body, int32_t n_rays, float max_length, float *out, void *stream);
+
 /* Bytes of the static scratch arena used by goib2d_step_noalloc (on every device that loads the library). */
 #define GOIB2D_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -75,6 +75,22 @@ def step(model, state, settings, dt, n_steps=1, threads=0, actions=None, action_
     return out
 
 
+def raycast(model, state, body, n_rays, max_length):
+    """The oracle's ray casts (see goib2d_raycast) for a batched numpy State: (N, n_rays) float32."""
+    lib = load()
+    st = batched(state)
+    leaves = [np.ascontiguousarray(x) for x in state_leaves(st)]
+    N, B = leaves[0].shape[0], leaves[0].shape[1]
+    pm = native.model_desc(model, B)
+    out = np.zeros((N, n_rays), np.float32)
+    ptrs = (C.c_void_p * len(leaves))(*[x.ctypes.data for x in leaves])
+    lib.oracle_raycast.argtypes = [C.POINTER(native.ModelDesc), C.c_int32, C.c_int64, C.POINTER(C.c_void_p),
+                                   C.c_int32, C.c_int32, C.c_float, C.c_void_p]
+    assert lib.oracle_raycast(C.byref(pm.desc), st.fixtures.friction.shape[1], N, ptrs, body, n_rays,
+                              C.c_float(max_length), out.ctypes.data) == 0
+    return out
+
+
 def sin_cos(x):
     lib = load()
     x = np.ascontiguousarray(x, np.float32)
