@@ -16,7 +16,6 @@ of the same workload. The reference's own JAX engine cannot run here (no jax/jax
 import argparse
 import json
 import os
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -62,35 +61,57 @@ def state_bytes(state):
 
 
 class Clocks:
-    """nvidia-smi sampled every 200 ms during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """The SM clock, its maximum and the active clock-event (throttle) reasons of the bench's GPU, read through NVML
+    every 2 ms by a thread while the timed region runs (nvidia-smi's query when NVML is unavailable). Reads only."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index):
-        self.index, self.proc = index, None
+    def __init__(self, device):
+        self.device, self.rows, self.thread, self.nvml, self.h = device, [], None, None, None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        try:  # the same GPU as the CUDA device, whatever CUDA_VISIBLE_DEVICES maps
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(int(self.device))
 
     def start(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            self.nvml, self.h = self._handle()
+        except Exception:
+            self.nvml = None
+            return
+        nv, h = self.nvml, self.h
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        self.stop_flag = False
+
+        def poll():
+            while not self.stop_flag:
+                self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), int(get_reasons(h))))
+                time.sleep(0.002)
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
-        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
-        sm = [float(r[1]) for r in rows if len(r) > 8 and r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) > 8 and r[2].strip().replace(".", "").isdigit()]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows if len(r) > 8 for n, v in zip(names, r[5:9]) if "Active" in v and
-                          "Not" not in v})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(sm)}
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML unavailable"], "samples": 0}
+        self.stop_flag = True
+        self.thread.join(timeout=5)
+        sm = [r[0] for r in self.rows]
+        mask = 0
+        for r in self.rows:
+            mask |= r[1]
+        mx = self.nvml.nvmlDeviceGetMaxClockInfo(self.h, self.nvml.NVML_CLOCK_SM)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": float(mx),
+                "reasons": sorted(n for b, n in self.REASONS.items() if mask & b), "samples": len(sm),
+                "source": "NVML, every 2 ms during the timed region"}
 
 
 WORKLOADS = {
@@ -224,22 +245,21 @@ def main():
     ms_max = float(t.item())
     value = world_size * n * K / (ms_max / 1e3)
 
-    # e2e through the public API with host buffers: per step, this step's actions from pinned host memory to the
-    # device, the step, and the pot's position (the env's observation) back to pinned host memory
+    # e2e through the public API with host buffers: per step, this step's actions read from pinned host memory by
+    # the step's first kernel (mapped memory: the host->device transfer, no separate copy), the step, and the pot's
+    # observation (position, angle, velocities) written by goib2d_observe into pinned host memory; the host
+    # synchronises at the end of the timed region before reading it
     Ke = max(3, min(K, 20))
     a_pin = torch.from_numpy(actions_for(n, Ke, args.seed + 1, first)).pin_memory() if na else None
-    a_dev = torch.empty((n, max(na, 1)), dtype=torch.float32, device=dev)
-    obs_pin = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+    obs_pin = torch.empty((n, 1, 6), dtype=torch.float32).pin_memory()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world_size > 1:
         dist.barrier()
     e0.record(stream)
     for k in range(Ke):
-        if na:
-            a_dev.copy_(a_pin[k], non_blocking=True)
-        world_step(a_dev if na else None)
-        obs_pin.copy_(state.bodies.c[:, 1], non_blocking=True)
+        world_step(a_pin[k] if na else None)
+        eng.observe(state, [1], out=obs_pin)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
@@ -284,7 +304,9 @@ def main():
                          "traffic_source": f"profiles/traffic_{args.config}.json (ncu dram bytes of the launch group)"
                                            if traffic is not None else None},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": n * na * 4 * world_size,
-                    "d2h_bytes_per_step": n * 2 * 4 * world_size, "steps": Ke},
+                    "d2h_bytes_per_step": n * 6 * 4 * world_size, "steps": Ke,
+                    "path": "actions read from pinned host memory by the step kernel; goib2d_observe writes the pot's "
+                            "pose and velocity to pinned host memory"},
             "gpu_launches": K * (native.load().goib2d_kernels_per_step(n) + int(resets)), "clocks": clk,
             "wall_s_timed": wall,
             "nonfinite_worlds": nonfinite,

@@ -206,6 +206,23 @@ struct goib2d_model {
 
 extern "C" {
 
+// A kernel-accessible address for a caller's buffer: device memory as is; page-locked (pinned) host memory through
+// its mapped device address, so the kernels read or write it over the bus with no separate copy.
+static int device_view(const void *ptr, const void **out) {
+    *out = ptr;
+    if (!ptr) return 0;
+    cudaPointerAttributes a{};
+    CUDA_TRY(cudaPointerGetAttributes(&a, ptr));
+    if (a.type == cudaMemoryTypeHost) {
+        void *d = nullptr;
+        CUDA_TRY(cudaHostGetDevicePointer(&d, const_cast<void *>(ptr), 0));
+        *out = d;
+    } else if (a.type == cudaMemoryTypeUnregistered) {
+        return fail(GOIB2D_EINVAL, "a host buffer that is not page-locked cannot be read by the kernels");
+    }
+    return 0;
+}
+
 int goib2d_version(void) { return GOIB2D_ABI_VERSION; }
 
 int goib2d_kernels_per_step(int64_t n_worlds) { return gb::kernels_per_step(n_worlds); }
@@ -416,7 +433,10 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
     m->status_n = n_worlds;
     p.scratch = m->scratch, p.status = m->status;
     if (actions && m->n_action > 0) {
-        p.actions = actions, p.n_action = m->n_action, p.action_joint = m->action_joint;
+        const void *a = nullptr;
+        int arc = device_view(actions, &a);
+        if (arc) return arc;
+        p.actions = (const float *)a, p.n_action = m->n_action, p.action_joint = m->action_joint;
         p.action_scale = m->action_scale;
     }
     if ((n_worlds + 3) / 4 > 0x7fffffff) return fail(GOIB2D_ELIMIT, "too many worlds");
@@ -508,7 +528,10 @@ int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int
     p.scratch = scratch;
     p.status = nullptr;  // no per-world status words (their buffer would need an allocation)
     if (actions && m->n_action > 0) {
-        p.actions = actions, p.n_action = m->n_action, p.action_joint = m->action_joint;
+        const void *a = nullptr;
+        int arc = device_view(actions, &a);
+        if (arc) return arc;
+        p.actions = (const float *)a, p.n_action = m->n_action, p.action_joint = m->action_joint;
         p.action_scale = m->action_scale;
     }
     CUDA_TRY(gb::launch_steps(p, (cudaStream_t)stream));
@@ -586,7 +609,9 @@ int goib2d_observe(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, v
         if (bodies[k] < 0 || bodies[k] >= p.B) return fail(GOIB2D_EINVAL, "body %d out of range", bodies[k]);
         p.obs_body[k] = bodies[k];
     }
-    p.n_obs = n_bodies, p.out = out;
+    const void *o = nullptr;
+    if ((rc = device_view(out, &o))) return rc;
+    p.n_obs = n_bodies, p.out = (float *)o;
     CUDA_TRY(gb::launch_observe(p, (cudaStream_t)stream));
     return 0;
 }
@@ -598,7 +623,9 @@ int goib2d_raycast(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, v
     if (rc) return rc;
     if (body < 0 || body >= p.B) return fail(GOIB2D_EINVAL, "body %d out of range", body);
     if (n_rays < 0 || (!out && n_worlds && n_rays)) return fail(GOIB2D_EINVAL, "bad ray arguments");
-    p.body = body, p.n_rays = n_rays, p.max_length = max_length, p.out = out;
+    const void *o = nullptr;
+    if ((rc = device_view(out, &o))) return rc;
+    p.body = body, p.n_rays = n_rays, p.max_length = max_length, p.out = (float *)o;
     CUDA_TRY(gb::launch_raycast(p, (cudaStream_t)stream));
     return 0;
 }

@@ -92,8 +92,9 @@ class Engine:
         ss = self._settings[1]
         act = None
         if actions is not None:
-            if not (isinstance(actions, torch.Tensor) and actions.is_cuda and actions.dtype == torch.float32):
-                raise TypeError("actions must be a float32 cuda tensor (N, n_action)")
+            if not (isinstance(actions, torch.Tensor) and actions.dtype == torch.float32 and
+                    (actions.is_cuda or actions.is_pinned())):
+                raise TypeError("actions must be a float32 tensor (N, n_action) on the device or in pinned host memory")
             if tuple(actions.shape) != (n, self.n_action) or not actions.is_contiguous():
                 raise ValueError(f"actions must be contiguous ({n}, {self.n_action})")
             act = actions.data_ptr()
@@ -130,7 +131,8 @@ class Engine:
         return state
 
     def observe(self, state, bodies, out=None):
-        """(N, len(bodies), 6) float32: c.x, c.y, angle, v.x, v.y, w of the given bodies."""
+        """(N, len(bodies), 6) float32: c.x, c.y, angle, v.x, v.y, w of the given bodies. out may be a pinned host
+        tensor: the kernel writes it directly (synchronise the stream before reading it)."""
         n, C_, rows, device, ptrs = self._bind(state)
         b = np.ascontiguousarray(bodies, np.int32)
         if out is None:

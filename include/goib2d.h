@@ -121,8 +121,9 @@ int goib2d_model_set_action_map(goib2d_model *model, int32_t n, const int32_t *j
 
 /* Step n_worlds worlds n_steps times: b2World::Step (reference step.py:28-47) per world, in place on the State
  * leaves (device pointers, leaves[GOIB2D_NUM_LEAVES]). contact_capacity = C, fixture_rows = F (full layout) or the
- * number of non-static fixtures (compact). actions: NULL, or device float32 [n_worlds][n_action] used before every
- * step (goib2d_model_set_action_map). stream: a cudaStream_t (NULL = the legacy default stream). Asynchronous:
+ * number of non-static fixtures (compact). actions: NULL, or float32 [n_worlds][n_action] used before every
+ * step (goib2d_model_set_action_map), in device memory or in page-locked host memory (read by the kernel over the
+ * bus: no separate copy). stream: a cudaStream_t (NULL = the legacy default stream). Asynchronous:
  * returns after enqueueing the launches on `stream`. */
 int goib2d_step(goib2d_model *model, const goib2d_settings *settings, float dt, int32_t contact_capacity,
                 int32_t fixture_rows, int64_t n_worlds, int32_t n_steps, void *const *leaves, const float *actions,
@@ -155,13 +156,14 @@ int goib2d_reset_below(goib2d_model *model, int32_t contact_capacity, int32_t fi
                        void *const *leaves, void *const *init_leaves, int32_t body, float y_min, int32_t *reset_count,
                        void *stream);
 
-/* Observations: out (device float32 [n_worlds][n_bodies][6]) = c.x, c.y, angle, v.x, v.y, w of bodies[k] (host
- * int32 [n_bodies], at most 16). */
+/* Observations: out (float32 [n_worlds][n_bodies][6], device or page-locked host memory, written by the kernel)
+ * = c.x, c.y, angle, v.x, v.y, w of bodies[k] (host int32 [n_bodies], at most 16). */
 int goib2d_observe(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
                    void *const *leaves, int32_t n_bodies, const int32_t *bodies, float *out, void *stream);
 
 /* Ray casts against the static level: ray k of world w leaves body `body`'s centre of mass in direction
- * 2 pi k / n_rays (world frame) for max_length; out (device float32 [n_worlds][n_rays]) = the nearest hit fraction
+ * 2 pi k / n_rays (world frame) for max_length; out (float32 [n_worlds][n_rays], device or page-locked host
+ * memory) = the nearest hit fraction
  * over the fixtures of static bodies (b2RayCastOutput::fraction; 1 = no hit). */
 int goib2d_raycast(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
                    void *const *leaves, int32_t body, int32_t n_rays, float max_length, float *out, void *stream);

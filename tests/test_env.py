@@ -84,3 +84,29 @@ def test_gpu_resets_restore_the_initial_rows():
     for a, b, h in zip(state_leaves(got), state_leaves(before), state_leaves(host)):
         assert np.array_equal(np.asarray(a)[fell], np.asarray(h)[fell])
         assert np.array_equal(np.asarray(a)[~fell], np.asarray(b)[~fell])
+
+
+@pytest.mark.gpu
+def test_gpu_pinned_host_buffers_equal_device_buffers():
+    """Actions read from pinned host memory and observations written into it by the kernels (no separate copy) give
+    the same results as device buffers."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from goib2d import api, configs
+    from goib2d.world import state_leaves
+    sc, model, host = configs.batch("c1", 128)
+    eng = api.Engine(model, host.bodies.type.shape[1], sc.action_joints, sc.action_scale)
+    a = torch.from_numpy(np.random.default_rng(4).uniform(-2, 2, (5, 128, 2)).astype(np.float32))
+    d1, d2 = api.to_device(host), api.to_device(host)
+    a_pin = a.pin_memory()
+    for k in range(5):
+        eng.step_(d1, sc.settings, 0.02, 1, a[k].cuda())
+        eng.step_(d2, sc.settings, 0.02, 1, a_pin[k])
+    for x, y in zip(state_leaves(api.to_host(d1)), state_leaves(api.to_host(d2))):
+        assert np.array_equal(np.asarray(x), np.asarray(y))
+    out = torch.empty((128, 2, 6), dtype=torch.float32).pin_memory()
+    eng.observe(d2, [1, 3], out=out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.numpy(), eng.observe(d2, [1, 3]).cpu().numpy())
+    with pytest.raises(RuntimeError):  # pageable host memory cannot be read by a kernel
+        eng.observe(d2, [1], out=torch.empty((128, 1, 6), dtype=torch.float32))
