@@ -84,6 +84,19 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);
+    // the fused solve kernel's shared-memory region: small, so that 7 blocks of 4 warps per SM keep most of the
+    // L1 cache the arena and the State go through
+#ifndef GOIB2D_SM_WARP_BYTES
+#define GOIB2D_SM_WARP_BYTES 2048
+#endif
+    const int budget = GOIB2D_SM_WARP_BYTES, bp = (B + 3) & ~3;
+    const int fixed = 12 * 4 * bp + (int)sizeof(gb::JRow) * J;
+    if (fixed <= budget) {
+        int cap = (budget - fixed) / (int)sizeof(gb::VCRow);
+        cap = cap < C ? cap : C;
+        L.sm_bpad = bp, L.sm_jr = 12 * 4 * bp, L.sm_vc = fixed, L.sm_vc_cap = cap;
+        L.sm_bytes = (fixed + (int)sizeof(gb::VCRow) * cap + 15) & ~15;
+    }
     return L;
 }
 

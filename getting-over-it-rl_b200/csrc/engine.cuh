@@ -110,6 +110,10 @@ struct Layout {
     int64_t bitmap;
     int64_t hits;  // [max_hits] new-pair candidates of the grid path
     int64_t stride;  // bytes per world (multiple of 256)
+    // The fused solve kernel's shared-memory region, sm_bytes per warp (0: none): the body arrays (9 x sm_bpad
+    // floats), the position iterations' island flags (3 x sm_bpad), the joint rows at sm_jr, up to sm_vc_cap contact
+    // rows at sm_vc (see IslandWork in step.cu)
+    int sm_bytes, sm_bpad, sm_jr, sm_vc, sm_vc_cap;
 };
 
 struct StepParams {

@@ -488,8 +488,40 @@ __device__ __forceinline__ Bodies bodies_of(Ctx &x) {
             sp<float>(x.scr, L.qa)};
 }
 
+// Where the island solve keeps its working set: the body arrays, the per-island flags of the position iterations,
+// the joint rows and the contact rows. In the world's arena, or (the fused solve kernel) in the warp's region of
+// shared memory: the Gauss-Seidel sweeps store a body's velocity and read it back in the next constraint, which
+// through global memory is a ~680-cycle round trip on this part (stores do not stay in L1) and through shared
+// memory ~30. Islands with more contact rows than the region holds keep those rows in the arena.
+struct IslandWork {
+    Bodies bd;
+    int *done, *jok;
+    float *minsep;
+    VCRow *vc;
+    JRow *jr;
+};
+__device__ __forceinline__ IslandWork sweep_arena(char *scr, const Layout &L) {
+    return {{sp<float>(scr, L.vx), sp<float>(scr, L.vy), sp<float>(scr, L.vw), sp<float>(scr, L.cx),
+             sp<float>(scr, L.cy), sp<float>(scr, L.ca), sp<float>(scr, L.qc), sp<float>(scr, L.qs),
+             sp<float>(scr, L.qa)},
+            sp<int>(scr, L.done), sp<int>(scr, L.jok), sp<float>(scr, L.minsep), sp<VCRow>(scr, L.vc),
+            sp<JRow>(scr, L.jr)};
+}
+__device__ __forceinline__ IslandWork sweep_shared(char *scr, const Layout &L, int n_contacts) {
+    extern __shared__ __align__(16) char dyn_smem[];
+    char *base = dyn_smem + (threadIdx.x >> 5) * L.sm_bytes;
+    float *f = reinterpret_cast<float *>(base);
+    const int bp = L.sm_bpad;
+    int *flags = reinterpret_cast<int *>(f + 9 * bp);
+    return {{f, f + bp, f + 2 * bp, f + 3 * bp, f + 4 * bp, f + 5 * bp, f + 6 * bp, f + 7 * bp, f + 8 * bp},
+            flags, flags + bp, reinterpret_cast<float *>(flags + 2 * bp),
+            n_contacts <= L.sm_vc_cap ? reinterpret_cast<VCRow *>(base + L.sm_vc) : sp<VCRow>(scr, L.vc),
+            reinterpret_cast<JRow *>(base + L.sm_jr)};
+}
+
 // ---------------------------------------------------------------- b2World::Solve (step.py:73-194)
-__device__ void solve(Ctx &x, float dt, float dt_ratio) {
+// shared: the working set may live in this warp's shared-memory region (the fused solve kernel only)
+__device__ IslandWork solve(Ctx &x, float dt, float dt_ratio, bool shared) {
     const DevModel &m = x.m;
     const goib2d_settings &s = x.s;
     W &w = x.w;
@@ -498,12 +530,11 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
     IslandOut isl = find_islands(x);
     GB_PHASE(x, 2);
     int *bisl = sp<int>(x.scr, L.bisl), *corder = sp<int>(x.scr, L.corder), *cisl = sp<int>(x.scr, L.cisl);
-    int *jorder = sp<int>(x.scr, L.jorder), *jisl = sp<int>(x.scr, L.jisl);
-    int *done = sp<int>(x.scr, L.done), *jok = sp<int>(x.scr, L.jok), *moved = sp<int>(x.scr, L.moved);
-    float *minsep = sp<float>(x.scr, L.minsep);
-    VCRow *vc = sp<VCRow>(x.scr, L.vc);
-    JRow *jr = sp<JRow>(x.scr, L.jr);
-    Bodies bd = bodies_of(x);
+    int *jorder = sp<int>(x.scr, L.jorder);
+    const IslandWork sw = shared && L.sm_bytes ? sweep_shared(x.scr, L, isl.n_contacts) : sweep_arena(x.scr, L);
+    const Bodies &bd = sw.bd;
+    VCRow *vc = sw.vc;
+    JRow *jr = sw.jr;
     const float h = dt;
     const float gx = w.gravity[0], gy = w.gravity[1];
     for (int b = lane; b < B; b += 32) {  // integrate velocities (step.py:83-100)
@@ -538,13 +569,14 @@ __device__ void solve(Ctx &x, float dt, float dt_ratio) {
     }
     __syncwarp();
     GB_PHASE(x, 3);
+    return sw;
 }
 
 // The island constraint sweeps of one world (step.py:101-140, 197-251), run by ONE thread: warm start, the
 // velocity iterations, StoreImpulses, position integration and the position iterations with per-island early
 // exit. These loops are sequential within a world, so a warp runs 32 worlds' sweeps side by side (one per lane)
 // rather than one world's on a single lane. Reads the rows solve() prepared in the world's arena.
-__device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t world) {
+__device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t world, const IslandWork &sw) {
     const Layout &L = p.lay;
     const goib2d_settings &s = p.s;
     char *scr = p.scratch + world * L.stride;
@@ -552,13 +584,11 @@ __device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t w
     const int *cnt = sp<int>(scr, L.isl);
     const int n_contacts = cnt[0], n_joints = cnt[1], n_islands = cnt[2];
     int *bisl = sp<int>(scr, L.bisl), *cisl = sp<int>(scr, L.cisl), *jisl = sp<int>(scr, L.jisl);
-    int *done = sp<int>(scr, L.done), *jok = sp<int>(scr, L.jok);
-    float *minsep = sp<float>(scr, L.minsep);
-    VCRow *vc = sp<VCRow>(scr, L.vc);
-    JRow *jr = sp<JRow>(scr, L.jr);
-    const Bodies bd{sp<float>(scr, L.vx), sp<float>(scr, L.vy), sp<float>(scr, L.vw), sp<float>(scr, L.cx),
-                    sp<float>(scr, L.cy), sp<float>(scr, L.ca), sp<float>(scr, L.qc), sp<float>(scr, L.qs),
-                    sp<float>(scr, L.qa)};
+    int *done = sw.done, *jok = sw.jok;
+    float *minsep = sw.minsep;
+    VCRow *vc = sw.vc;
+    JRow *jr = sw.jr;
+    const Bodies &bd = sw.bd;
     const bool warm = s.warm_starting, v24 = s.revolute_v24;
     if (warm)
         for (int k = 0; k < n_contacts; ++k) contact_warm_start(vc[k], bd);
@@ -629,7 +659,7 @@ __device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t w
 }
 
 // b2World::Solve after the sweeps (step.py:141-194): write back, sleep, the moved bodies
-__device__ void solve_finish(Ctx &x, float dt) {
+__device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
     const DevModel &m = x.m;
     const goib2d_settings &s = x.s;
     W &w = x.w;
@@ -637,8 +667,9 @@ __device__ void solve_finish(Ctx &x, float dt) {
     const Layout &L = x.p.lay;
     const float h = dt;
     int *bisl = sp<int>(x.scr, L.bisl), *cisl = sp<int>(x.scr, L.cisl), *jisl = sp<int>(x.scr, L.jisl);
-    int *done = sp<int>(x.scr, L.done), *moved = sp<int>(x.scr, L.moved);
-    Bodies bd = bodies_of(x);
+    int *moved = sp<int>(x.scr, L.moved);
+    const int *done = sw.done;
+    const Bodies &bd = sw.bd;
     for (int b = lane; b < B; b += 32) {  // write back + SynchronizeTransform (step.py:141-151)
         if (bisl[b] < 0) continue;
         w.c[2 * b] = bd.cx[b], w.c[2 * b + 1] = bd.cy[b], w.a[b] = bd.ca[b];
@@ -1093,16 +1124,16 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
         collide(x);
         GB_PHASE(x, 1);
     } else if (PART == 1) {  // the whole of b2World::Solve, the sweeps on lane 0
-        solve(x, dt, *w.inv_dt0 * dt);
-        if (x.lane == 0) solve_constraints(p, world);
+        const IslandWork sw = solve(x, dt, *w.inv_dt0 * dt, true);
+        if (x.lane == 0) solve_constraints(p, world, sw);
         __syncwarp();
         GB_PHASE(x, 5);
-        solve_finish(x, dt);
+        solve_finish(x, dt, sw);
         broadphase(x);
     } else if (PART == 2) {
-        solve(x, dt, *w.inv_dt0 * dt);
+        solve(x, dt, *w.inv_dt0 * dt, false);
     } else if (PART == 3) {
-        solve_finish(x, dt);
+        solve_finish(x, dt, sweep_arena(x.scr, p.lay));
     } else if (PART == 4) {
         broadphase(x);
     } else {
@@ -1152,7 +1183,7 @@ extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
 // one world per THREAD (solve_constraints)
 extern "C" __global__ void __launch_bounds__(32) goib2d_constraints_kernel(const __grid_constant__ StepParams p) {
     const int64_t world = p.world0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (world < p.world_end) solve_constraints(p, world);
+    if (world < p.world_end) solve_constraints(p, world, sweep_arena(p.scratch + world * p.lay.stride, p.lay));
 }
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_finish_kernel(const __grid_constant__ StepParams p) {
@@ -1185,7 +1216,7 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
         p.step = k;
         goib2d_collide_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         if (n < THREAD_SWEEPS_MIN_WORLDS) {
-            goib2d_solve_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+            goib2d_solve_kernel<<<blocks, 32 * wpb, (size_t)wpb * p.lay.sm_bytes, stream>>>(p);
         } else {
             goib2d_solve_rows_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
             goib2d_constraints_kernel<<<(unsigned)((n + 31) / 32), 32, 0, stream>>>(p);
