@@ -65,6 +65,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
         return o;
     };
     const int64_t b4 = 4 * (int64_t)(B > 0 ? B : 1), c4 = 4 * (int64_t)(C > 0 ? C : 1), j4 = 4 * (int64_t)(J > 0 ? J : 1);
+    // the hot part first: the small arrays the sequential phases write and read back (see Layout::hot_end)
     L.vx = take(b4), L.vy = take(b4), L.vw = take(b4), L.cx = take(b4), L.cy = take(b4), L.ca = take(b4);
     L.qc = take(b4), L.qs = take(b4), L.qa = take(b4);
     L.aw = take(b4), L.bisl = take(b4), L.stack = take(b4), L.bflag = take(b4), L.last = take(b4);
@@ -74,28 +75,32 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.order = take(c4), L.lpos = take(c4), L.corder = take(c4), L.cisl = take(c4), L.cflag = take(c4);
     L.freeslot = take(c4), L.active = take(c4), L.over = take(c4), L.edges = take(c4), L.tneed = take(c4);
     L.tisl = take(c4), L.solved = take(c4);
+    L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
+    L.isl = take(16);
+    L.adj_start = take(4 * (int64_t)(B + 1)), L.adj_cur = take(b4), L.adj = take(2 * 8 * (int64_t)(C > 0 ? C : 1));
+#ifndef GOIB2D_HOT_MAX_BYTES
+#define GOIB2D_HOT_MAX_BYTES 6144
+#endif
+    L.hot_end = off <= GOIB2D_HOT_MAX_BYTES ? (int)off : 0;
+    // the cold part: rows, manifolds, records and the broadphase buffers
     L.man = take((int64_t)sizeof(gb::Man) * (C > 0 ? C : 1));
     L.vc = take((int64_t)sizeof(gb::VCRow) * (C > 0 ? C : 1));
     L.rec = take(8 * c4);
     L.jr = take((int64_t)sizeof(gb::JRow) * (J > 0 ? J : 1));
-    L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
-    L.isl = take(16);
-    L.adj_start = take(4 * (int64_t)(B + 1)), L.adj_cur = take(b4), L.adj = take(2 * 8 * (int64_t)(C > 0 ? C : 1));
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);
-    // the fused solve kernel's shared-memory region: small, so that 7 blocks of 4 warps per SM keep most of the
-    // L1 cache the arena and the State go through
-#ifndef GOIB2D_SM_WARP_BYTES
-#define GOIB2D_SM_WARP_BYTES 2048
+    // the fused solve kernel's constraint rows in shared memory (after the hot part): the joint rows and the first
+    // contact rows, within a small budget, so that 7 blocks of 4 warps per SM keep most of the L1 cache
+#ifndef GOIB2D_ROWS_MAX_BYTES
+#define GOIB2D_ROWS_MAX_BYTES 1536
 #endif
-    const int budget = GOIB2D_SM_WARP_BYTES, bp = (B + 3) & ~3;
-    const int fixed = 12 * 4 * bp + (int)sizeof(gb::JRow) * J;
-    if (fixed <= budget) {
-        int cap = (budget - fixed) / (int)sizeof(gb::VCRow);
+    const int jbytes = (int)sizeof(gb::JRow) * J;
+    if (L.hot_end > 0 && jbytes <= GOIB2D_ROWS_MAX_BYTES) {
+        int cap = (GOIB2D_ROWS_MAX_BYTES - jbytes) / (int)sizeof(gb::VCRow);
         cap = cap < C ? cap : C;
-        L.sm_bpad = bp, L.sm_jr = 12 * 4 * bp, L.sm_vc = fixed, L.sm_vc_cap = cap;
-        L.sm_bytes = (fixed + (int)sizeof(gb::VCRow) * cap + 15) & ~15;
+        L.sm_jr = 0, L.sm_vc = jbytes, L.sm_vc_cap = cap;
+        L.rows_bytes = (jbytes + (int)sizeof(gb::VCRow) * cap + 15) & ~15;
     }
     return L;
 }

@@ -110,10 +110,11 @@ struct Layout {
     int64_t bitmap;
     int64_t hits;  // [max_hits] new-pair candidates of the grid path
     int64_t stride;  // bytes per world (multiple of 256)
-    // The fused solve kernel's shared-memory region, sm_bytes per warp (0: none): the body arrays (9 x sm_bpad
-    // floats), the position iterations' island flags (3 x sm_bpad), the joint rows at sm_jr, up to sm_vc_cap contact
-    // rows at sm_vc (see IslandWork in step.cu)
-    int sm_bytes, sm_bpad, sm_jr, sm_vc, sm_vc_cap;
+    // Shared-memory copies (per warp) used by the per-step kernels: the arena's first hot_end bytes - the small
+    // arrays whose writes the sequential phases read back, which through global memory is an L2 round trip each
+    // (0: the arena only) - and, in the fused solve kernel after them, rows_bytes of constraint rows: the joint rows
+    // at sm_jr and up to sm_vc_cap contact rows at sm_vc (see IslandWork in step.cu)
+    int hot_end, rows_bytes, sm_jr, sm_vc, sm_vc_cap;
 };
 
 struct StepParams {

@@ -63,11 +63,19 @@ struct Ctx {
     const DevModel &m;
     const goib2d_settings &s;
     W &w;  // shared memory, one per warp: a per-thread copy would cost 32x its size in local memory
-    char *scr;
+    char *scr;   // the world's arena (global memory)
+    char *hot;   // this warp's shared copy of the arena's hot part (Layout::hot_end), or null
+    char *rows;  // this warp's shared constraint rows (the fused solve kernel), or null
     int lane;
     int status;
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
 };
+
+// An arena array of the world: in the warp's shared memory when the kernel holds the hot part there, else global.
+template <class T>
+__device__ __forceinline__ T *ap(const Ctx &x, int64_t off) {
+    return reinterpret_cast<T *>((x.hot && off < x.p.lay.hot_end ? x.hot : x.scr) + off);
+}
 
 
 __device__ __forceinline__ void wake_body(W &w, int b) {  // b2Body::SetAwake(true)
@@ -170,8 +178,8 @@ __device__ void find_new_contacts(Ctx &x) {
     W &w = x.w;
     const int P = m.P, C = w.C, lane = x.lane;
     if (P == 0) return;
-    uint32_t *bitmap = sp<uint32_t>(x.scr, x.p.lay.bitmap);
-    int *freeslot = sp<int>(x.scr, x.p.lay.freeslot);
+    uint32_t *bitmap = ap<uint32_t>(x, x.p.lay.bitmap);
+    int *freeslot = ap<int>(x, x.p.lay.freeslot);
     const int nw = (P + 31) >> 5;
     for (int i = lane; i < nw; i += 32) bitmap[i] = 0u;
     __syncwarp();
@@ -191,7 +199,7 @@ __device__ void find_new_contacts(Ctx &x) {
     __syncwarp();
     int n_new = -1;
     if (m.grid) {
-        int *hits = sp<int>(x.scr, x.p.lay.hits), *sorted = hits + m.max_hits;
+        int *hits = ap<int>(x, x.p.lay.hits), *sorted = hits + m.max_hits;
         n_new = grid_new_pairs(x, bitmap, hits);
         if (n_new > 0) {  // into candidate order (the hits are distinct), then into the lowest free slots
             for (int i = lane; i < n_new; i += 32) {
@@ -257,9 +265,9 @@ __device__ void collide(Ctx &x) {
     W &w = x.w;
     const int C = w.C, B = w.B, lane = x.lane;
     const Layout &L = x.p.lay;
-    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *active = sp<int>(x.scr, L.active);
-    int *over = sp<int>(x.scr, L.over), *aw = sp<int>(x.scr, L.aw);
-    Man *man = sp<Man>(x.scr, L.man);
+    int *order = ap<int>(x, L.order), *lpos = ap<int>(x, L.lpos), *active = ap<int>(x, L.active);
+    int *over = ap<int>(x, L.over), *aw = ap<int>(x, L.aw);
+    Man *man = ap<Man>(x, L.man);
     int n_live = list_order(x, order, lpos);
     for (int s = lane; s < C; s += 32) {
         active[s] = 0;
@@ -332,12 +340,12 @@ __device__ IslandOut find_islands(Ctx &x) {
     W &w = x.w;
     const int C = w.C, B = w.B, J = w.J, lane = x.lane;
     const Layout &L = x.p.lay;
-    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *edges = sp<int>(x.scr, L.edges);
-    int *corder = sp<int>(x.scr, L.corder), *cisl = sp<int>(x.scr, L.cisl), *cflag = sp<int>(x.scr, L.cflag);
-    int *jorder = sp<int>(x.scr, L.jorder), *jisl = sp<int>(x.scr, L.jisl), *jflag = sp<int>(x.scr, L.jflag);
-    int *bisl = sp<int>(x.scr, L.bisl), *bflag = sp<int>(x.scr, L.bflag), *stack = sp<int>(x.scr, L.stack);
-    int *adj_start = sp<int>(x.scr, L.adj_start), *adj_cur = sp<int>(x.scr, L.adj_cur);
-    int2 *adj = sp<int2>(x.scr, L.adj);
+    int *order = ap<int>(x, L.order), *lpos = ap<int>(x, L.lpos), *edges = ap<int>(x, L.edges);
+    int *corder = ap<int>(x, L.corder), *cisl = ap<int>(x, L.cisl), *cflag = ap<int>(x, L.cflag);
+    int *jorder = ap<int>(x, L.jorder), *jisl = ap<int>(x, L.jisl), *jflag = ap<int>(x, L.jflag);
+    int *bisl = ap<int>(x, L.bisl), *bflag = ap<int>(x, L.bflag), *stack = ap<int>(x, L.stack);
+    int *adj_start = ap<int>(x, L.adj_start), *adj_cur = ap<int>(x, L.adj_cur);
+    int2 *adj = ap<int2>(x, L.adj);
     int n_live = list_order(x, order, lpos);
     for (int s = lane; s < C; s += 32) cisl[s] = -1, cflag[s] = 0;
     for (int j = lane; j < J; j += 32) jisl[j] = -1, jflag[j] = 0;
@@ -483,9 +491,9 @@ __device__ void synchronize_fixtures(Ctx &x, const int *moved, int n_rows) {
 
 __device__ __forceinline__ Bodies bodies_of(Ctx &x) {
     const Layout &L = x.p.lay;
-    return {sp<float>(x.scr, L.vx), sp<float>(x.scr, L.vy), sp<float>(x.scr, L.vw), sp<float>(x.scr, L.cx),
-            sp<float>(x.scr, L.cy), sp<float>(x.scr, L.ca), sp<float>(x.scr, L.qc), sp<float>(x.scr, L.qs),
-            sp<float>(x.scr, L.qa)};
+    return {ap<float>(x, L.vx), ap<float>(x, L.vy), ap<float>(x, L.vw), ap<float>(x, L.cx),
+            ap<float>(x, L.cy), ap<float>(x, L.ca), ap<float>(x, L.qc), ap<float>(x, L.qs),
+            ap<float>(x, L.qa)};
 }
 
 // Where the island solve keeps its working set: the body arrays, the per-island flags of the position iterations,
@@ -500,28 +508,24 @@ struct IslandWork {
     VCRow *vc;
     JRow *jr;
 };
-__device__ __forceinline__ IslandWork sweep_arena(char *scr, const Layout &L) {
+__device__ __forceinline__ IslandWork sweep_arena(char *scr, const Layout &L) {  // global memory (any kernel)
     return {{sp<float>(scr, L.vx), sp<float>(scr, L.vy), sp<float>(scr, L.vw), sp<float>(scr, L.cx),
              sp<float>(scr, L.cy), sp<float>(scr, L.ca), sp<float>(scr, L.qc), sp<float>(scr, L.qs),
              sp<float>(scr, L.qa)},
             sp<int>(scr, L.done), sp<int>(scr, L.jok), sp<float>(scr, L.minsep), sp<VCRow>(scr, L.vc),
             sp<JRow>(scr, L.jr)};
 }
-__device__ __forceinline__ IslandWork sweep_shared(char *scr, const Layout &L, int n_contacts) {
-    extern __shared__ __align__(16) char dyn_smem[];
-    char *base = dyn_smem + (threadIdx.x >> 5) * L.sm_bytes;
-    float *f = reinterpret_cast<float *>(base);
-    const int bp = L.sm_bpad;
-    int *flags = reinterpret_cast<int *>(f + 9 * bp);
-    return {{f, f + bp, f + 2 * bp, f + 3 * bp, f + 4 * bp, f + 5 * bp, f + 6 * bp, f + 7 * bp, f + 8 * bp},
-            flags, flags + bp, reinterpret_cast<float *>(flags + 2 * bp),
-            n_contacts <= L.sm_vc_cap ? reinterpret_cast<VCRow *>(base + L.sm_vc) : sp<VCRow>(scr, L.vc),
-            reinterpret_cast<JRow *>(base + L.sm_jr)};
+__device__ __forceinline__ IslandWork sweep_of(const Ctx &x, int n_contacts) {  // the kernel's own placement
+    const Layout &L = x.p.lay;
+    return {{ap<float>(x, L.vx), ap<float>(x, L.vy), ap<float>(x, L.vw), ap<float>(x, L.cx), ap<float>(x, L.cy),
+             ap<float>(x, L.ca), ap<float>(x, L.qc), ap<float>(x, L.qs), ap<float>(x, L.qa)},
+            ap<int>(x, L.done), ap<int>(x, L.jok), ap<float>(x, L.minsep),
+            x.rows && n_contacts <= L.sm_vc_cap ? reinterpret_cast<VCRow *>(x.rows + L.sm_vc) : ap<VCRow>(x, L.vc),
+            x.rows ? reinterpret_cast<JRow *>(x.rows + L.sm_jr) : ap<JRow>(x, L.jr)};
 }
 
 // ---------------------------------------------------------------- b2World::Solve (step.py:73-194)
-// shared: the working set may live in this warp's shared-memory region (the fused solve kernel only)
-__device__ IslandWork solve(Ctx &x, float dt, float dt_ratio, bool shared) {
+__device__ IslandWork solve(Ctx &x, float dt, float dt_ratio) {
     const DevModel &m = x.m;
     const goib2d_settings &s = x.s;
     W &w = x.w;
@@ -529,9 +533,9 @@ __device__ IslandWork solve(Ctx &x, float dt, float dt_ratio, bool shared) {
     const Layout &L = x.p.lay;
     IslandOut isl = find_islands(x);
     GB_PHASE(x, 2);
-    int *bisl = sp<int>(x.scr, L.bisl), *corder = sp<int>(x.scr, L.corder), *cisl = sp<int>(x.scr, L.cisl);
-    int *jorder = sp<int>(x.scr, L.jorder);
-    const IslandWork sw = shared && L.sm_bytes ? sweep_shared(x.scr, L, isl.n_contacts) : sweep_arena(x.scr, L);
+    int *bisl = ap<int>(x, L.bisl), *corder = ap<int>(x, L.corder), *cisl = ap<int>(x, L.cisl);
+    int *jorder = ap<int>(x, L.jorder);
+    const IslandWork sw = sweep_of(x, isl.n_contacts);
     const Bodies &bd = sw.bd;
     VCRow *vc = sw.vc;
     JRow *jr = sw.jr;
@@ -564,7 +568,7 @@ __device__ IslandWork solve(Ctx &x, float dt, float dt_ratio, bool shared) {
     __syncwarp();
     GB_PHASE(x, 3);
     if (lane == 0) {  // the island counts, for the constraint sweeps (solve_constraints)
-        int *cnt = sp<int>(x.scr, L.isl);
+        int *cnt = ap<int>(x, L.isl);
         cnt[0] = isl.n_contacts, cnt[1] = isl.n_joints, cnt[2] = isl.n_islands;
     }
     __syncwarp();
@@ -576,14 +580,16 @@ __device__ IslandWork solve(Ctx &x, float dt, float dt_ratio, bool shared) {
 // velocity iterations, StoreImpulses, position integration and the position iterations with per-island early
 // exit. These loops are sequential within a world, so a warp runs 32 worlds' sweeps side by side (one per lane)
 // rather than one world's on a single lane. Reads the rows solve() prepared in the world's arena.
-__device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t world, const IslandWork &sw) {
-    const Layout &L = p.lay;
+// The island's arrays the sweeps read (counts, island ids), wherever the calling kernel keeps them.
+struct IslandIds {
+    const int *cnt, *bisl, *cisl, *jisl;
+};
+__device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t world, const IslandWork &sw,
+                                                  const IslandIds &ids) {
     const goib2d_settings &s = p.s;
-    char *scr = p.scratch + world * L.stride;
     const int B = p.m.B, C = p.C, J = p.m.J;
-    const int *cnt = sp<int>(scr, L.isl);
-    const int n_contacts = cnt[0], n_joints = cnt[1], n_islands = cnt[2];
-    int *bisl = sp<int>(scr, L.bisl), *cisl = sp<int>(scr, L.cisl), *jisl = sp<int>(scr, L.jisl);
+    const int n_contacts = ids.cnt[0], n_joints = ids.cnt[1], n_islands = ids.cnt[2];
+    const int *bisl = ids.bisl, *cisl = ids.cisl, *jisl = ids.jisl;
     int *done = sw.done, *jok = sw.jok;
     float *minsep = sw.minsep;
     VCRow *vc = sw.vc;
@@ -666,8 +672,8 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
     const int B = w.B, C = w.C, J = w.J, lane = x.lane;
     const Layout &L = x.p.lay;
     const float h = dt;
-    int *bisl = sp<int>(x.scr, L.bisl), *cisl = sp<int>(x.scr, L.cisl), *jisl = sp<int>(x.scr, L.jisl);
-    int *moved = sp<int>(x.scr, L.moved);
+    int *bisl = ap<int>(x, L.bisl), *cisl = ap<int>(x, L.cisl), *jisl = ap<int>(x, L.jisl);
+    int *moved = ap<int>(x, L.moved);
     const int *done = sw.done;
     const Bodies &bd = sw.bd;
     for (int b = lane; b < B; b += 32) {  // write back + SynchronizeTransform (step.py:141-151)
@@ -678,8 +684,8 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
         w.xf_p[2 * b] = xf.p.x, w.xf_p[2 * b + 1] = xf.p.y, w.xf_q[2 * b] = xf.q.c, w.xf_q[2 * b + 1] = xf.q.s;
     }
     __syncwarp();
-    int *islsleep = sp<int>(x.scr, L.islsleep), *last = sp<int>(x.scr, L.last);
-    float *minst = sp<float>(x.scr, L.minst), *st = sp<float>(x.scr, L.st);
+    int *islsleep = ap<int>(x, L.islsleep), *last = ap<int>(x, L.last);
+    float *minst = ap<float>(x, L.minst), *st = ap<float>(x, L.st);
     if (lane == 0) {  // sleep per island (step.py:153-171), static bodies' awake flag (step.py:173-194)
         for (int i = 0; i < B; ++i) islsleep[i] = 0;
         if (s.allow_sleep) {
@@ -729,7 +735,7 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
 
 // the end of b2World::Solve: SynchronizeFixtures of the moved bodies, then FindNewContacts (step.py:185-194)
 __device__ void broadphase(Ctx &x) {
-    synchronize_fixtures(x, sp<int>(x.scr, x.p.lay.moved), x.w.rows);
+    synchronize_fixtures(x, ap<int>(x, x.p.lay.moved), x.w.rows);
     GB_PHASE(x, 7);
     find_new_contacts(x);
     GB_PHASE(x, 8);
@@ -758,8 +764,8 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
     W &w = x.w;
     const int lane = x.lane;
     const Layout &L = x.p.lay;
-    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *tneed = sp<int>(x.scr, L.tneed);
-    float *rec = sp<float>(x.scr, L.rec);
+    int *order = ap<int>(x, L.order), *lpos = ap<int>(x, L.lpos), *tneed = ap<int>(x, L.tneed);
+    float *rec = ap<float>(x, L.rec);
     int n_live = list_order(x, order, lpos);
     // Sweep alignment in list order (toi.py:500-536): a candidate whose bodies' sweeps sit at different alpha0
     // advances the one behind, which every later candidate of that body sees. Between two advances nothing moves, so
@@ -861,13 +867,13 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     W &w = x.w;
     const int B = w.B, C = w.C, lane = x.lane;
     const Layout &L = x.p.lay;
-    int *order = sp<int>(x.scr, L.order), *lpos = sp<int>(x.scr, L.lpos), *tisl = sp<int>(x.scr, L.tisl);
-    int *flip_b = sp<int>(x.scr, L.aw), *in_other = sp<int>(x.scr, L.bflag), *touched = sp<int>(x.scr, L.stack);
-    int *newbody = sp<int>(x.scr, L.last), *moved = sp<int>(x.scr, L.moved), *solved = sp<int>(x.scr, L.solved);
-    int *old_pair = sp<int>(x.scr, L.cflag), *old_key = sp<int>(x.scr, L.active);
-    float *adv = sp<float>(x.scr, L.adv);
-    Man *man = sp<Man>(x.scr, L.man);
-    VCRow *vc = sp<VCRow>(x.scr, L.vc);
+    int *order = ap<int>(x, L.order), *lpos = ap<int>(x, L.lpos), *tisl = ap<int>(x, L.tisl);
+    int *flip_b = ap<int>(x, L.aw), *in_other = ap<int>(x, L.bflag), *touched = ap<int>(x, L.stack);
+    int *newbody = ap<int>(x, L.last), *moved = ap<int>(x, L.moved), *solved = ap<int>(x, L.solved);
+    int *old_pair = ap<int>(x, L.cflag), *old_key = ap<int>(x, L.active);
+    float *adv = ap<float>(x, L.adv);
+    Man *man = ap<Man>(x, L.man);
+    VCRow *vc = ap<VCRow>(x, L.vc);
     Bodies bd = bodies_of(x);
     const int A = m.fixture_body[w.fa[min_slot]], Bb = m.fixture_body[w.fb[min_slot]];
 #ifdef GOIB2D_PHASE_TIMERS
@@ -1108,7 +1114,14 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     __shared__ W s_world[4];  // blockDim.x <= 128
     if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
-    Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, (int)(threadIdx.x & 31), 0, clock64()};
+    // the per-step kernels (collide, fused solve, TOI) keep the arena's hot part in shared memory: every arena array
+    // they use is written and read within the kernel; the large-batch split solve passes arrays between kernels
+    extern __shared__ __align__(16) char dyn_smem[];
+    const bool hot = (PART == 0 || PART == 1 || PART == 5) && p.lay.hot_end > 0;
+    const int region = hot ? p.lay.hot_end + (PART == 1 ? p.lay.rows_bytes : 0) : 0;
+    char *mine = dyn_smem + warp * region;
+    Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
+          hot && PART == 1 && p.lay.rows_bytes ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64()};
     W &w = x.w;
     const float dt = p.dt;
     if (PART == 0) {
@@ -1124,16 +1137,19 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
         collide(x);
         GB_PHASE(x, 1);
     } else if (PART == 1) {  // the whole of b2World::Solve, the sweeps on lane 0
-        const IslandWork sw = solve(x, dt, *w.inv_dt0 * dt, true);
-        if (x.lane == 0) solve_constraints(p, world, sw);
+        const IslandWork sw = solve(x, dt, *w.inv_dt0 * dt);
+        if (x.lane == 0)
+            solve_constraints(p, world, sw,
+                              {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
+                               ap<int>(x, p.lay.jisl)});
         __syncwarp();
         GB_PHASE(x, 5);
         solve_finish(x, dt, sw);
         broadphase(x);
     } else if (PART == 2) {
-        solve(x, dt, *w.inv_dt0 * dt, false);
+        solve(x, dt, *w.inv_dt0 * dt);
     } else if (PART == 3) {
-        solve_finish(x, dt, sweep_arena(x.scr, p.lay));
+        solve_finish(x, dt, sweep_of(x, 0));
     } else if (PART == 4) {
         broadphase(x);
     } else {
@@ -1183,7 +1199,11 @@ extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
 // one world per THREAD (solve_constraints)
 extern "C" __global__ void __launch_bounds__(32) goib2d_constraints_kernel(const __grid_constant__ StepParams p) {
     const int64_t world = p.world0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (world < p.world_end) solve_constraints(p, world, sweep_arena(p.scratch + world * p.lay.stride, p.lay));
+    if (world >= p.world_end) return;
+    char *scr = p.scratch + world * p.lay.stride;
+    const Layout &L = p.lay;
+    solve_constraints(p, world, sweep_arena(scr, L),
+                      {sp<int>(scr, L.isl), sp<int>(scr, L.bisl), sp<int>(scr, L.cisl), sp<int>(scr, L.jisl)});
 }
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_finish_kernel(const __grid_constant__ StepParams p) {
@@ -1212,18 +1232,19 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     p.world0 = 0, p.world_end = p.n_worlds;
     const int64_t n = p.n_worlds;
     const unsigned blocks = (unsigned)((n + wpb - 1) / wpb);
+    const size_t hot = (size_t)wpb * p.lay.hot_end;  // dynamic shared memory of the per-step kernels
     for (int k = 0; k < p.n_steps; ++k) {
         p.step = k;
-        goib2d_collide_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        goib2d_collide_kernel<<<blocks, 32 * wpb, hot, stream>>>(p);
         if (n < THREAD_SWEEPS_MIN_WORLDS) {
-            goib2d_solve_kernel<<<blocks, 32 * wpb, (size_t)wpb * p.lay.sm_bytes, stream>>>(p);
+            goib2d_solve_kernel<<<blocks, 32 * wpb, hot + (size_t)wpb * p.lay.rows_bytes, stream>>>(p);
         } else {
             goib2d_solve_rows_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
             goib2d_constraints_kernel<<<(unsigned)((n + 31) / 32), 32, 0, stream>>>(p);
             goib2d_finish_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
             goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         }
-        goib2d_toi_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        goib2d_toi_kernel<<<blocks, 32 * wpb, hot, stream>>>(p);
     }
     return cudaGetLastError();
 }
