@@ -18,6 +18,8 @@ int kernels_per_step(int64_t n_worlds);                       // step.cu
 cudaError_t launch_reset(const EnvParams &p, cudaStream_t s);    // env.cuh (compiled in step.cu)
 cudaError_t launch_observe(const EnvParams &p, cudaStream_t s);  // env.cuh
 cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s);  // env.cuh
+cudaError_t launch_pair_count(const PairScene &s, int64_t *count);                              // scene.cuh
+cudaError_t launch_pair_fill(const PairScene &s, const int64_t *start, int32_t *pa, int32_t *pb);  // scene.cuh
 }
 
 namespace {
@@ -645,6 +647,72 @@ int goib2d_raycast(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, v
     if ((rc = device_view(out, &o))) return rc;
     p.body = body, p.n_rays = n_rays, p.max_length = max_length, p.out = (float *)o;
     CUDA_TRY(gb::launch_raycast(p, (cudaStream_t)stream));
+    return 0;
+}
+
+int goib2d_candidate_pairs(const goib2d_pair_desc *d, int32_t *pair_a, int32_t *pair_b, int64_t capacity,
+                           int64_t *n_pairs) {
+    if (!d || !n_pairs) return fail(GOIB2D_EINVAL, "null argument");
+    *n_pairs = 0;
+    const int B = d->n_bodies, F = d->n_fixtures, J = d->n_joints;
+    if (B < 0 || F < 0 || J < 0 || capacity < 0) return fail(GOIB2D_EINVAL, "negative size");
+    if (F && (!d->fixture_body || !d->shape_type || !d->sensor || !d->category || !d->mask || !d->group || !d->layer))
+        return fail(GOIB2D_EINVAL, "null fixture array");
+    if ((B && !d->body_type) || (J && (!d->joint_a || !d->joint_b || !d->joint_collide)))
+        return fail(GOIB2D_EINVAL, "null body or joint array");
+    for (int f = 0; f < F; ++f)
+        if (d->fixture_body[f] < 0 || d->fixture_body[f] >= B) return fail(GOIB2D_EINVAL, "fixture %d body", f);
+    std::vector<int64_t> keys;  // bodies joined without collideConnected
+    for (int j = 0; j < J; ++j) {
+        int a = d->joint_a[j], b = d->joint_b[j];
+        if (a < 0 || a >= B || b < 0 || b >= B) return fail(GOIB2D_EINVAL, "joint %d bodies", j);
+        if (!d->joint_collide[j]) keys.push_back(a < b ? ((int64_t)a << 32) | b : ((int64_t)b << 32) | a);
+    }
+    std::sort(keys.begin(), keys.end());
+    keys.erase(std::unique(keys.begin(), keys.end()), keys.end());
+    if (F == 0) return 0;
+    std::vector<void *> tmp;
+    struct Free {
+        std::vector<void *> &v;
+        ~Free() {
+            for (void *p : v) cudaFree(p);
+        }
+    } release{tmp};
+    gb::PairScene s{};
+    s.F = F, s.J = J, s.n_no_collide = (int)keys.size();
+    int rc = 0;
+    rc = rc ? rc : upload(tmp, d->fixture_body, (size_t)F, &s.fixture_body);
+    rc = rc ? rc : upload(tmp, d->shape_type, (size_t)F, &s.shape_type);
+    rc = rc ? rc : upload(tmp, d->body_type, (size_t)B, &s.body_type);
+    rc = rc ? rc : upload(tmp, d->sensor, (size_t)F, &s.sensor);
+    rc = rc ? rc : upload(tmp, d->category, (size_t)F, &s.category);
+    rc = rc ? rc : upload(tmp, d->mask, (size_t)F, &s.mask);
+    rc = rc ? rc : upload(tmp, d->group, (size_t)F, &s.group);
+    rc = rc ? rc : upload(tmp, d->layer, (size_t)F, &s.layer);
+    rc = rc ? rc : upload(tmp, (const int64_t *)keys.data(), keys.size(), &s.no_collide);
+    if (!rc && d->layer_masks) rc = upload(tmp, d->layer_masks, 32, &s.layer_masks);
+    if (rc) return rc;
+    const int64_t *count_c = nullptr;
+    if ((rc = upload<int64_t>(tmp, nullptr, (size_t)F, &count_c))) return rc;
+    int64_t *count = const_cast<int64_t *>(count_c);
+    CUDA_TRY(gb::launch_pair_count(s, count));
+    std::vector<int64_t> start((size_t)F + 1, 0);
+    CUDA_TRY(cudaMemcpy(start.data() + 1, count, sizeof(int64_t) * F, cudaMemcpyDeviceToHost));
+    for (int f = 0; f < F; ++f) start[f + 1] += start[f];
+    *n_pairs = start[F];
+    if (start[F] > capacity) return fail(GOIB2D_ELIMIT, "%lld candidate pairs, capacity %lld", (long long)start[F],
+                                         (long long)capacity);
+    if (start[F] == 0) return 0;
+    if (!pair_a || !pair_b) return fail(GOIB2D_EINVAL, "null output");
+    const int64_t *d_start = nullptr;
+    const int32_t *d_pa = nullptr, *d_pb = nullptr;
+    rc = rc ? rc : upload(tmp, start.data(), (size_t)F, &d_start);
+    rc = rc ? rc : upload<int32_t>(tmp, nullptr, (size_t)start[F], &d_pa);
+    rc = rc ? rc : upload<int32_t>(tmp, nullptr, (size_t)start[F], &d_pb);
+    if (rc) return rc;
+    CUDA_TRY(gb::launch_pair_fill(s, d_start, const_cast<int32_t *>(d_pa), const_cast<int32_t *>(d_pb)));
+    CUDA_TRY(cudaMemcpy(pair_a, d_pa, sizeof(int32_t) * start[F], cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(pair_b, d_pb, sizeof(int32_t) * start[F], cudaMemcpyDeviceToHost));
     return 0;
 }
 

@@ -156,6 +156,17 @@ struct EnvParams {
     float max_length;
 };
 
+// The scene given to the candidate-pair build (scene.cuh), device arrays.
+struct PairScene {
+    int F, J;
+    const int32_t *fixture_body, *shape_type, *body_type;
+    const uint8_t *sensor;
+    const int32_t *category, *mask, *group, *layer;
+    const uint32_t *layer_masks;  // [32] or null
+    const int64_t *no_collide;    // [J] sorted keys (lower body << 32 | higher body) of joints without collideConnected
+    int n_no_collide;
+};
+
 // Status bits (include/goib2d.h goib2d_status)
 enum { ST_OVERFLOW = 1, ST_NONFINITE = 2, ST_CAP = 4, ST_LIMIT = 8 };
 

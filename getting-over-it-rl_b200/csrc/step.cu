@@ -46,6 +46,7 @@ __device__ unsigned long long g_toi_cycles[16];
 #endif
 
 #include "env.cuh"
+#include "scene.cuh"
 #include "solver.cuh"
 #include "toi.cuh"
 

@@ -391,16 +391,26 @@ def scene(name, seed=0, n=None, first=0):
 # ---- batches
 
 
-def batch(name, n, seed=0, compact=True, first=0):
+def _cuda():
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except ImportError:
+        return False
+
+
+def batch(name, n, seed=0, compact=True, first=0, device_pairs=None):
     """(scene, Model, batched State (leaves (n, ...))) for n worlds of a workload. The Model comes from world 0's
     full build; each world's bodies, joints and dynamic-fixture AABBs come from replaying that world's dynamic
     builder calls on a WorldDef holding only the ground body, so every world equals its full WorldDef build (the
-    static level is identical in all of them). compact: the compact fixture layout (static fixtures in the Model)."""
+    static level is identical in all of them). compact: the compact fixture layout (static fixtures in the Model).
+    device_pairs: build the candidate list on the GPU (default: when CUDA is available)."""
     from .world import Fixtures, State, compact_model, compact_state, empty_contacts, empty_toi
 
     sc = scene(name, seed, n, first)
     full = sc.world_def(0)
-    model, st0 = full.build(sc.capacity)
+    # the candidate list on the GPU when there is one (goib2d_candidate_pairs: the host scan's list, checked equal)
+    model, st0 = full.build(sc.capacity, device_pairs=_cuda() if device_pairs is None else device_pairs)
     n_static = sum(1 for f in full.fixtures if f["body"] == 0)  # the level: fixtures of the ground body
     geom = full.fixture_geometry()
     per = []

@@ -19,6 +19,52 @@ _i = C.POINTER(C.c_int32)
 _u = C.POINTER(C.c_uint8)
 
 
+class PairDesc(C.Structure):
+    _fields_ = [("n_bodies", C.c_int32), ("n_fixtures", C.c_int32), ("n_joints", C.c_int32), ("body_type", _i),
+                ("fixture_body", _i), ("shape_type", _i), ("sensor", _u), ("category", _i), ("mask", _i),
+                ("group", _i), ("layer", _i), ("layer_masks", C.POINTER(C.c_uint32)), ("joint_a", _i),
+                ("joint_b", _i), ("joint_collide", _u)]
+
+
+def candidate_pairs_device(body_type, fixtures, joints, layer_masks=None):
+    """goib2d_candidate_pairs on the current CUDA device: fixtures / joints as the WorldDef dicts; returns the
+    (P, 2) int32 pair list."""
+    lib = load()
+    F, J = len(fixtures), len(joints)
+    keep = []
+
+    def arr(x, dt):
+        a = np.ascontiguousarray(np.asarray(x, dt).reshape(-1))
+        if a.size == 0:
+            a = np.zeros(1, dt)
+        keep.append(a)
+        return a
+    d = PairDesc()
+    d.n_bodies, d.n_fixtures, d.n_joints = len(body_type), F, J
+    d.body_type = arr(body_type, np.int32).ctypes.data_as(_i)
+    d.fixture_body = arr([f["body"] for f in fixtures], np.int32).ctypes.data_as(_i)
+    d.shape_type = arr([f["shape_type"] for f in fixtures], np.int32).ctypes.data_as(_i)
+    d.sensor = arr([f["sensor"] for f in fixtures], np.uint8).ctypes.data_as(_u)
+    d.category = arr([f["category"] for f in fixtures], np.int32).ctypes.data_as(_i)
+    d.mask = arr([f["mask"] for f in fixtures], np.int32).ctypes.data_as(_i)
+    d.group = arr([f["group"] for f in fixtures], np.int32).ctypes.data_as(_i)
+    d.layer = arr([f["layer"] for f in fixtures], np.int32).ctypes.data_as(_i)
+    d.layer_masks = None if layer_masks is None else \
+        arr(np.asarray(layer_masks, np.int64) & 0xFFFFFFFF, np.uint32).ctypes.data_as(C.POINTER(C.c_uint32))
+    d.joint_a = arr([j["a"] for j in joints], np.int32).ctypes.data_as(_i)
+    d.joint_b = arr([j["b"] for j in joints], np.int32).ctypes.data_as(_i)
+    d.joint_collide = arr([j["collide"] for j in joints], np.uint8).ctypes.data_as(_u)
+    n = C.c_int64()
+    rc = lib.goib2d_candidate_pairs(C.byref(d), None, None, 0, C.byref(n))
+    if rc not in (0, -4):
+        check(rc)
+    out = np.zeros((max(n.value, 1), 2), np.int32)
+    pa, pb = np.zeros(max(n.value, 1), np.int32), np.zeros(max(n.value, 1), np.int32)
+    check(lib.goib2d_candidate_pairs(C.byref(d), pa.ctypes.data_as(_i), pb.ctypes.data_as(_i), n.value, C.byref(n)))
+    out[:, 0], out[:, 1] = pa, pb
+    return out[:n.value]
+
+
 class ModelDesc(C.Structure):
     _fields_ = [("n_bodies", C.c_int32), ("n_fixtures", C.c_int32), ("n_joints", C.c_int32), ("n_pairs", C.c_int32),
                 ("fixture_body", _i), ("shape_type", _i), ("count", _i), ("radius", _f), ("verts", _f),
@@ -149,6 +195,7 @@ def load():
         "goib2d_step_noalloc": (C.c_int, [vp, vp, C.c_float, C.c_int32, C.c_int32, C.c_int64, C.c_int32,
                                           C.POINTER(vp), vp, vp]),
         "goib2d_kernels_per_step": (C.c_int, [C.c_int64]),
+        "goib2d_candidate_pairs": (C.c_int, [C.POINTER(PairDesc), _i, _i, C.c_int64, C.POINTER(C.c_int64)]),
         "goib2d_reset_masked": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp), vp, vp]),
         "goib2d_reset_below": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp),
                                          C.c_int32, C.c_float, vp, vp]),

@@ -378,11 +378,16 @@ class WorldDef:
 
     # ---- build
 
-    def candidate_pairs(self):
+    def candidate_pairs(self, device=False):
         """Fixture pairs that can ever touch, in b2BroadPhase::UpdatePairs order (ascending (lower, higher) proxy
         id), polygon first in a polygon-circle pair as b2Contact::Create orders them. Dropped for good: same body,
         both static, joined by a joint without collideConnected, filtered out, or a sensor (reference
-        world.py:308-329)."""
+        world.py:308-329). device=True builds the same list on the GPU (goib2d_candidate_pairs)."""
+        if device:
+            from . import native
+            pairs = native.candidate_pairs_device([b["type"] for b in self.bodies], self.fixtures, self.joints,
+                                                  self.layer_masks)
+            return [(int(a), int(b)) for a, b in pairs]
         no_collide = {frozenset((j["a"], j["b"])) for j in self.joints if not j["collide"]}
         fx, out = self.fixtures, []
         E = shapes.EDGE
@@ -462,12 +467,12 @@ class WorldDef:
             impulse=np.zeros((J, 3), F32), motor_impulse=np.zeros(J, F32), limit_state=np.zeros(J, I32),
             lower_impulse=np.zeros(J, F32), upper_impulse=np.zeros(J, F32))
 
-    def build(self, contact_capacity=16):
+    def build(self, contact_capacity=16, device_pairs=False):
         """(Model, State) as numpy arrays: fat AABBs from b2BroadPhase::CreateProxy (shape AABB at the body
         transform, extended), contacts empty, new_fixture set (reference world.py:331-386)."""
         B, F, J, C = len(self.bodies), len(self.fixtures), len(self.joints), contact_capacity
         js = self.joints
-        pairs = self.candidate_pairs()
+        pairs = self.candidate_pairs(device_pairs)
         bodies = self.body_arrays()
         geom = self.fixture_geometry()
         xaxes, yaxes = [], []

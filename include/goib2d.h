@@ -168,6 +168,25 @@ int goib2d_observe(goib2d_model *model, int32_t contact_capacity, int32_t fixtur
 int goib2d_raycast(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
                    void *const *leaves, int32_t body, int32_t n_rays, float max_length, float *out, void *stream);
 
+/* ---- Scene build on the device. The candidate pairs of a Model (the host builder's O(F^2) scan, goib2d/world.py
+ * WorldDef.candidate_pairs; reference world.py:308-329): every fixture pair (i < k) except same body, a sensor, two
+ * edges, two static bodies, bodies joined without collideConnected, or filtered out (the Unity layer matrix when
+ * layer_masks is given, else Box2D's groups, categories and masks); ordered by i then k, each pair written edge
+ * first, else polygon before circle. Host arrays in and out: *n_pairs = the number of pairs (also when capacity is
+ * too small, then nothing is written and GOIB2D_ELIMIT is returned). */
+typedef struct goib2d_pair_desc {
+    int32_t n_bodies, n_fixtures, n_joints;
+    const int32_t *body_type;                          /* [B] */
+    const int32_t *fixture_body, *shape_type;          /* [F] */
+    const uint8_t *sensor;                             /* [F] */
+    const int32_t *category, *mask, *group, *layer;    /* [F] */
+    const uint32_t *layer_masks;                       /* [32] or NULL */
+    const int32_t *joint_a, *joint_b;                  /* [J] */
+    const uint8_t *joint_collide;                      /* [J] collideConnected */
+} goib2d_pair_desc;
+int goib2d_candidate_pairs(const goib2d_pair_desc *desc, int32_t *pair_a, int32_t *pair_b, int64_t capacity,
+                           int64_t *n_pairs);
+
 /* Bytes of the static scratch arena used by goib2d_step_noalloc (on every device that loads the library). */
 #define GOIB2D_NOALLOC_SCRATCH_BYTES (32u << 20)
 
