@@ -221,6 +221,10 @@ struct goib2d_model {
     int32_t n_action = 0;
     int32_t *action_joint = nullptr;
     float *action_scale = nullptr;
+    int32_t event_cap = 0;  // contact event log per world (0: off)
+    goib2d_event *events = nullptr;
+    int32_t *event_count = nullptr;
+    int64_t event_worlds = 0, event_n = 0;
     std::mutex mu;
 };
 
@@ -390,6 +394,8 @@ int goib2d_model_destroy(goib2d_model *m) {
     if (m->status) cudaFree(m->status);
     if (m->action_joint) cudaFree(m->action_joint);
     if (m->action_scale) cudaFree(m->action_scale);
+    if (m->events) cudaFree(m->events);
+    if (m->event_count) cudaFree(m->event_count);
     delete m;
     return 0;
 }
@@ -452,6 +458,18 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
     }
     m->status_n = n_worlds;
     p.scratch = m->scratch, p.status = m->status;
+    if (m->event_cap > 0) {  // the contact event log
+        if (n_worlds > m->event_worlds) {
+            if (m->events) cudaFree(m->events), m->events = nullptr;
+            if (m->event_count) cudaFree(m->event_count), m->event_count = nullptr;
+            m->event_worlds = 0;
+            CUDA_TRY(cudaMalloc(&m->events, sizeof(goib2d_event) * (size_t)m->event_cap * n_worlds));
+            CUDA_TRY(cudaMalloc(&m->event_count, sizeof(int32_t) * n_worlds));
+            m->event_worlds = n_worlds;
+        }
+        m->event_n = n_worlds;
+        p.events = m->events, p.event_count = m->event_count, p.event_cap = m->event_cap;
+    }
     if (actions && m->n_action > 0) {
         const void *a = nullptr;
         int arc = device_view(actions, &a);
@@ -461,6 +479,36 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
     }
     if ((n_worlds + 3) / 4 > 0x7fffffff) return fail(GOIB2D_ELIMIT, "too many worlds");
     CUDA_TRY(gb::launch_steps(p, (cudaStream_t)stream));
+    return 0;
+}
+
+int goib2d_set_event_log(goib2d_model *m, int32_t capacity) {
+    if (!m) return fail(GOIB2D_EINVAL, "null argument");
+    if (capacity < 0) return fail(GOIB2D_EINVAL, "negative capacity");
+    std::lock_guard<std::mutex> lk(m->mu);
+    if (capacity != m->event_cap) {  // the buffers follow the next step's batch
+        if (m->events) cudaFree(m->events), m->events = nullptr;
+        if (m->event_count) cudaFree(m->event_count), m->event_count = nullptr;
+        m->event_worlds = m->event_n = 0;
+    }
+    m->event_cap = capacity;
+    return 0;
+}
+
+int goib2d_events(goib2d_model *m, const goib2d_event **events, const int32_t **counts, int64_t *n, int32_t *cap) {
+    if (!m || !events || !counts || !n || !cap) return fail(GOIB2D_EINVAL, "null argument");
+    *events = m->events, *counts = m->event_count, *n = m->event_n, *cap = m->event_cap;
+    return 0;
+}
+
+int goib2d_events_copy(goib2d_model *m, goib2d_event *host_events, int32_t *host_counts, int64_t n) {
+    if (!m || ((!host_events || !host_counts) && n)) return fail(GOIB2D_EINVAL, "null argument");
+    if (n > m->event_n) return fail(GOIB2D_EINVAL, "%lld worlds requested, the log holds %lld", (long long)n,
+                                    (long long)m->event_n);
+    if (n == 0 || m->event_cap == 0) return 0;
+    CUDA_TRY(cudaMemcpy(host_events, m->events, sizeof(goib2d_event) * (size_t)m->event_cap * n,
+                        cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(host_counts, m->event_count, sizeof(int32_t) * n, cudaMemcpyDeviceToHost));
     return 0;
 }
 

@@ -135,6 +135,9 @@ struct StepParams {
     char *scratch;
     Layout lay;
     int32_t *status;
+    goib2d_event *events;  // contact event log [n_worlds][event_cap], or null (goib2d_set_event_log)
+    int32_t *event_count;  // [n_worlds]
+    int event_cap;
 };
 
 // Parameters of the env kernels (env.cu): resets, observations, ray casts.

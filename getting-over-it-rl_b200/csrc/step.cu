@@ -70,7 +70,19 @@ struct Ctx {
     int lane;
     int status;
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
+    int64_t world;
 };
+
+// ---- contact event log (the reference C API's Begin / End / PostSolve listener, capi.cpp:45-78)
+enum { EV_BEGIN = 0, EV_END = 1, EV_POST_SOLVE = 2 };
+__device__ __forceinline__ void put_event(const StepParams &p, int64_t world, int idx, int kind, int fa, int fb,
+                                          int count = 0, const float *ni = nullptr, const float *ti = nullptr) {
+    if (idx >= p.event_cap) return;
+    goib2d_event &e = p.events[world * p.event_cap + idx];
+    e.kind = kind, e.fixture_a = fa, e.fixture_b = fb, e.child_a = 0, e.child_b = 0, e.count = count;
+    for (int j = 0; j < 2; ++j)
+        e.normal_impulse[j] = j < count ? ni[j] : 0.0f, e.tangent_impulse[j] = j < count ? ti[j] : 0.0f;
+}
 
 // An arena array of the world: in the warp's shared memory when the kernel holds the hot part there, else global.
 template <class T>
@@ -318,11 +330,26 @@ __device__ void collide(Ctx &x) {
     __syncwarp();
     for (int s = lane; s < C; s += 32) {
         if (!active[s]) continue;
+        int ev = -1;  // the event this update raises
         if (!over[s]) {
+            if (w.touching[s]) ev = EV_END;  // a touching contact destroyed
             w.pair[s] = -1, w.touching[s] = 0, w.count[s] = 0;
-        } else {
-            apply_manifold(w, s, man[s]);
+        } else if (apply_manifold(w, s, man[s])) {
+            ev = w.touching[s] ? EV_BEGIN : EV_END;
         }
+        active[s] = ev + 1;  // reused: the event of each visited slot
+    }
+    if (x.p.events) {  // the step's log starts with Collide's events, in contact-list order
+        __syncwarp();
+        int n = 0;
+        for (int base = 0; base < n_live; base += 32) {
+            int k = base + lane, s = k < n_live ? order[k] : -1;
+            int ev = s >= 0 ? active[s] - 1 : -1;
+            unsigned mk = __ballot_sync(FULL, ev >= 0);
+            if (ev >= 0) put_event(x.p, x.world, n + __popc(mk & ((1u << lane) - 1)), ev, w.fa[s], w.fb[s]);
+            n += __popc(mk);
+        }
+        if (lane == 0) x.p.event_count[x.world] = n;
     }
     for (int b = lane; b < B; b += 32) {
         if (aw[b] && !w.awake[b]) w.sleep_time[b] = 0.0f;
@@ -623,6 +650,16 @@ __device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t w
         motor_impulse[r.jid] = r.mimp;
         limit_state[r.jid] = r.limit_state;
     }
+    if (p.events) {  // b2Island::Report: PostSolve per island contact, in solve order
+        const int32_t *fa = (const int32_t *)p.L.p[GOIB2D_C_FA] + world * C;
+        const int32_t *fb = (const int32_t *)p.L.p[GOIB2D_C_FB] + world * C;
+        const int base = p.event_count[world];
+        for (int k = 0; k < n_contacts; ++k) {
+            const VCRow &c = vc[k];
+            put_event(p, world, base + k, EV_POST_SOLVE, fa[c.slot], fb[c.slot], c.count, c.ni, c.ti);
+        }
+        p.event_count[world] = base + n_contacts;
+    }
     const float h = p.dt;
     const float max_t = s.clamps_per_second ? s.max_translation * h : s.max_translation;
     const float max_r = s.clamps_per_second ? s.max_rotation * h : s.max_rotation;
@@ -902,8 +939,15 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     int n_isl = 0;
     bool t_min = false;
     if (lane == 0) {
+        int ev_n = x.p.events ? x.p.event_count[x.world] : 0;  // b2Contact::Update's Begin / End, in order
+        auto update = [&](int slot) {
+            bool flip = apply_manifold(w, slot, man[slot]);
+            if (flip && x.p.events)
+                put_event(x.p, x.world, ev_n++, w.touching[slot] ? EV_BEGIN : EV_END, w.fa[slot], w.fb[slot]);
+            return flip;
+        };
         t_min = man[min_slot].count > 0;
-        if (apply_manifold(w, min_slot, man[min_slot]))
+        if (update(min_slot))
             flip_b[m.fixture_body[w.fa[min_slot]]] = flip_b[m.fixture_body[w.fb[min_slot]]] = 1;
         w.t_enabled[min_slot] = t_min;
         w.t_count[min_slot] += 1;
@@ -929,7 +973,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                     int other = ca == owner ? cb : ca;
                     if (w.type[other] == DYNAMIC && !w.bullet[owner] && !w.bullet[other]) continue;
                     if (s.unity_toi && !toi_pair_rule(w, owner, other, true)) continue;
-                    if (apply_manifold(w, slot, man[slot])) flip_b[ca] = flip_b[cb] = 1;
+                    if (update(slot)) flip_b[ca] = flip_b[cb] = 1;
                     w.t_enabled[slot] = 1;
                     touched[other] = 1;
                     if (man[slot].count <= 0) continue;
@@ -939,6 +983,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                 }
             }
         }
+        if (x.p.events) x.p.event_count[x.world] = ev_n;
     }
     t_min = __shfl_sync(FULL, (int)t_min, 0);
     n_isl = __shfl_sync(FULL, n_isl, 0);
@@ -1030,7 +1075,8 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         w.v[2 * b] = vx, w.v[2 * b + 1] = vy, w.w[b] = ww;
         w.xf_p[2 * b] = xf.p.x, w.xf_p[2 * b + 1] = xf.p.y, w.xf_q[2 * b] = xf.q.c, w.xf_q[2 * b + 1] = xf.q.s;
     }
-    for (int k = lane; k < n_isl; k += 32) {  // b2Island::Report
+    const int ev_base = x.p.events ? x.p.event_count[x.world] : 0;
+    for (int k = lane; k < n_isl; k += 32) {  // b2Island::Report (PostSolve per island contact)
         const VCRow &c = vc[k];
         solved[c.slot] = 1;
         w.t_solved[c.slot] = 1;
@@ -1038,7 +1084,10 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
             w.t_ni[2 * c.slot + j] = j < c.count ? c.ni[j] : 0.0f;
             w.t_ti[2 * c.slot + j] = j < c.count ? c.ti[j] : 0.0f;
         }
+        if (x.p.events) put_event(x.p, x.world, ev_base + k, EV_POST_SOLVE, w.fa[c.slot], w.fb[c.slot], c.count, c.ni, c.ti);
     }
+    __syncwarp();
+    if (lane == 0 && x.p.events) x.p.event_count[x.world] = ev_base + n_isl;
     __syncwarp();
 #ifdef GOIB2D_PHASE_TIMERS
     if (lane == 0) atomicAdd(&g_toi_cycles[13], (unsigned long long)(clock64() - ev_t0));
@@ -1122,7 +1171,8 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     const int region = hot ? p.lay.hot_end + (PART == 1 ? p.lay.rows_bytes : 0) : 0;
     char *mine = dyn_smem + warp * region;
     Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
-          hot && PART == 1 && p.lay.rows_bytes ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64()};
+          hot && PART == 1 && p.lay.rows_bytes ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64(),
+          world};
     W &w = x.w;
     const float dt = p.dt;
     if (PART == 0) {

@@ -151,6 +151,23 @@ class Engine:
                                              C.c_float(max_length), out.data_ptr(), self._stream(device)))
         return out
 
+    def set_event_log(self, capacity):
+        """Log each world's contact events (Begin / End / PostSolve, goib2d_event) of every step, capacity per world
+        (0: off)."""
+        native.check(self.lib.goib2d_set_event_log(self.handle, int(capacity)))
+
+    def events(self):
+        """The last step's event log: (events (n_worlds, capacity) of native.EVENT_DTYPE, counts (n_worlds,))
+        copied to the host; a count above capacity means the later events were dropped."""
+        ev, cnt, n, cap = C.c_void_p(), C.c_void_p(), C.c_int64(), C.c_int32()
+        native.check(self.lib.goib2d_events(self.handle, C.byref(ev), C.byref(cnt), C.byref(n), C.byref(cap)))
+        N, K = n.value, cap.value
+        out = np.zeros((N, K), native.EVENT_DTYPE)
+        counts = np.zeros(N, np.int32)
+        if N and K:
+            native.check(self.lib.goib2d_events_copy(self.handle, out.ctypes.data, counts.ctypes.data_as(native._i), N))
+        return out, counts
+
     def status(self):
         """Per-world status words of the last step, copied to the host (numpy int32; see goib2d_status)."""
         n = C.c_int64()

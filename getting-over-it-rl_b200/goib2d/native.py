@@ -65,6 +65,13 @@ def candidate_pairs_device(body_type, fixtures, joints, layer_masks=None):
     return out[:n.value]
 
 
+# goib2d_event: kind, fixture_a, fixture_b, child_a, child_b, count, normal_impulse[2], tangent_impulse[2]
+EVENT_DTYPE = np.dtype([("kind", np.int32), ("fixture_a", np.int32), ("fixture_b", np.int32), ("child_a", np.int32),
+                        ("child_b", np.int32), ("count", np.int32), ("normal_impulse", np.float32, 2),
+                        ("tangent_impulse", np.float32, 2)])
+assert EVENT_DTYPE.itemsize == 40
+
+
 class ModelDesc(C.Structure):
     _fields_ = [("n_bodies", C.c_int32), ("n_fixtures", C.c_int32), ("n_joints", C.c_int32), ("n_pairs", C.c_int32),
                 ("fixture_body", _i), ("shape_type", _i), ("count", _i), ("radius", _f), ("verts", _f),
@@ -196,6 +203,9 @@ def load():
                                           C.POINTER(vp), vp, vp]),
         "goib2d_kernels_per_step": (C.c_int, [C.c_int64]),
         "goib2d_candidate_pairs": (C.c_int, [C.POINTER(PairDesc), _i, _i, C.c_int64, C.POINTER(C.c_int64)]),
+        "goib2d_set_event_log": (C.c_int, [vp, C.c_int32]),
+        "goib2d_events": (C.c_int, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int32)]),
+        "goib2d_events_copy": (C.c_int, [vp, vp, _i, C.c_int64]),
         "goib2d_reset_masked": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp), vp, vp]),
         "goib2d_reset_below": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp),
                                          C.c_int32, C.c_float, vp, vp]),

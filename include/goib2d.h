@@ -187,6 +187,25 @@ typedef struct goib2d_pair_desc {
 int goib2d_candidate_pairs(const goib2d_pair_desc *desc, int32_t *pair_a, int32_t *pair_b, int64_t capacity,
                            int64_t *n_pairs);
 
+/* ---- Contact event log: the reference C API's listener (goi_jax/reference/capi.cpp:45-78, goi_b2_events at
+ * :838-847) for a batch. Per world, the Begin (kind 0), End (1) and PostSolve (2) events of the last step, in the
+ * order Box2D raises them: Collide's updates in contact-list order (End also for a touching contact that Collide
+ * destroys), PostSolve per island contact after the island solve, then each TOI event's updates and its PostSolve.
+ * The record has the reference's Event layout; child indices are 0 (a chain's children are fixtures here). */
+typedef struct goib2d_event {
+    int32_t kind, fixture_a, fixture_b, child_a, child_b, count;
+    float normal_impulse[2], tangent_impulse[2];
+} goib2d_event;
+/* capacity events per world (0: off, the default). Logging changes no result. With n_steps > 1 the log holds the
+ * last step's events. */
+int goib2d_set_event_log(goib2d_model *model, int32_t capacity);
+/* The log of the last step: device goib2d_event [n_worlds][capacity] and device int32 [n_worlds] counts (a count
+ * above capacity: the events past capacity were dropped). Valid until the next step on this model. */
+int goib2d_events(goib2d_model *model, const goib2d_event **device_events, const int32_t **device_counts,
+                  int64_t *n_worlds, int32_t *capacity);
+/* The same log copied to host memory: n_worlds x capacity events and n_worlds counts; synchronises the device. */
+int goib2d_events_copy(goib2d_model *model, goib2d_event *host_events, int32_t *host_counts, int64_t n_worlds);
+
 /* Bytes of the static scratch arena used by goib2d_step_noalloc (on every device that loads the library). */
 #define GOIB2D_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -142,6 +142,10 @@ struct Model {
 
 struct World {
     int B, rows, J, C;
+    // contact event log of the current step (null: off), see goib2d_event in include/goib2d.h
+    goib2d_event *events = nullptr;
+    int32_t *event_count = nullptr;
+    int event_cap = 0;
     // bodies
     int32_t *type;
     uint8_t *active, *awake, *allow_sleep, *bullet, *continuous;
@@ -183,6 +187,19 @@ AABB fixture_fat(const Model &m, const World &w, int f);
 float fixture_friction(const Model &m, const World &w, int f);
 float fixture_restitution(const Model &m, const World &w, int f);
 AABB fixture_aabb(const Model &m, int f, Xf xf);
+
+// Contact events (the reference C API's listener): appended in the order they are raised
+enum { EV_BEGIN = 0, EV_END = 1, EV_POST_SOLVE = 2 };
+static inline void emit_event(World &w, int kind, int slot, int count = 0, const float *ni = nullptr,
+                              const float *ti = nullptr) {
+    if (!w.events) return;
+    int k = (*w.event_count)++;
+    if (k >= w.event_cap) return;
+    goib2d_event e{};
+    e.kind = kind, e.fixture_a = w.fa[slot], e.fixture_b = w.fb[slot], e.count = count;
+    for (int j = 0; j < count && j < 2; ++j) e.normal_impulse[j] = ni[j], e.tangent_impulse[j] = ti[j];
+    w.events[k] = e;
+}
 
 // Narrow phase (collide.py)
 struct Manifold {

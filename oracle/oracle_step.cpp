@@ -89,14 +89,17 @@ static void collide(const Model &m, World &w, const goib2d_settings &s) {
         bool wakes = over[s_] ? (touching_new != (bool)w.touching[s_]) : (w.count[s_] > 0);
         if (visit && wakes) aw[ba] = aw[bb] = 1;
     }
+    if (w.events) *w.event_count = 0;  // a new step's log
     for (int s_ : order) {
         if (!active[s_]) continue;
-        if (!over[s_]) {  // destroy
+        if (!over[s_]) {  // destroy (EndContact when it was touching)
+            if (w.touching[s_]) emit_event(w, EV_END, s_);
             w.pair[s_] = -1;
             w.touching[s_] = 0;
             w.count[s_] = 0;
             continue;
         }
+        if ((man[s_].count > 0) != (bool)w.touching[s_]) emit_event(w, man[s_].count > 0 ? EV_BEGIN : EV_END, s_);
         const Manifold &mn = man[s_];
         int old_n = w.count[s_];
         float ni[2], ti[2];
@@ -1089,6 +1092,7 @@ static void solve(const Model &m, World &w, const goib2d_settings &s, float dt, 
             w.normal_impulse[2 * c.slot + j] = c.ni[j];
             w.tangent_impulse[2 * c.slot + j] = c.ti[j];
         }
+    for (const VC &c : vc) emit_event(w, EV_POST_SOLVE, c.slot, c.count, c.ni, c.ti);  // b2Island::Report
     for (const JR &r : jr) {  // joints.py:609-622
         if (s.revolute_v24) w.lower_impulse[r.jid] = r.imp[3], w.upper_impulse[r.jid] = r.imp[4];
         for (int k = 0; k < 3; ++k) w.impulse[3 * r.jid + k] = r.imp[k];
@@ -1237,14 +1241,17 @@ void oracle_sin_cos(const float *x, int64_t n, float *s, float *c) {
 
 // Step worlds [w0, w1) of a batch n_steps times on the host (leaves: host pointers, (N, ...) layout).
 // actions: NULL or float [N][n_action]; before each step joints.motor_speed[joint[k]] = scale[k] * action[k].
-int oracle_step_range(const goib2d_model_desc *desc, const goib2d_settings *s, float dt, int32_t C, int32_t rows,
-                      int64_t w0, int64_t w1, int32_t n_steps, void *const *leaves, const float *actions,
-                      int32_t n_action, const int32_t *action_joint, const float *action_scale) {
+int oracle_step_range_events(const goib2d_model_desc *desc, const goib2d_settings *s, float dt, int32_t C,
+                             int32_t rows, int64_t w0, int64_t w1, int32_t n_steps, void *const *leaves,
+                             const float *actions, int32_t n_action, const int32_t *action_joint,
+                             const float *action_scale, goib2d_event *events, int32_t *event_count,
+                             int32_t event_cap) {
     orc::Model m{desc, desc->n_bodies, desc->n_fixtures, desc->n_joints, desc->n_pairs, desc->fixture_slot != nullptr};
     if (m.compact && rows == m.F) m.compact = false;  // a full-layout State also works with a compact Model
     for (int64_t wi = w0; wi < w1; ++wi) {
         orc::World w;
         orc::bind_world(w, leaves, wi, m.B, rows, m.J, C);
+        if (events) w.events = events + wi * event_cap, w.event_count = event_count + wi, w.event_cap = event_cap;
         for (int k = 0; k < n_steps; ++k) {
             if (actions)
                 for (int a = 0; a < n_action; ++a)
@@ -1253,5 +1260,12 @@ int oracle_step_range(const goib2d_model_desc *desc, const goib2d_settings *s, f
         }
     }
     return 0;
+}
+
+int oracle_step_range(const goib2d_model_desc *desc, const goib2d_settings *s, float dt, int32_t C, int32_t rows,
+                      int64_t w0, int64_t w1, int32_t n_steps, void *const *leaves, const float *actions,
+                      int32_t n_action, const int32_t *action_joint, const float *action_scale) {
+    return oracle_step_range_events(desc, s, dt, C, rows, w0, w1, n_steps, leaves, actions, n_action, action_joint,
+                                    action_scale, nullptr, nullptr, 0);
 }
 }

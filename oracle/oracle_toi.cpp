@@ -426,6 +426,7 @@ void update_contact(World &w, int s_, const Manifold &mn, bool *flip) {  // b2Co
     }
     bool touching = mn.count > 0;
     *flip = touching != (bool)w.touching[s_];
+    if (*flip) emit_event(w, touching ? EV_BEGIN : EV_END, s_);
     w.touching[s_] = touching;
     w.count[s_] = mn.count;
     if (mn.count > 0) {
@@ -789,6 +790,7 @@ void event(const Model &m, World &w, const goib2d_settings &s, float dt, int min
             w.xf_p[2 * b] = x.p.x, w.xf_p[2 * b + 1] = x.p.y, w.xf_q[2 * b] = x.q.c, w.xf_q[2 * b + 1] = x.q.s;
         }
         for (const TV &c : vcs) {  // b2Island::Report
+            emit_event(w, EV_POST_SOLVE, c.slot, c.count, c.ni, c.ti);
             solved[c.slot] = 1;
             for (int j = 0; j < 2; ++j) {
                 ni_r[2 * c.slot + j] = j < c.count ? c.ni[j] : 0.0f;

@@ -75,6 +75,27 @@ def step(model, state, settings, dt, n_steps=1, threads=0, actions=None, action_
     return out
 
 
+def step_events(model, state, settings, dt, n_steps, capacity, threads=0):
+    """Step a copy of `state` with the contact event log on: (new State, events (N, capacity), counts (N,)); the log
+    holds the last step's events (goib2d_event layout)."""
+    lib = load()
+    st = batched(state)
+    leaves = [np.ascontiguousarray(x).copy() for x in state_leaves(st)]
+    N, B = leaves[0].shape[0], leaves[0].shape[1]
+    pm = native.model_desc(model, B)
+    ss = settings_struct(settings)
+    ptrs = (C.c_void_p * len(leaves))(*[x.ctypes.data for x in leaves])
+    ev = np.zeros((N, capacity), native.EVENT_DTYPE)
+    cnt = np.zeros(N, np.int32)
+    lib.oracle_step_batch_events.argtypes = [C.POINTER(native.ModelDesc), C.c_void_p, C.c_float, C.c_int32, C.c_int32,
+                                             C.c_int64, C.c_int32, C.POINTER(C.c_void_p), C.c_void_p, C.c_void_p,
+                                             C.c_int32, C.c_int32]
+    assert lib.oracle_step_batch_events(C.byref(pm.desc), C.addressof(ss), C.c_float(dt), st.contacts.pair.shape[1],
+                                        st.fixtures.friction.shape[1], N, n_steps, ptrs, ev.ctypes.data,
+                                        cnt.ctypes.data, capacity, threads) == 0
+    return state_from_leaves(leaves), ev, cnt
+
+
 def raycast(model, state, body, n_rays, max_length):
     """The oracle's ray casts (see goib2d_raycast) for a batched numpy State: (N, n_rays) float32."""
     lib = load()
