@@ -129,7 +129,7 @@ __device__ __forceinline__ void gjk_solve3(SV &s0, SV &s1, SV &s2, int &count) {
 
 // b2Distance, useRadii = false (toi.py:230-294)
 // The simplex lives in three named vertices (s0, s1, s2), not an indexed array, so that it stays in registers.
-__device__ __noinline__ float gjk_distance(Cache &cache, const Proxy &pA, Xf xfA, const Proxy &pB, Xf xfB) {
+__device__ __forceinline__ float gjk_distance(Cache &cache, const Proxy &pA, Xf xfA, const Proxy &pB, Xf xfB) {
     const SV zero{{0, 0}, {0, 0}, {0, 0}, 0.0f, 0, 0};
     SV s0 = zero, s1 = zero, s2 = zero;
     const int cc = cache.count;
@@ -254,7 +254,7 @@ __device__ float sep_find_min(const SepFn &f, const Proxy &pA, Xf xfA, const Pro
 }
 
 // b2TimeOfImpact with tMax = 1 (toi.py:364-457). Returns the b2TOIOutput state; *t_out its t.
-__device__ __noinline__ int time_of_impact(const Proxy &pA, Sweep swA, const Proxy &pB, Sweep swB, float slop,
+__device__ __forceinline__ int time_of_impact(const Proxy &pA, Sweep swA, const Proxy &pB, Sweep swB, float slop,
                                            float *t_out) {
     const float two_pi = 2.0f * PI_F;
     {  // b2Sweep::Normalize
