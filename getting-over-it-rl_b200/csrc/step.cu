@@ -936,29 +936,83 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                  s.linear_slop, s.angular_slop, man[s_]);
     }
     __syncwarp();
-    int n_isl = 0;
+    // The island walk (toi.py:633-657): bodyA's contact list then bodyB's, newest first; each walked contact is
+    // updated (b2Contact::Update, Begin / End events) and, when touching, joins the island. Its only order-dependent
+    // rule is the cap (32 contacts, 64 bodies): when a side-effect-free count shows the island cannot reach it, the
+    // walk runs on all lanes, island and event order kept by ballots; otherwise on lane 0 as listed.
+    auto walked = [&](int oi, int slot, int &other) {  // does the walk of owner oi update this contact?
+        const int owner = oi ? Bb : A;
+        int ca = m.fixture_body[w.fa[slot]], cb = m.fixture_body[w.fb[slot]];
+        if (ca != owner && cb != owner) return false;
+        if (oi == 1 && w.type[A] == DYNAMIC && (ca == A || cb == A)) return false;
+        if (slot == min_slot) return false;
+        other = ca == owner ? cb : ca;
+        if (w.type[other] == DYNAMIC && !w.bullet[owner] && !w.bullet[other]) return false;
+        if (s.unity_toi && !toi_pair_rule(w, owner, other, true)) return false;
+        return true;
+    };
+    int n_isl = 0, ev_n = 0;
     bool t_min = false;
-    if (lane == 0) {
-        int ev_n = x.p.events ? x.p.event_count[x.world] : 0;  // b2Contact::Update's Begin / End, in order
-        auto update = [&](int slot) {
-            bool flip = apply_manifold(w, slot, man[slot]);
-            if (flip && x.p.events)
-                put_event(x.p, x.world, ev_n++, w.touching[slot] ? EV_BEGIN : EV_END, w.fa[slot], w.fb[slot]);
-            return flip;
-        };
+    if (lane == 0) {  // the minimum contact
+        ev_n = x.p.events ? x.p.event_count[x.world] : 0;
         t_min = man[min_slot].count > 0;
-        if (update(min_slot))
+        if (apply_manifold(w, min_slot, man[min_slot])) {
             flip_b[m.fixture_body[w.fa[min_slot]]] = flip_b[m.fixture_body[w.fb[min_slot]]] = 1;
+            if (x.p.events)
+                put_event(x.p, x.world, ev_n++, w.touching[min_slot] ? EV_BEGIN : EV_END, w.fa[min_slot],
+                          w.fb[min_slot]);
+        }
         w.t_enabled[min_slot] = t_min;
         w.t_count[min_slot] += 1;
         w.t_flag[min_slot] = 0;
-        if (t_min) {  // the island walk: bodyA's contact list then bodyB's, newest first (toi.py:633-657)
-            tisl[n_isl++] = min_slot;
+        if (t_min) tisl[n_isl++] = min_slot;
+    }
+    t_min = __shfl_sync(FULL, (int)t_min, 0);
+    ev_n = __shfl_sync(FULL, ev_n, 0);
+    n_isl = __shfl_sync(FULL, n_isl, 0);
+    __syncwarp();
+    if (t_min) {
+        int total = 0;  // contacts the walk would add to the island
+        for (int oi = 0; oi < 2; ++oi) {
+            if (w.type[oi ? Bb : A] != DYNAMIC) continue;
+            for (int base = 0; base < n_live; base += 32) {
+                int k = base + lane, other = 0;
+                bool add = k < n_live && walked(oi, order[k], other) && man[order[k]].count > 0;
+                total += __popc(__ballot_sync(FULL, add));
+            }
+        }
+        if (total + 1 < MAX_TOI_CONTACTS) {  // the cap cannot be reached: all lanes
+            for (int oi = 0; oi < 2; ++oi) {
+                if (w.type[oi ? Bb : A] != DYNAMIC) continue;
+                for (int base = 0; base < n_live; base += 32) {
+                    int k = base + lane, other = 0, slot = k < n_live ? order[k] : -1;
+                    bool upd = slot >= 0 && walked(oi, slot, other), flip = false, add = false;
+                    if (upd) {
+                        flip = apply_manifold(w, slot, man[slot]);
+                        if (flip) flip_b[m.fixture_body[w.fa[slot]]] = flip_b[m.fixture_body[w.fb[slot]]] = 1;
+                        w.t_enabled[slot] = 1;
+                        touched[other] = 1;
+                        add = man[slot].count > 0;
+                        if (add) {
+                            in_other[other] = 1;
+                            if (other != A && other != Bb) newbody[other] = 1;
+                        }
+                    }
+                    unsigned fm = __ballot_sync(FULL, flip), am = __ballot_sync(FULL, add);
+                    const unsigned below = (1u << lane) - 1;
+                    if (flip && x.p.events)
+                        put_event(x.p, x.world, ev_n + __popc(fm & below), w.touching[slot] ? EV_BEGIN : EV_END,
+                                  w.fa[slot], w.fb[slot]);
+                    if (add) tisl[n_isl + __popc(am & below)] = slot;
+                    ev_n += __popc(fm), n_isl += __popc(am);
+                }
+            }
+            __syncwarp();
+        } else if (lane == 0) {  // near the cap: as listed
             int n_bodies = 2;
-            const int owners[2] = {A, Bb};
             bool stop = false;
             for (int oi = 0; oi < 2 && !stop; ++oi) {
-                int owner = owners[oi];
+                int owner = oi ? Bb : A;
                 if (w.type[owner] != DYNAMIC) continue;
                 for (int k = 0; k < n_live; ++k) {
                     int slot = order[k];
@@ -969,11 +1023,14 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                         stop = true;
                         break;
                     }
-                    if (slot == min_slot) continue;
-                    int other = ca == owner ? cb : ca;
-                    if (w.type[other] == DYNAMIC && !w.bullet[owner] && !w.bullet[other]) continue;
-                    if (s.unity_toi && !toi_pair_rule(w, owner, other, true)) continue;
-                    if (update(slot)) flip_b[ca] = flip_b[cb] = 1;
+                    int other = 0;
+                    if (!walked(oi, slot, other)) continue;
+                    if (apply_manifold(w, slot, man[slot])) {
+                        flip_b[ca] = flip_b[cb] = 1;
+                        if (x.p.events)
+                            put_event(x.p, x.world, ev_n++, w.touching[slot] ? EV_BEGIN : EV_END, w.fa[slot],
+                                      w.fb[slot]);
+                    }
                     w.t_enabled[slot] = 1;
                     touched[other] = 1;
                     if (man[slot].count <= 0) continue;
@@ -983,10 +1040,10 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                 }
             }
         }
-        if (x.p.events) x.p.event_count[x.world] = ev_n;
+        n_isl = __shfl_sync(FULL, n_isl, 0);
+        ev_n = __shfl_sync(FULL, ev_n, 0);
     }
-    t_min = __shfl_sync(FULL, (int)t_min, 0);
-    n_isl = __shfl_sync(FULL, n_isl, 0);
+    if (lane == 0 && x.p.events) x.p.event_count[x.world] = ev_n;
     __syncwarp();
     for (int b = lane; b < B; b += 32) {  // body sweeps after the walk (toi.py:667-681)
         bool pair_b = b == A || b == Bb;
