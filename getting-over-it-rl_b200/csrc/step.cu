@@ -1072,7 +1072,9 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     if (lane == 0) atomicAdd(&g_toi_cycles[12], (unsigned long long)(clock64() - ev_t0));
     ev_t0 = clock64();
 #endif
-    // b2Island::SolveTOI: position passes moving only the TOI pair, then velocity passes, then integration
+    // b2Island::SolveTOI: position passes moving only the TOI pair, then velocity passes, then integration; the
+    // island's rows in the warp's shared rows region when they fit
+    if (x.rows && n_isl <= L.sm_vc_cap) vc = reinterpret_cast<VCRow *>(x.rows + L.sm_vc);
     for (int b = lane; b < B; b += 32) {
         bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
         bd.vx[b] = w.v[2 * b], bd.vy[b] = w.v[2 * b + 1], bd.vw[b] = w.w[b];
@@ -1225,10 +1227,11 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     // they use is written and read within the kernel; the large-batch split solve passes arrays between kernels
     extern __shared__ __align__(16) char dyn_smem[];
     const bool hot = (PART == 0 || PART == 1 || PART == 5) && p.lay.hot_end > 0;
-    const int region = hot ? p.lay.hot_end + (PART == 1 ? p.lay.rows_bytes : 0) : 0;
+    const bool rows = hot && (PART == 1 || PART == 5) && p.lay.rows_bytes;  // the solve's and the TOI island's rows
+    const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
     char *mine = dyn_smem + warp * region;
     Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
-          hot && PART == 1 && p.lay.rows_bytes ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64(),
+          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64(),
           world};
     W &w = x.w;
     const float dt = p.dt;
@@ -1352,7 +1355,7 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
             goib2d_finish_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
             goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         }
-        goib2d_toi_kernel<<<blocks, 32 * wpb, hot, stream>>>(p);
+        goib2d_toi_kernel<<<blocks, 32 * wpb, hot ? hot + (size_t)wpb * p.lay.rows_bytes : 0, stream>>>(p);
     }
     return cudaGetLastError();
 }
