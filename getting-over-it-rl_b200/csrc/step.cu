@@ -1082,9 +1082,15 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = bd.ca[b];
     }
     __syncwarp();
+#ifdef GOIB2D_PHASE_TIMERS
+    long long isl_t0 = clock64();
+#endif
     for (int k = lane; k < n_isl; k += 32)  // position rows (the position-independent fields)
         prepare_contact(m, w, tisl[k], bd, false, 1.0f, s.velocity_threshold, vc[k]);
     __syncwarp();
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[4], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
+#endif
     if (lane == 0) {
         const float okay_sep = -1.5f * s.linear_slop;
         for (int it = 0; it < 20; ++it) {
@@ -1107,13 +1113,23 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     __syncwarp();
     for (int b = lane; b < B; b += 32) body_rot(bd, b, bd.ca[b]);
     __syncwarp();
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[5], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
+#endif
     for (int k = lane; k < n_isl; k += 32)  // velocity constraints at the solved poses, no warm start
         prepare_contact(m, w, tisl[k], bd, false, 1.0f, s.velocity_threshold, vc[k]);
     __syncwarp();
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[6], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
+#endif
     if (lane == 0)
         for (int it = 0; it < s.velocity_iterations; ++it)
             for (int k = 0; k < n_isl; ++k) contact_solve_velocity(vc[k], bd);
     __syncwarp();
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[7], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
+    if (lane == 0) atomicAdd(&g_toi_cycles[11], (unsigned long long)n_isl);
+#endif
     const float h = (1.0f - min_alpha) * dt;
     const float max_t = s.clamps_per_second ? s.max_translation * dt : s.max_translation;
     const float max_r = s.clamps_per_second ? s.max_rotation * dt : s.max_rotation;
