@@ -139,13 +139,23 @@ __device__ float find_max_separation(const Poly &p1, Xf xf1, const Poly &p2, Xf 
     Rot q{xf2.q.c * xf1.q.c + xf2.q.s * xf1.q.s, xf2.q.c * xf1.q.s - xf2.q.s * xf1.q.c};
     V2 p = rot_t(xf2.q, sub(xf1.p, xf2.p));
     Xf xf{p, q};
+    // p2's vertices load once, as the four 16-byte words of its 64-byte-aligned slot, for every edge of p1
+    const float4 *q2 = reinterpret_cast<const float4 *>(p2.v);
+    float4 w[MAXV / 2];
+#pragma unroll
+    for (int k = 0; k < MAXV / 2; ++k) w[k] = __ldg(q2 + k);
     int best = 0;
     float maxsep = -MAXF;
     for (int i = 0; i < p1.count; ++i) {
         V2 n = rot(q, p1.norm(i));
         V2 v1 = xf_mul(xf, p1.vert(i));
         float si = MAXF;
-        for (int j = 0; j < p2.count; ++j) si = fminf(si, dot(n, sub(p2.vert(j), v1)));
+#pragma unroll
+        for (int j = 0; j < MAXV; ++j) {
+            V2 pj = (j & 1) ? V2{w[j >> 1].z, w[j >> 1].w} : V2{w[j >> 1].x, w[j >> 1].y};
+            float dj = dot(n, sub(pj, v1));
+            if (j < p2.count) si = fminf(si, dj);
+        }
         if (i == 0 || si > maxsep) maxsep = si, best = i;
     }
     *edge = best;

@@ -33,13 +33,24 @@ struct Proxy {
         i = i < 0 ? 0 : (i > MAXV - 1 ? MAXV - 1 : i);
         return {v[2 * i], v[2 * i + 1]};
     }
-    __device__ int support(V2 d) const {  // b2DistanceProxy::GetSupport
+    // b2DistanceProxy::GetSupport: the first vertex of largest projection on d, returned with its coordinates in
+    // *pt. A fixture's slot holds MAXV vertices in one 64-byte-aligned run, so the four 16-byte words load together
+    // (one memory round trip, not one per vertex); vertices past `count` are loaded but never chosen.
+    __device__ __forceinline__ int support(V2 d, V2 *pt = nullptr) const {
+        const float4 *q = reinterpret_cast<const float4 *>(v);
+        float4 w[MAXV / 2];
+#pragma unroll
+        for (int k = 0; k < MAXV / 2; ++k) w[k] = __ldg(q + k);
         int best = 0;
-        float bv = 0.0f;
-        for (int i = 0; i < count; ++i) {
-            float val = v[2 * i] * d.x + v[2 * i + 1] * d.y;
-            if (i == 0 || val > bv) best = i, bv = val;
+        float bv = w[0].x * d.x + w[0].y * d.y;
+        V2 bp{w[0].x, w[0].y};
+#pragma unroll
+        for (int i = 1; i < MAXV; ++i) {
+            const float px = (i & 1) ? w[i >> 1].z : w[i >> 1].x, py = (i & 1) ? w[i >> 1].w : w[i >> 1].y;
+            float val = px * d.x + py * d.y;
+            if (i < count && val > bv) best = i, bv = val, bp = V2{px, py};
         }
+        if (pt) *pt = bp;
         return best;
     }
 };
@@ -66,13 +77,16 @@ struct Cache {
     float metric;
 };
 
-__device__ __forceinline__ SV make_vertex(const Proxy &pA, Xf xfA, int iA, const Proxy &pB, Xf xfB, int iB) {
+__device__ __forceinline__ SV make_vertex_at(Xf xfA, V2 la, int iA, Xf xfB, V2 lb, int iB) {
     SV v;
-    v.wA = xf_mul(xfA, pA.vert(iA));
-    v.wB = xf_mul(xfB, pB.vert(iB));
+    v.wA = xf_mul(xfA, la);
+    v.wB = xf_mul(xfB, lb);
     v.w = sub(v.wB, v.wA);
     v.a = 0.0f, v.iA = iA, v.iB = iB;
     return v;
+}
+__device__ __forceinline__ SV make_vertex(const Proxy &pA, Xf xfA, int iA, const Proxy &pB, Xf xfB, int iB) {
+    return make_vertex_at(xfA, pA.vert(iA), iA, xfB, pB.vert(iB), iB);
 }
 __device__ __forceinline__ float simplex_metric(const SV &s0, const SV &s1, const SV &s2, int count) {
     if (count == 2) return length(sub(s0.w, s1.w));
@@ -161,9 +175,10 @@ __device__ __forceinline__ float gjk_distance(Cache &cache, const Proxy &pA, Xf 
             d = sgn > 0 ? cross_sv(1.0f, e12) : cross_vs(e12, 1.0f);
         }
         if (dot(d, d) < EPS * EPS) break;
-        int iA = pA.support(rot_t(xfA.q, neg(d)));
-        int iB = pB.support(rot_t(xfB.q, d));
-        SV v = make_vertex(pA, xfA, iA, pB, xfB, iB);
+        V2 la, lb;
+        int iA = pA.support(rot_t(xfA.q, neg(d)), &la);
+        int iB = pB.support(rot_t(xfB.q, d), &lb);
+        SV v = make_vertex_at(xfA, la, iA, xfB, lb, iB);
         if (count == 1) {  // the new vertex goes to slot `count`; its weight is left as the slot had it
             v.a = s1.a;
             s1 = v;
@@ -239,18 +254,27 @@ __device__ float sep_eval(const SepFn &f, const Proxy &pA, Xf xfA, int iA, const
     return dot(sub(pa, qb), n);
 }
 
+// b2SeparationFunction::FindMinSeparation: the support points, then Evaluate's arithmetic on them (sep_eval)
 __device__ float sep_find_min(const SepFn &f, const Proxy &pA, Xf xfA, const Proxy &pB, Xf xfB, int &iA, int &iB) {
+    V2 la, lb;
     if (f.type == E_POINTS) {
-        iA = pA.support(rot_t(xfA.q, f.axis));
-        iB = pB.support(rot_t(xfB.q, neg(f.axis)));
-    } else if (f.type == E_FACE_A) {
-        iA = -1;
-        iB = pB.support(rot_t(xfB.q, neg(rot(xfA.q, f.axis))));
-    } else {
-        iB = -1;
-        iA = pA.support(rot_t(xfA.q, neg(rot(xfB.q, f.axis))));
+        iA = pA.support(rot_t(xfA.q, f.axis), &la);
+        iB = pB.support(rot_t(xfB.q, neg(f.axis)), &lb);
+        V2 pa = xf_mul(xfA, la), pb = xf_mul(xfB, lb);
+        return dot(sub(pb, pa), f.axis);
     }
-    return sep_eval(f, pA, xfA, iA, pB, xfB, iB);
+    if (f.type == E_FACE_A) {
+        iA = -1;
+        V2 n = rot(xfA.q, f.axis);
+        iB = pB.support(rot_t(xfB.q, neg(n)), &lb);
+        V2 qa = xf_mul(xfA, f.lp), pb = xf_mul(xfB, lb);
+        return dot(sub(pb, qa), n);
+    }
+    iB = -1;
+    V2 n = rot(xfB.q, f.axis);
+    iA = pA.support(rot_t(xfA.q, neg(n)), &la);
+    V2 qb = xf_mul(xfB, f.lp), pa = xf_mul(xfA, la);
+    return dot(sub(pa, qb), n);
 }
 
 // b2TimeOfImpact with tMax = 1 (toi.py:364-457). Returns the b2TOIOutput state; *t_out its t.
