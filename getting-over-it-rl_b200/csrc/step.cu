@@ -26,7 +26,18 @@ __device__ unsigned long long g_counts[16];
 // cycles in the TOI parts (0 sweep_xf, 1 GJK, 2 sep_init, 3 sep_find_min) and the island solver's calls (4 contact
 // velocity, 5 joint velocity, 6 contact position, 7 joint position; their counts at 8-11)
 __device__ unsigned long long g_toi_cycles[16];
+// per-warp cycles in a part kernel (sum, warps, max): 0-2 TOI without events, 3-5 TOI with events, 6-8 solve,
+// 9-11 collide
+__device__ unsigned long long g_span[16];
 }  // namespace gb
+#define GB_SPAN(x, k, ev)                                                                   \
+    do {                                                                                    \
+        if ((x).lane == 0) {                                                                \
+            unsigned long long d_ = (unsigned long long)(clock64() - gb_span0_);              \
+            const int i_ = (k) + 3 * ((ev) ? 1 : 0);                                        \
+            atomicAdd(&g_span[i_], d_), atomicAdd(&g_span[i_ + 1], 1ull), atomicMax(&g_span[i_ + 2], d_); \
+        }                                                                                   \
+    } while (0)
 #define GB_COUNT(i, v) atomicAdd(&g_counts[i], (unsigned long long)(v))
 #define GB_TOI_T0() long long gb_t0_ = clock64()
 #define GB_TOI_T1(i) atomicAdd(&g_toi_cycles[i], (unsigned long long)(clock64() - gb_t0_))
@@ -42,6 +53,9 @@ __device__ unsigned long long g_toi_cycles[16];
     } while (0)
 #define GB_TOI_T1(i) \
     do {             \
+    } while (0)
+#define GB_SPAN(x, k, ev) \
+    do {                  \
     } while (0)
 #endif
 
@@ -702,6 +716,13 @@ __device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t w
     }
 }
 
+// A float's order-preserving integer key (NaN excluded): the integer order of keys is the float order, -0 below +0.
+__device__ __forceinline__ int fkey(float f) {
+    const int i = __float_as_int(f);
+    return i ^ ((i >> 31) & 0x7fffffff);
+}
+__device__ __forceinline__ float fkey_inv(int k) { return __int_as_float(k ^ ((k >> 31) & 0x7fffffff)); }
+
 // b2World::Solve after the sweeps (step.py:141-194): write back, sleep, the moved bodies
 __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
     const DevModel &m = x.m;
@@ -723,49 +744,56 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
     }
     __syncwarp();
     int *islsleep = ap<int>(x, L.islsleep), *last = ap<int>(x, L.last);
-    float *minst = ap<float>(x, L.minst), *st = ap<float>(x, L.st);
-    if (lane == 0) {  // sleep per island (step.py:153-171), static bodies' awake flag (step.py:173-194)
-        for (int i = 0; i < B; ++i) islsleep[i] = 0;
-        if (s.allow_sleep) {
-            float lin_tol = s.linear_sleep_tolerance * s.linear_sleep_tolerance;
-            float ang_tol = s.angular_sleep_tolerance * s.angular_sleep_tolerance;
-            for (int i = 0; i < B; ++i) minst[i] = MAXF;
-            for (int b = 0; b < B; ++b) {
-                bool nonstatic = bisl[b] >= 0 && w.type[b] != STATIC;
-                bool mov = !w.allow_sleep[b] || (w.w[b] * w.w[b] > ang_tol) ||
-                           (w.v[2 * b] * w.v[2 * b] + w.v[2 * b + 1] * w.v[2 * b + 1] > lin_tol);
-                float t = mov ? 0.0f : w.sleep_time[b] + h;
-                st[b] = nonstatic ? t : w.sleep_time[b];
-                if (nonstatic) minst[bisl[b]] = fminf(minst[bisl[b]], mov ? 0.0f : st[b]);
+    float *st = ap<float>(x, L.st);
+    int *minkey = ap<int>(x, L.minst);
+    // Sleep per island (step.py:153-171) and the static bodies' awake flag (step.py:173-194), all lanes. The two
+    // reductions have no order: an island's minimum sleep time (a float minimum, as integer atomics on the order-
+    // preserving key of the float; a NaN time, which the float minimum skips, is skipped) and a static body's last
+    // island (an integer maximum).
+    for (int i = lane; i < B; i += 32) islsleep[i] = 0, last[i] = -1, minkey[i] = fkey(MAXF);
+    __syncwarp();
+    if (s.allow_sleep) {
+        const float lin_tol = s.linear_sleep_tolerance * s.linear_sleep_tolerance;
+        const float ang_tol = s.angular_sleep_tolerance * s.angular_sleep_tolerance;
+        for (int b = lane; b < B; b += 32) {
+            const bool nonstatic = bisl[b] >= 0 && w.type[b] != STATIC;
+            const float t0 = w.sleep_time[b];
+            float stb = t0;
+            if (nonstatic) {  // the island's velocities are the ones just written back
+                const float vx = bd.vx[b], vy = bd.vy[b], vw = bd.vw[b];
+                const bool mov = !w.allow_sleep[b] || (vw * vw > ang_tol) || (vx * vx + vy * vy > lin_tol);
+                stb = mov ? 0.0f : t0 + h;
+                const float contrib = mov ? 0.0f : stb;
+                if (contrib == contrib) atomicMin(minkey + bisl[b], fkey(contrib));
             }
-            for (int i = 0; i < B; ++i) islsleep[i] = minst[i] >= s.time_to_sleep && done[i];
-            for (int b = 0; b < B; ++b) {
-                bool nonstatic = bisl[b] >= 0 && w.type[b] != STATIC;
-                bool sl = nonstatic && islsleep[bisl[b]];
-                w.sleep_time[b] = sl ? 0.0f : st[b];
-                if (sl) {
-                    w.awake[b] = 0;
-                    w.v[2 * b] = w.v[2 * b + 1] = 0.0f, w.w[b] = 0.0f;
-                    w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
-                }
+            st[b] = stb;
+        }
+        __syncwarp();
+        for (int i = lane; i < B; i += 32) islsleep[i] = fkey_inv(minkey[i]) >= s.time_to_sleep && done[i];
+        __syncwarp();
+        for (int b = lane; b < B; b += 32) {
+            const bool sl = bisl[b] >= 0 && w.type[b] != STATIC && islsleep[bisl[b]];
+            w.sleep_time[b] = sl ? 0.0f : st[b];
+            if (sl) {
+                w.awake[b] = 0;
+                w.v[2 * b] = w.v[2 * b + 1] = 0.0f, w.w[b] = 0.0f;
+                w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
             }
         }
-        for (int b = 0; b < B; ++b) last[b] = -1;
-        for (int sl = 0; sl < C; ++sl) {
-            int i = cisl[sl];
-            if (i < 0) continue;
-            int ba = m.fixture_body[w.fa[sl]], bb = m.fixture_body[w.fb[sl]];
-            last[ba] = max(last[ba], i), last[bb] = max(last[bb], i);
-        }
-        for (int j = 0; j < J; ++j) {
-            int i = jisl[j];
-            if (i < 0) continue;
-            int ja = m.joint_a[j], jb = m.joint_b[j];
-            last[ja] = max(last[ja], i), last[jb] = max(last[jb], i);
-        }
-        for (int b = 0; b < B; ++b)
-            if (w.type[b] == STATIC && last[b] >= 0) w.awake[b] = !islsleep[last[b]], w.sleep_time[b] = 0.0f;
     }
+    for (int sl = lane; sl < C; sl += 32) {
+        const int i = cisl[sl];
+        if (i < 0) continue;
+        atomicMax(last + m.fixture_body[w.fa[sl]], i), atomicMax(last + m.fixture_body[w.fb[sl]], i);
+    }
+    for (int j = lane; j < J; j += 32) {
+        const int i = jisl[j];
+        if (i < 0) continue;
+        atomicMax(last + m.joint_a[j], i), atomicMax(last + m.joint_b[j], i);
+    }
+    __syncwarp();
+    for (int b = lane; b < B; b += 32)
+        if (w.type[b] == STATIC && last[b] >= 0) w.awake[b] = !islsleep[last[b]], w.sleep_time[b] = 0.0f;
     for (int b = lane; b < B; b += 32) moved[b] = bisl[b] >= 0 && w.type[b] != STATIC;
     __syncwarp();
     GB_PHASE(x, 6);
@@ -1251,6 +1279,9 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
           world};
     W &w = x.w;
     const float dt = p.dt;
+#ifdef GOIB2D_PHASE_TIMERS
+    const long long gb_span0_ = clock64();
+#endif
     if (PART == 0) {
         if (p.actions && x.lane < p.n_action)  // action channels -> joint motor speeds
             w.motor_speed[p.action_joint[x.lane]] = p.action_scale[x.lane] * p.actions[world * p.n_action + x.lane];
@@ -1263,6 +1294,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
         GB_PHASE(x, 0);
         collide(x);
         GB_PHASE(x, 1);
+        GB_SPAN(x, 9, false);
     } else if (PART == 1) {  // the whole of b2World::Solve, the sweeps on lane 0
         const IslandWork sw = solve(x, dt, *w.inv_dt0 * dt);
         if (x.lane == 0)
@@ -1273,6 +1305,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
         GB_PHASE(x, 5);
         solve_finish(x, dt, sw);
         broadphase(x);
+        GB_SPAN(x, 6, false);
     } else if (PART == 2) {
         solve(x, dt, *w.inv_dt0 * dt);
     } else if (PART == 3) {
@@ -1282,6 +1315,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     } else {
         if (x.s.continuous_physics) solve_toi(x, dt);
         __syncwarp();
+        GB_SPAN(x, 0, x.s.continuous_physics && *w.t_events > 0);
         if (x.lane == 0 && dt > 0) *w.inv_dt0 = 1.0f / dt;
         if (x.s.auto_clear_forces)
             for (int b = x.lane; b < w.B; b += 32) w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
@@ -1382,11 +1416,13 @@ extern "C" int goib2d_debug_phase_cycles(unsigned long long *out, int reset) {
     if (cudaMemcpyFromSymbol(out, g_phase_cycles, sizeof(g_phase_cycles)) != cudaSuccess) return -2;
     if (cudaMemcpyFromSymbol(out + 16, g_counts, sizeof(g_counts)) != cudaSuccess) return -2;
     if (cudaMemcpyFromSymbol(out + 32, g_toi_cycles, sizeof(g_toi_cycles)) != cudaSuccess) return -2;
+    if (cudaMemcpyFromSymbol(out + 48, g_span, sizeof(g_span)) != cudaSuccess) return -2;
     if (reset) {
         unsigned long long z[16] = {0};
         cudaMemcpyToSymbol(g_phase_cycles, z, sizeof(z));
         cudaMemcpyToSymbol(g_counts, z, sizeof(z));
         cudaMemcpyToSymbol(g_toi_cycles, z, sizeof(g_toi_cycles));
+        cudaMemcpyToSymbol(g_span, z, sizeof(g_span));
     }
     return 0;
 }
