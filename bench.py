@@ -298,8 +298,8 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                          "algorithmic_bytes_per_world_step": bytes_ws,
-                         "kernel": (f"one step's launch group ({native.load().goib2d_kernels_per_step(n)} part "
-                                    f"kernels{' + the reset kernel' if resets else ''}), timed as one unit by the "
+                         "kernel": (f"one step's launch group ({native.load().goib2d_kernels_per_step(n)} "
+                                    f"kernel(s){' + the reset kernel' if resets else ''}), timed as one unit by the "
                                     "per-step CUDA events"),
                          "traffic_source": f"profiles/traffic_{args.config}.json (ncu dram bytes of the launch group)"
                                            if traffic is not None else None},

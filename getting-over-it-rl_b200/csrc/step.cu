@@ -85,7 +85,14 @@ struct Ctx {
     int status;
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
     int64_t world;
+    int nsync;  // threads that meet at phase_sync (the block's working warps), or 0
 };
+
+// The whole-step kernel's block barrier between phases (named barrier 1, the block's working warps only): every
+// working warp of the block runs each phase of the step, so all of them reach every phase_sync in the same order.
+__device__ __forceinline__ void phase_sync(const Ctx &x) {
+    if (x.nsync) asm volatile("bar.sync 1, %0;" ::"r"(x.nsync) : "memory");
+}
 
 // ---- contact event log (the reference C API's Begin / End / PostSolve listener, capi.cpp:45-78)
 enum { EV_BEGIN = 0, EV_END = 1, EV_POST_SOLVE = 2 };
@@ -575,6 +582,7 @@ __device__ IslandWork solve(Ctx &x, float dt, float dt_ratio) {
     const Layout &L = x.p.lay;
     IslandOut isl = find_islands(x);
     GB_PHASE(x, 2);
+    phase_sync(x);
     int *bisl = ap<int>(x, L.bisl), *corder = ap<int>(x, L.corder), *cisl = ap<int>(x, L.cisl);
     int *jorder = ap<int>(x, L.jorder);
     const IslandWork sw = sweep_of(x, isl.n_contacts);
@@ -1250,8 +1258,8 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
 #endif
 }
 
-// b2World::Step (step.py:28-47) in parts, each a kernel of its own (the parts' code is large, and warps that run
-// the same part at the same time share the SM's instruction cache). One warp per world:
+// b2World::Step (step.py:28-47) in parts; one warp per world. Below THREAD_SWEEPS_MIN_WORLDS a step is one launch
+// (goib2d_step_kernel: parts 0, 1, 5 with a block barrier between them); above it each part is a kernel of its own.
 //   0  the action channels, FindNewContacts for new fixtures, b2ContactManager::Collide
 //   1  b2World::Solve: islands, velocity integration, the constraint rows (solve), the constraint sweeps on lane 0
 //      (solve_constraints), write back and sleep (solve_finish), SynchronizeFixtures and FindNewContacts
@@ -1259,24 +1267,13 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
 //      the sweeps between the first two run one world per thread (goib2d_constraints_kernel)
 //   5  SolveTOI, then the end of the step (inv_dt0, cleared forces; the status word after the last step)
 // Every value one part hands the next is in the State or the world's arena.
+// One part of one world's step on this warp: w is the world's bound State, hot / rows its shared-memory regions
+// (or null).
 template <int PART>
-__device__ __forceinline__ void step_part(const StepParams &p) {
-    const int warp = threadIdx.x >> 5;
-    const int64_t world = p.world0 + (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
-    if (world >= p.world_end) return;
-    __shared__ W s_world[4];  // blockDim.x <= 128
-    if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
-    __syncwarp();
-    // the per-step kernels (collide, fused solve, TOI) keep the arena's hot part in shared memory: every arena array
-    // they use is written and read within the kernel; the large-batch split solve passes arrays between kernels
-    extern __shared__ __align__(16) char dyn_smem[];
-    const bool hot = (PART == 0 || PART == 1 || PART == 5) && p.lay.hot_end > 0;
-    const bool rows = hot && (PART == 1 || PART == 5) && p.lay.rows_bytes;  // the solve's and the TOI island's rows
-    const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
-    char *mine = dyn_smem + warp * region;
-    Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
-          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64(),
-          world};
+__device__ __forceinline__ void run_part(const StepParams &p, int64_t world, W &w_, char *hot, char *rows,
+                                         int nsync) {
+    Ctx x{p, p.m, p.s, w_, p.scratch + world * p.lay.stride, hot, rows, (int)(threadIdx.x & 31), 0, clock64(),
+          world, nsync};
     W &w = x.w;
     const float dt = p.dt;
 #ifdef GOIB2D_PHASE_TIMERS
@@ -1297,13 +1294,16 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
         GB_SPAN(x, 9, false);
     } else if (PART == 1) {  // the whole of b2World::Solve, the sweeps on lane 0
         const IslandWork sw = solve(x, dt, *w.inv_dt0 * dt);
+        phase_sync(x);
         if (x.lane == 0)
             solve_constraints(p, world, sw,
                               {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
                                ap<int>(x, p.lay.jisl)});
         __syncwarp();
         GB_PHASE(x, 5);
+        phase_sync(x);
         solve_finish(x, dt, sw);
+        phase_sync(x);
         broadphase(x);
         GB_SPAN(x, 6, false);
     } else if (PART == 2) {
@@ -1336,6 +1336,55 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     }
 }
 
+template <int PART>
+__device__ __forceinline__ void step_part(const StepParams &p) {
+    const int warp = threadIdx.x >> 5;
+    const int64_t world = p.world0 + (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    if (world >= p.world_end) return;
+    __shared__ W s_world[4];  // blockDim.x <= 128
+    if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
+    __syncwarp();
+    // the per-step kernels (collide, fused solve, TOI) keep the arena's hot part in shared memory: every arena array
+    // they use is written and read within the kernel; the large-batch split solve passes arrays between kernels
+    extern __shared__ __align__(16) char dyn_smem[];
+    const bool hot = (PART == 0 || PART == 1 || PART == 5) && p.lay.hot_end > 0;
+    const bool rows = hot && (PART == 1 || PART == 5) && p.lay.rows_bytes;  // the solve's and the TOI island's rows
+    const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
+    char *mine = dyn_smem + warp * region;
+    run_part<PART>(p, world, s_world[warp], hot ? mine : nullptr, rows ? mine + p.lay.hot_end : nullptr, 0);
+}
+
+// The whole step in one launch (batches below THREAD_SWEEPS_MIN_WORLDS): one warp per world, one block of up to
+// STEP_MAX_WARPS worlds per SM, the block's warps starting each phase together (phase_sync: collide | islands | rows |
+// sweeps | write back and sleep | broadphase | TOI). Worlds are independent, so a phase's tail is the slowest of the
+// block's worlds rather than of the whole batch, and every warp of an SM runs the same phase at the same time (the
+// step's code does not fit the SM's instruction cache; warps spread over all phases thrash it). Per warp in dynamic
+// shared memory: the bound State, the arena's hot part and the rows region.
+constexpr int STEP_MAX_WARPS = 28;       // 72 registers per thread: 28 warps per SM
+constexpr int STEP_MAX_SMEM = 232448;    // dynamic shared memory per block
+__host__ __device__ __forceinline__ int step_region(const Layout &L) {
+    return (int)((sizeof(W) + 15) & ~size_t(15)) + L.hot_end + (L.hot_end > 0 ? L.rows_bytes : 0);
+}
+__device__ __forceinline__ void whole_step(const StepParams &p) {
+    const int warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+    const int64_t first = p.world0 + (int64_t)blockIdx.x * wpb, world = first + warp;
+    if (world >= p.world_end) return;  // the block's spare warps (last block only) take no part
+    const int64_t left = p.world_end - first;
+    const int nsync = 32 * (int)(left < wpb ? left : wpb);
+    extern __shared__ __align__(16) char dyn_smem[];
+    char *mine = dyn_smem + warp * step_region(p.lay);
+    W &w = *reinterpret_cast<W *>(mine);
+    char *hot = p.lay.hot_end > 0 ? mine + ((sizeof(W) + 15) & ~size_t(15)) : nullptr;
+    char *rows = hot && p.lay.rows_bytes ? hot + p.lay.hot_end : nullptr;
+    if ((threadIdx.x & 31) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
+    __syncwarp();
+    run_part<0>(p, world, w, hot, nullptr, nsync);
+    asm volatile("bar.sync 1, %0;" ::"r"(nsync) : "memory");
+    run_part<1>(p, world, w, hot, rows, nsync);
+    asm volatile("bar.sync 1, %0;" ::"r"(nsync) : "memory");
+    run_part<5>(p, world, w, hot, rows, 0);
+}
+
 }  // namespace gb
 
 using namespace gb;
@@ -1348,10 +1397,6 @@ using namespace gb;
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_collide_kernel(const __grid_constant__ StepParams p) {
     step_part<0>(p);
-}
-extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
-    goib2d_solve_kernel(const __grid_constant__ StepParams p) {
-    step_part<1>(p);
 }
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_solve_rows_kernel(const __grid_constant__ StepParams p) {
@@ -1378,33 +1423,58 @@ extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_toi_kernel(const __grid_constant__ StepParams p) {
     step_part<5>(p);
 }
+// the whole step, one warp per world, up to STEP_MAX_WARPS worlds per block (whole_step)
+extern "C" __global__ void __launch_bounds__(32 * STEP_MAX_WARPS, 1)
+    goib2d_step_kernel(const __grid_constant__ StepParams p) {
+    whole_step(p);
+}
 
 namespace gb {
 // From this many worlds the constraint sweeps run one world per thread: 32 worlds' sweeps share a warp's issue
 // slots, which pays once the batch fills the SMs with warps of sweeps; below it a warp per world keeps more warps in
 // flight per SM. (Both run the same code, in the same order within a world.)
 constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = 16384;
-// p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: per step the collide part, the solve
-// part (the fused kernel, or for large batches rows / thread sweeps / finish and the broadphase part), the TOI part
-int kernels_per_step(int64_t n_worlds) { return n_worlds < THREAD_SWEEPS_MIN_WORLDS ? 3 : 6; }
+// p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: per step one goib2d_step_kernel, or for
+// large batches the collide part, the solve part in pieces (rows / thread sweeps / finish / broadphase), the TOI part
+int kernels_per_step(int64_t n_worlds) { return n_worlds < THREAD_SWEEPS_MIN_WORLDS ? 1 : 6; }
 
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
-    const int wpb = 4;  // worlds (warps) per block
     p.world0 = 0, p.world_end = p.n_worlds;
     const int64_t n = p.n_worlds;
+    if (n < THREAD_SWEEPS_MIN_WORLDS) {  // one launch per step
+        int dev = 0, sms = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int region = step_region(p.lay);
+        int wpb = (int)((n + sms - 1) / sms);  // one block per SM where the batch allows
+        wpb = wpb < 1 ? 1 : (wpb > STEP_MAX_WARPS ? STEP_MAX_WARPS : wpb);
+        const int fit = STEP_MAX_SMEM / region;
+        wpb = wpb > fit ? fit : wpb;
+        const size_t smem = (size_t)wpb * region;
+        static int smem_set[64];  // the dynamic shared memory limit set per device
+        if (dev < 64 && smem > 48 * 1024 && (size_t)smem_set[dev] < smem) {
+            cudaError_t e = cudaFuncSetAttribute(goib2d_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+            smem_set[dev] = (int)smem;
+        }
+        const unsigned sblocks = (unsigned)((n + wpb - 1) / wpb);
+        for (int k = 0; k < p.n_steps; ++k) {
+            p.step = k;
+            goib2d_step_kernel<<<sblocks, 32 * wpb, smem, stream>>>(p);
+        }
+        return cudaGetLastError();
+    }
+    const int wpb = 4;  // worlds (warps) per block
     const unsigned blocks = (unsigned)((n + wpb - 1) / wpb);
     const size_t hot = (size_t)wpb * p.lay.hot_end;  // dynamic shared memory of the per-step kernels
     for (int k = 0; k < p.n_steps; ++k) {
         p.step = k;
         goib2d_collide_kernel<<<blocks, 32 * wpb, hot, stream>>>(p);
-        if (n < THREAD_SWEEPS_MIN_WORLDS) {
-            goib2d_solve_kernel<<<blocks, 32 * wpb, hot + (size_t)wpb * p.lay.rows_bytes, stream>>>(p);
-        } else {
-            goib2d_solve_rows_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
-            goib2d_constraints_kernel<<<(unsigned)((n + 31) / 32), 32, 0, stream>>>(p);
-            goib2d_finish_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
-            goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
-        }
+        goib2d_solve_rows_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        goib2d_constraints_kernel<<<(unsigned)((n + 31) / 32), 32, 0, stream>>>(p);
+        goib2d_finish_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
+        goib2d_broadphase_kernel<<<blocks, 32 * wpb, 0, stream>>>(p);
         goib2d_toi_kernel<<<blocks, 32 * wpb, hot ? hot + (size_t)wpb * p.lay.rows_bytes : 0, stream>>>(p);
     }
     return cudaGetLastError();

@@ -137,9 +137,9 @@ int goib2d_status(goib2d_model *model, const int32_t **device_status, int64_t *n
 /* The same status words copied to host memory (n <= the last step's n_worlds); synchronises the device. */
 int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
 
-/* Kernel launches one goib2d_step step makes for a batch of n_worlds worlds: 3, or 6 for batches of 16384 worlds
- * and more (their constraint sweeps run one world per thread). For launch accounting and profilers; no counterpart
- * in the reference engine. */
+/* Kernel launches one goib2d_step step makes for a batch of n_worlds worlds: 1 (the whole step in one launch), or
+ * 6 for batches of 16384 worlds and more (collide, the solve in four pieces with the constraint sweeps run one
+ * world per thread, TOI). For launch accounting and profilers; no counterpart in the reference engine. */
 int goib2d_kernels_per_step(int64_t n_worlds);
 
 /* ---- Env helpers around the step (no counterpart in the reference engine, whose RL env is outside it). Same
