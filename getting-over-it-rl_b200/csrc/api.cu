@@ -92,7 +92,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);
-    // the fused solve kernel's constraint rows in shared memory (after the hot part): the joint rows and the first
+    // the step kernel's constraint rows in shared memory (after the hot part): the joint rows and the first
     // contact rows, within a small budget, so that 7 blocks of 4 warps per SM keep most of the L1 cache
 #ifndef GOIB2D_ROWS_MAX_BYTES
 #define GOIB2D_ROWS_MAX_BYTES 1536

@@ -112,7 +112,7 @@ struct Layout {
     int64_t stride;  // bytes per world (multiple of 256)
     // Shared-memory copies (per warp) used by the per-step kernels: the arena's first hot_end bytes - the small
     // arrays whose writes the sequential phases read back, which through global memory is an L2 round trip each
-    // (0: the arena only) - and, in the fused solve kernel after them, rows_bytes of constraint rows: the joint rows
+    // (0: the arena only) - and, in the step kernel after them, rows_bytes of constraint rows: the joint rows
     // at sm_jr and up to sm_vc_cap contact rows at sm_vc (see IslandWork in step.cu)
     int hot_end, rows_bytes, sm_jr, sm_vc, sm_vc_cap;
 };
@@ -125,8 +125,8 @@ struct StepParams {
     int C, rows;
     int64_t n_worlds;
     int n_steps;
-    int step;        // index of the step a part kernel belongs to
-    int64_t world0;  // a part kernel's launch covers worlds world0 .. world_end - 1
+    int step;        // index of the step a launch belongs to
+    int64_t world0;  // a launch covers worlds world0 .. world_end - 1
     int64_t world_end;
     const float *actions;
     int n_action;

@@ -1,4 +1,5 @@
-// goib2d: the batched b2World::Step for sm_100a. One warp per world; each step runs as a sequence of part kernels.
+// goib2d: the batched b2World::Step for sm_100a. One warp per world; a step is one launch (goib2d_step_kernel), or
+// for batches of 16384 worlds and more a sequence of part kernels.
 //
 // Mapping. Each world's State is a row of every leaf (contiguous per world), so a warp reads and writes its own
 // world with unit-stride lane accesses. Data-parallel phases run one element per lane: the candidate-pair scan
@@ -14,11 +15,15 @@
 #ifdef GOIB2D_PHASE_TIMERS
 namespace gb {
 __device__ unsigned long long g_phase_cycles[16];
-#define GB_PHASE(x, i)                                                                       \
-    do {                                                                                     \
-        long long t1_ = clock64();                                                           \
-        if ((x).lane == 0) atomicAdd(&g_phase_cycles[i], (unsigned long long)(t1_ - (x).t0)); \
-        (x).t0 = t1_;                                                                        \
+__device__ unsigned long long g_phase_max[16];  // the longest single warp's time in each phase
+#define GB_PHASE(x, i)                                                                             \
+    do {                                                                                           \
+        long long t1_ = clock64();                                                                 \
+        if ((x).lane == 0) {                                                                       \
+            atomicAdd(&g_phase_cycles[i], (unsigned long long)(t1_ - (x).t0));                     \
+            atomicMax(&g_phase_max[i], (unsigned long long)(t1_ - (x).t0));                        \
+        }                                                                                          \
+        (x).t0 = t1_;                                                                              \
     } while (0)
 // 0 events, 1 TOI position passes, 2 TOI solves, 3 searches, 4 max events, 5 TOI cycles, 6 outer iterations,
 // 7 push-backs, 8 root-finder steps, 9 GJK iterations, 10-13 TOI outcomes
@@ -80,7 +85,7 @@ struct Ctx {
     W &w;  // shared memory, one per warp: a per-thread copy would cost 32x its size in local memory
     char *scr;   // the world's arena (global memory)
     char *hot;   // this warp's shared copy of the arena's hot part (Layout::hot_end), or null
-    char *rows;  // this warp's shared constraint rows (the fused solve kernel), or null
+    char *rows;  // this warp's shared constraint rows (solve and TOI phases), or null
     int lane;
     int status;
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
@@ -90,8 +95,9 @@ struct Ctx {
 
 // The whole-step kernel's block barrier between phases (named barrier 1, the block's working warps only): every
 // working warp of the block runs each phase of the step, so all of them reach every phase_sync in the same order.
-__device__ __forceinline__ void phase_sync(const Ctx &x) {
+__device__ __forceinline__ void phase_sync(Ctx &x) {
     if (x.nsync) asm volatile("bar.sync 1, %0;" ::"r"(x.nsync) : "memory");
+    GB_PHASE(x, 4);  // profiling builds: the wait counts as phase 4
 }
 
 // ---- contact event log (the reference C API's Begin / End / PostSolve listener, capi.cpp:45-78)
@@ -546,7 +552,7 @@ __device__ __forceinline__ Bodies bodies_of(Ctx &x) {
 }
 
 // Where the island solve keeps its working set: the body arrays, the per-island flags of the position iterations,
-// the joint rows and the contact rows. In the world's arena, or (the fused solve kernel) in the warp's region of
+// the joint rows and the contact rows. In the world's arena, or (the step kernel) in the warp's region of
 // shared memory: the Gauss-Seidel sweeps store a body's velocity and read it back in the next constraint, which
 // through global memory is a ~680-cycle round trip on this part (stores do not stay in L1) and through shared
 // memory ~30. Islands with more contact rows than the region holds keep those rows in the arena.
@@ -1344,7 +1350,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     __shared__ W s_world[4];  // blockDim.x <= 128
     if ((threadIdx.x & 31) == 0) bind_world(s_world[warp], p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
-    // the per-step kernels (collide, fused solve, TOI) keep the arena's hot part in shared memory: every arena array
+    // the collide and TOI part kernels keep the arena's hot part in shared memory: every arena array
     // they use is written and read within the kernel; the large-batch split solve passes arrays between kernels
     extern __shared__ __align__(16) char dyn_smem[];
     const bool hot = (PART == 0 || PART == 1 || PART == 5) && p.lay.hot_end > 0;
@@ -1487,12 +1493,14 @@ extern "C" int goib2d_debug_phase_cycles(unsigned long long *out, int reset) {
     if (cudaMemcpyFromSymbol(out + 16, g_counts, sizeof(g_counts)) != cudaSuccess) return -2;
     if (cudaMemcpyFromSymbol(out + 32, g_toi_cycles, sizeof(g_toi_cycles)) != cudaSuccess) return -2;
     if (cudaMemcpyFromSymbol(out + 48, g_span, sizeof(g_span)) != cudaSuccess) return -2;
+    if (cudaMemcpyFromSymbol(out + 64, g_phase_max, sizeof(g_phase_max)) != cudaSuccess) return -2;
     if (reset) {
         unsigned long long z[16] = {0};
         cudaMemcpyToSymbol(g_phase_cycles, z, sizeof(z));
         cudaMemcpyToSymbol(g_counts, z, sizeof(z));
         cudaMemcpyToSymbol(g_toi_cycles, z, sizeof(g_toi_cycles));
         cudaMemcpyToSymbol(g_span, z, sizeof(g_span));
+        cudaMemcpyToSymbol(g_phase_max, z, sizeof(g_phase_max));
     }
     return 0;
 }
