@@ -221,6 +221,7 @@ struct goib2d_model {
     int32_t n_action = 0;
     int32_t *action_joint = nullptr;
     float *action_scale = nullptr;
+    int32_t step_mode = 0;  // goib2d_set_step_mode
     int32_t event_cap = 0;  // contact event log per world (0: off)
     goib2d_event *events = nullptr;
     int32_t *event_count = nullptr;
@@ -444,6 +445,7 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
     p.m = *dm;
     for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
     p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
+    p.step_mode = m->step_mode;
     p.lay = scratch_layout(dm->B, C, dm->J, dm->P, dm->grid ? dm->max_hits : 0);
     size_t need = (size_t)p.lay.stride * (size_t)n_worlds;
     if (need > m->scratch_bytes) {
@@ -479,6 +481,14 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
     }
     if ((n_worlds + 3) / 4 > 0x7fffffff) return fail(GOIB2D_ELIMIT, "too many worlds");
     CUDA_TRY(gb::launch_steps(p, (cudaStream_t)stream));
+    return 0;
+}
+
+int goib2d_set_step_mode(goib2d_model *m, int32_t mode) {
+    if (!m) return fail(GOIB2D_EINVAL, "null argument");
+    if (mode < 0 || mode > 2) return fail(GOIB2D_EINVAL, "step mode %d: 0 (per batch), 1 or 2 worlds per warp", mode);
+    std::lock_guard<std::mutex> lk(m->mu);
+    m->step_mode = mode;
     return 0;
 }
 
@@ -593,6 +603,7 @@ int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int
     p.m = *dm;
     for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
     p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
+    p.step_mode = m->step_mode;
     p.scratch = scratch;
     p.status = nullptr;  // no per-world status words (their buffer would need an allocation)
     if (actions && m->n_action > 0) {

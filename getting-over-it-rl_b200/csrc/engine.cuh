@@ -125,6 +125,7 @@ struct StepParams {
     int C, rows;
     int64_t n_worlds;
     int n_steps;
+    int step_mode;   // below 16384 worlds: 0 chosen per batch, 1 one world per warp, 2 two worlds per warp
     int step;        // index of the step a launch belongs to
     int64_t world0;  // a launch covers worlds world0 .. world_end - 1
     int64_t world_end;

@@ -82,22 +82,27 @@ struct Ctx {
     const StepParams &p;
     const DevModel &m;
     const goib2d_settings &s;
-    W &w;  // shared memory, one per warp: a per-thread copy would cost 32x its size in local memory
+    W &w;  // shared memory, one per world: a per-thread copy would cost 32x its size in local memory
     char *scr;   // the world's arena (global memory)
-    char *hot;   // this warp's shared copy of the arena's hot part (Layout::hot_end), or null
-    char *rows;  // this warp's shared constraint rows (solve and TOI phases), or null
-    int lane;
+    char *hot;   // this world's shared copy of the arena's hot part (Layout::hot_end), or null
+    char *rows;  // this world's shared constraint rows (solve and TOI phases), or null
+    int lane;    // the thread's lane in the world's group, 0 .. wl - 1
     int status;
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
     int64_t world;
-    int nsync;  // threads that meet at phase_sync (the block's working warps), or 0
+    unsigned gmask;  // the world's lanes in the warp: all 32, or one half (the step kernel: two worlds per warp)
+    int gbase, wl;   // the group's first lane in the warp, and its width (32 or 16)
 };
 
-// The whole-step kernel's block barrier between phases (named barrier 1, the block's working warps only): every
-// working warp of the block runs each phase of the step, so all of them reach every phase_sync in the same order.
-__device__ __forceinline__ void phase_sync(Ctx &x) {
-    if (x.nsync) asm volatile("bar.sync 1, %0;" ::"r"(x.nsync) : "memory");
-    GB_PHASE(x, 4);  // profiling builds: the wait counts as phase 4
+// Warp collectives over the world's own group of lanes. Every function below runs all of a world's lanes through
+// the same sequence of these calls; the two worlds of a warp may be at different calls at the same time.
+__device__ __forceinline__ void gsync(const Ctx &x) { __syncwarp(x.gmask); }
+__device__ __forceinline__ unsigned gballot(const Ctx &x, bool pred) {
+    return (__ballot_sync(x.gmask, pred) & x.gmask) >> x.gbase;  // bit i: the group's lane i
+}
+template <class T>
+__device__ __forceinline__ T gshfl(const Ctx &x, T v, int src) {  // from the group's lane src
+    return __shfl_sync(x.gmask, v, src, x.wl);
 }
 
 // ---- contact event log (the reference C API's Begin / End / PostSolve listener, capi.cpp:45-78)
@@ -176,7 +181,7 @@ __device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits) {
             for (int cx = cx0; cx <= cx1; ++cx) {
                 int c = cy * m.nx + cx;
                 int b0 = m.cell_start[c], b1 = m.cell_start[c + 1];
-                for (int base = b0; base < b1; base += 32) {
+                for (int base = b0; base < b1; base += x.wl) {
                     int i = base + lane, p = -1;
                     if (i < b1) {
                         int si = m.cell_items[i];
@@ -190,7 +195,7 @@ __device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits) {
                             if (pc >= 0 && is_new_pair(x, pc, bitmap)) p = pc;
                         }
                     }
-                    unsigned mk = __ballot_sync(FULL, p >= 0);
+                    unsigned mk = gballot(x, p >= 0);
                     if (p >= 0) {
                         int k = n + __popc(mk & ((1u << lane) - 1));
                         if (k < cap) hits[k] = p;
@@ -199,17 +204,17 @@ __device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits) {
                 }
             }
     }
-    for (int base = 0; base < m.n_dd; base += 32) {  // pairs of two non-static fixtures: every one, in order
+    for (int base = 0; base < m.n_dd; base += x.wl) {  // pairs of two non-static fixtures: every one, in order
         int i = base + lane, p = -1;
         if (i < m.n_dd && is_new_pair(x, m.dd[i], bitmap)) p = m.dd[i];
-        unsigned mk = __ballot_sync(FULL, p >= 0);
+        unsigned mk = gballot(x, p >= 0);
         if (p >= 0) {
             int k = n + __popc(mk & ((1u << lane) - 1));
             if (k < cap) hits[k] = p;
         }
         n += __popc(mk);
     }
-    __syncwarp();
+    gsync(x);
     return n <= cap ? n : -1;
 }
 
@@ -221,42 +226,42 @@ __device__ void find_new_contacts(Ctx &x) {
     uint32_t *bitmap = ap<uint32_t>(x, x.p.lay.bitmap);
     int *freeslot = ap<int>(x, x.p.lay.freeslot);
     const int nw = (P + 31) >> 5;
-    for (int i = lane; i < nw; i += 32) bitmap[i] = 0u;
-    __syncwarp();
-    for (int s = lane; s < C; s += 32) {
+    for (int i = lane; i < nw; i += x.wl) bitmap[i] = 0u;
+    gsync(x);
+    for (int s = lane; s < C; s += x.wl) {
         int pr = w.pair[s];
         if (pr >= 0 && pr < P) atomicOr(&bitmap[pr >> 5], 1u << (pr & 31));
     }
     int n_free = 0;
-    for (int base = 0; base < C; base += 32) {
+    for (int base = 0; base < C; base += x.wl) {
         int s = base + lane;
         bool f = s < C && w.pair[s] < 0;
-        unsigned mk = __ballot_sync(FULL, f);
+        unsigned mk = gballot(x, f);
         if (f) freeslot[n_free + __popc(mk & ((1u << lane) - 1))] = s;
         n_free += __popc(mk);
     }
     const int key0 = *w.next_key;
-    __syncwarp();
+    gsync(x);
     int n_new = -1;
     if (m.grid) {
         int *hits = ap<int>(x, x.p.lay.hits), *sorted = hits + m.max_hits;
         n_new = grid_new_pairs(x, bitmap, hits);
         if (n_new > 0) {  // into candidate order (the hits are distinct), then into the lowest free slots
-            for (int i = lane; i < n_new; i += 32) {
+            for (int i = lane; i < n_new; i += x.wl) {
                 int h = hits[i], rank = 0;
                 for (int j = 0; j < n_new; ++j) rank += hits[j] < h;
                 sorted[rank] = h;
             }
-            __syncwarp();
-            for (int k = lane; k < n_new && k < n_free; k += 32) place_contact(x, freeslot[k], sorted[k], key0 + k);
+            gsync(x);
+            for (int k = lane; k < n_new && k < n_free; k += x.wl) place_contact(x, freeslot[k], sorted[k], key0 + k);
         }
     }
     if (n_new < 0) {  // the scan path
         n_new = 0;
-        for (int base = 0; base < P; base += 32) {
+        for (int base = 0; base < P; base += x.wl) {
             int p = base + lane;
             bool nw_ = p < P && is_new_pair(x, p, bitmap);
-            unsigned mk = __ballot_sync(FULL, nw_);
+            unsigned mk = gballot(x, nw_);
             if (nw_) {
                 int rank = n_new + __popc(mk & ((1u << lane) - 1));
                 if (rank < n_free) place_contact(x, freeslot[rank], p, key0 + rank);
@@ -264,14 +269,14 @@ __device__ void find_new_contacts(Ctx &x) {
             n_new += __popc(mk);
         }
     }
-    __syncwarp();
+    gsync(x);
     if (lane == 0) {
         *w.next_key = key0 + n_new;
         int placed = n_new < n_free ? n_new : n_free;
         *w.overflow += n_new - placed;
         if (n_new > placed) x.status |= ST_OVERFLOW;
     }
-    __syncwarp();
+    gsync(x);
 }
 
 // Live slots in contact-list order (descending key): order[0..n) and each slot's position lpos[slot] (C if dead)
@@ -279,7 +284,7 @@ __device__ int list_order(Ctx &x, int *order, int *lpos) {
     W &w = x.w;
     const int C = w.C, lane = x.lane;
     int n_live = 0;
-    for (int base = 0; base < C; base += 32) {
+    for (int base = 0; base < C; base += x.wl) {
         int s = base + lane;
         bool live = s < C && w.pair[s] >= 0;
         if (s < C) {
@@ -293,9 +298,9 @@ __device__ int list_order(Ctx &x, int *order, int *lpos) {
             }
             lpos[s] = pos;
         }
-        n_live += __popc(__ballot_sync(FULL, live));
+        n_live += __popc(gballot(x, live));
     }
-    __syncwarp();
+    gsync(x);
     return n_live;
 }
 
@@ -309,22 +314,22 @@ __device__ void collide(Ctx &x) {
     int *over = ap<int>(x, L.over), *aw = ap<int>(x, L.aw);
     Man *man = ap<Man>(x, L.man);
     int n_live = list_order(x, order, lpos);
-    for (int s = lane; s < C; s += 32) {
+    for (int s = lane; s < C; s += x.wl) {
         active[s] = 0;
         if (w.pair[s] < 0) continue;
         int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
         over[s] = overlap(fixture_fat(m, w, w.fa[s]), fixture_fat(m, w, w.fb[s]));
         evaluate(m, w.fa[s], w.fb[s], w.bxf(ba), w.bxf(bb), x.s.linear_slop, x.s.angular_slop, man[s]);
     }
-    for (int b = lane; b < B; b += 32) aw[b] = w.awake[b];
-    __syncwarp();
+    for (int b = lane; b < B; b += x.wl) aw[b] = w.awake[b];
+    gsync(x);
     // The walk newest first (pairs.py:60-90): a contact is visited when one of its bodies is awake and not static,
     // and a visited contact whose touching state changes wakes both bodies for the contacts after it. Between two
     // wakes of a non-static body nothing changes, so each round settles, in parallel, every contact up to the next
     // such wake, which lane 0 then applies. Wakes of static bodies only reach their awake flag, at the end.
     for (int k0 = 0;;) {
         int first = n_live;
-        for (int base = k0; base < n_live; base += 32) {
+        for (int base = k0; base < n_live; base += x.wl) {
             int k = base + lane, s = -1;
             bool visit = false, wakes = false, change = false;
             if (k < n_live) {
@@ -335,7 +340,7 @@ __device__ void collide(Ctx &x) {
                 wakes = over[s] ? ((man[s].count > 0) != (bool)w.touching[s]) : (w.count[s] > 0);
                 change = visit && wakes && ((!sa && !aw[ba]) || (!sb && !aw[bb]));
             }
-            unsigned mk = __ballot_sync(FULL, change);
+            unsigned mk = gballot(x, change);
             int f = mk ? base + __ffs(mk) - 1 : n_live;
             if (s >= 0 && k <= f) active[s] = visit && wakes ? 2 : (int)visit;
             if (mk) {
@@ -343,19 +348,19 @@ __device__ void collide(Ctx &x) {
                 break;
             }
         }
-        __syncwarp();
+        gsync(x);
         if (first == n_live) break;
         if (lane == 0) {
             int s = order[first];
             aw[m.fixture_body[w.fa[s]]] = 1, aw[m.fixture_body[w.fb[s]]] = 1;
         }
-        __syncwarp();
+        gsync(x);
         k0 = first + 1;
     }
-    for (int s = lane; s < C; s += 32)  // wakes of static bodies (value 2: visited and waking)
+    for (int s = lane; s < C; s += x.wl)  // wakes of static bodies (value 2: visited and waking)
         if (active[s] == 2) aw[m.fixture_body[w.fa[s]]] = 1, aw[m.fixture_body[w.fb[s]]] = 1, active[s] = 1;
-    __syncwarp();
-    for (int s = lane; s < C; s += 32) {
+    gsync(x);
+    for (int s = lane; s < C; s += x.wl) {
         if (!active[s]) continue;
         int ev = -1;  // the event this update raises
         if (!over[s]) {
@@ -367,22 +372,22 @@ __device__ void collide(Ctx &x) {
         active[s] = ev + 1;  // reused: the event of each visited slot
     }
     if (x.p.events) {  // the step's log starts with Collide's events, in contact-list order
-        __syncwarp();
+        gsync(x);
         int n = 0;
-        for (int base = 0; base < n_live; base += 32) {
+        for (int base = 0; base < n_live; base += x.wl) {
             int k = base + lane, s = k < n_live ? order[k] : -1;
             int ev = s >= 0 ? active[s] - 1 : -1;
-            unsigned mk = __ballot_sync(FULL, ev >= 0);
+            unsigned mk = gballot(x, ev >= 0);
             if (ev >= 0) put_event(x.p, x.world, n + __popc(mk & ((1u << lane) - 1)), ev, w.fa[s], w.fb[s]);
             n += __popc(mk);
         }
         if (lane == 0) x.p.event_count[x.world] = n;
     }
-    for (int b = lane; b < B; b += 32) {
+    for (int b = lane; b < B; b += x.wl) {
         if (aw[b] && !w.awake[b]) w.sleep_time[b] = 0.0f;
         w.awake[b] = aw[b];
     }
-    __syncwarp();
+    gsync(x);
 }
 
 // ---------------------------------------------------------------- islands (island.py:41-140), lane 0
@@ -402,19 +407,19 @@ __device__ IslandOut find_islands(Ctx &x) {
     int *adj_start = ap<int>(x, L.adj_start), *adj_cur = ap<int>(x, L.adj_cur);
     int2 *adj = ap<int2>(x, L.adj);
     int n_live = list_order(x, order, lpos);
-    for (int s = lane; s < C; s += 32) cisl[s] = -1, cflag[s] = 0;
-    for (int j = lane; j < J; j += 32) jisl[j] = -1, jflag[j] = 0;
-    for (int b = lane; b < B; b += 32) bisl[b] = -1, bflag[b] = 0, adj_cur[b] = 0;
-    __syncwarp();
+    for (int s = lane; s < C; s += x.wl) cisl[s] = -1, cflag[s] = 0;
+    for (int j = lane; j < J; j += x.wl) jisl[j] = -1, jflag[j] = 0;
+    for (int b = lane; b < B; b += x.wl) bisl[b] = -1, bflag[b] = 0, adj_cur[b] = 0;
+    gsync(x);
     // The contact graph the walk follows: the touching contacts in list order (edges) and, per non-static body, its
     // edges in that order with the body at the other end (~body when that one is static). Walking a body's list is
     // the reference's scan of every edge for those incident to the body, in the same order.
     int n_edges = 0;
-    for (int base = 0; base < n_live; base += 32) {
+    for (int base = 0; base < n_live; base += x.wl) {
         int k = base + lane;
         int s = k < n_live ? order[k] : -1;
         bool t = s >= 0 && w.touching[s];
-        unsigned mk = __ballot_sync(FULL, t);
+        unsigned mk = gballot(x, t);
         if (t) {
             edges[n_edges + __popc(mk & ((1u << lane) - 1))] = s;
             int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
@@ -423,21 +428,21 @@ __device__ IslandOut find_islands(Ctx &x) {
         }
         n_edges += __popc(mk);
     }
-    __syncwarp();
+    gsync(x);
     int run = 0;  // exclusive scan of the degrees
-    for (int base = 0; base < B; base += 32) {
+    for (int base = 0; base < B; base += x.wl) {
         int b = base + lane;
         int d = b < B ? adj_cur[b] : 0, inc = d;
-        for (int o = 1; o < 32; o <<= 1) {
-            int t = __shfl_up_sync(FULL, inc, o);
+        for (int o = 1; o < x.wl; o <<= 1) {
+            int t = __shfl_up_sync(x.gmask, inc, o, x.wl);
             if (lane >= o) inc += t;
         }
         if (b < B) adj_start[b] = run + inc - d, adj_cur[b] = 0;
-        run += __shfl_sync(FULL, inc, 31);
+        run += gshfl(x, inc, x.wl - 1);
     }
     if (lane == 0) adj_start[B] = run;
-    __syncwarp();
-    for (int base = 0; base < n_edges; base += 32) {  // fill 32 edges at a time, in edge order within each list
+    gsync(x);
+    for (int base = 0; base < n_edges; base += x.wl) {  // fill 32 edges at a time, in edge order within each list
         int e = base + lane;
         int s = -1, a = -1, b = -1, oa = 0, ob = 0;
         if (e < n_edges) {
@@ -448,16 +453,16 @@ __device__ IslandOut find_islands(Ctx &x) {
             oa = sb ? ~bb : bb, ob = sa ? ~ba : ba;           // the other end, seen from a and from b
         }
         int ra = 0, rb = 0;  // incidences of a (of b) on earlier lanes of this chunk
-        for (int j = 0; j < 32; ++j) {
-            int aj = __shfl_sync(FULL, a, j), bj = __shfl_sync(FULL, b, j);
+        for (int j = 0; j < x.wl; ++j) {
+            int aj = gshfl(x, a, j), bj = gshfl(x, b, j);
             if (j < lane) ra += (aj == a) + (bj == a), rb += (aj == b) + (bj == b);
         }
         if (a >= 0) adj[adj_start[a] + adj_cur[a] + ra] = make_int2(s, oa);
         if (b >= 0) adj[adj_start[b] + adj_cur[b] + rb] = make_int2(s, ob);
-        __syncwarp();
+        gsync(x);
         if (a >= 0) atomicAdd(&adj_cur[a], 1);
         if (b >= 0) atomicAdd(&adj_cur[b], 1);
-        __syncwarp();
+        gsync(x);
     }
     IslandOut out{0, 0, 0};
     if (lane == 0) {
@@ -504,10 +509,10 @@ __device__ IslandOut find_islands(Ctx &x) {
         }
         out = {nc, nj, ni};
     }
-    out.n_contacts = __shfl_sync(FULL, out.n_contacts, 0);
-    out.n_joints = __shfl_sync(FULL, out.n_joints, 0);
-    out.n_islands = __shfl_sync(FULL, out.n_islands, 0);
-    __syncwarp();
+    out.n_contacts = gshfl(x, out.n_contacts, 0);
+    out.n_joints = gshfl(x, out.n_joints, 0);
+    out.n_islands = gshfl(x, out.n_islands, 0);
+    gsync(x);
     return out;
 }
 
@@ -515,7 +520,7 @@ __device__ IslandOut find_islands(Ctx &x) {
 __device__ void synchronize_fixtures(Ctx &x, const int *moved, int n_rows) {
     const DevModel &m = x.m;
     W &w = x.w;
-    for (int r = x.lane; r < n_rows; r += 32) {
+    for (int r = x.lane; r < n_rows; r += x.wl) {
         int f = m.row_fixture[r];
         int b = m.fixture_body[f];
         if (!moved[b]) continue;
@@ -541,7 +546,7 @@ __device__ void synchronize_fixtures(Ctx &x, const int *moved, int n_rows) {
             uy = uy + ddy;
         old[0] = lx, old[1] = ly, old[2] = ux, old[3] = uy;
     }
-    __syncwarp();
+    gsync(x);
 }
 
 __device__ __forceinline__ Bodies bodies_of(Ctx &x) {
@@ -580,15 +585,13 @@ __device__ __forceinline__ IslandWork sweep_of(const Ctx &x, int n_contacts) {  
 }
 
 // ---------------------------------------------------------------- b2World::Solve (step.py:73-194)
-__device__ IslandWork solve(Ctx &x, float dt, float dt_ratio) {
+// velocity integration and the constraint rows of the islands find_islands() built
+__device__ IslandWork solve_rows(Ctx &x, float dt, float dt_ratio, const IslandOut &isl) {
     const DevModel &m = x.m;
     const goib2d_settings &s = x.s;
     W &w = x.w;
     const int B = w.B, lane = x.lane;
     const Layout &L = x.p.lay;
-    IslandOut isl = find_islands(x);
-    GB_PHASE(x, 2);
-    phase_sync(x);
     int *bisl = ap<int>(x, L.bisl), *corder = ap<int>(x, L.corder), *cisl = ap<int>(x, L.cisl);
     int *jorder = ap<int>(x, L.jorder);
     const IslandWork sw = sweep_of(x, isl.n_contacts);
@@ -597,7 +600,7 @@ __device__ IslandWork solve(Ctx &x, float dt, float dt_ratio) {
     JRow *jr = sw.jr;
     const float h = dt;
     const float gx = w.gravity[0], gy = w.gravity[1];
-    for (int b = lane; b < B; b += 32) {  // integrate velocities (step.py:83-100)
+    for (int b = lane; b < B; b += x.wl) {  // integrate velocities (step.py:83-100)
         bool in_isl = bisl[b] >= 0;
         float gs = w.gravity_scale[b];
         float ax = gs * gx + w.inv_mass[b] * w.force[2 * b];
@@ -616,20 +619,25 @@ __device__ IslandWork solve(Ctx &x, float dt, float dt_ratio) {
         Rot q = rot_of(bd.ca[b]);
         bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = bd.ca[b];
     }
-    __syncwarp();
+    gsync(x);
     const bool warm = s.warm_starting;
-    for (int k = lane; k < isl.n_contacts; k += 32)
+    for (int k = lane; k < isl.n_contacts; k += x.wl)
         prepare_contact(m, w, corder[k], bd, warm, dt_ratio, s.velocity_threshold, vc[k]);
-    for (int k = lane; k < isl.n_joints; k += 32) prepare_joint(m, w, jorder[k], bd, s, dt, dt_ratio, warm, jr[k]);
-    __syncwarp();
+    for (int k = lane; k < isl.n_joints; k += x.wl) prepare_joint(m, w, jorder[k], bd, s, dt, dt_ratio, warm, jr[k]);
+    gsync(x);
     GB_PHASE(x, 3);
     if (lane == 0) {  // the island counts, for the constraint sweeps (solve_constraints)
         int *cnt = ap<int>(x, L.isl);
         cnt[0] = isl.n_contacts, cnt[1] = isl.n_joints, cnt[2] = isl.n_islands;
     }
-    __syncwarp();
+    gsync(x);
     GB_PHASE(x, 3);
     return sw;
+}
+__device__ __forceinline__ IslandWork solve(Ctx &x, float dt, float dt_ratio) {
+    const IslandOut isl = find_islands(x);
+    GB_PHASE(x, 2);
+    return solve_rows(x, dt, dt_ratio, isl);
 }
 
 // The island constraint sweeps of one world (step.py:101-140, 197-251), run by ONE thread: warm start, the
@@ -749,14 +757,14 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
     int *moved = ap<int>(x, L.moved);
     const int *done = sw.done;
     const Bodies &bd = sw.bd;
-    for (int b = lane; b < B; b += 32) {  // write back + SynchronizeTransform (step.py:141-151)
+    for (int b = lane; b < B; b += x.wl) {  // write back + SynchronizeTransform (step.py:141-151)
         if (bisl[b] < 0) continue;
         w.c[2 * b] = bd.cx[b], w.c[2 * b + 1] = bd.cy[b], w.a[b] = bd.ca[b];
         w.v[2 * b] = bd.vx[b], w.v[2 * b + 1] = bd.vy[b], w.w[b] = bd.vw[b];
         Xf xf = xf_from(V2{bd.cx[b], bd.cy[b]}, bd.ca[b], w.blc(b));
         w.xf_p[2 * b] = xf.p.x, w.xf_p[2 * b + 1] = xf.p.y, w.xf_q[2 * b] = xf.q.c, w.xf_q[2 * b + 1] = xf.q.s;
     }
-    __syncwarp();
+    gsync(x);
     int *islsleep = ap<int>(x, L.islsleep), *last = ap<int>(x, L.last);
     float *st = ap<float>(x, L.st);
     int *minkey = ap<int>(x, L.minst);
@@ -764,12 +772,12 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
     // reductions have no order: an island's minimum sleep time (a float minimum, as integer atomics on the order-
     // preserving key of the float; a NaN time, which the float minimum skips, is skipped) and a static body's last
     // island (an integer maximum).
-    for (int i = lane; i < B; i += 32) islsleep[i] = 0, last[i] = -1, minkey[i] = fkey(MAXF);
-    __syncwarp();
+    for (int i = lane; i < B; i += x.wl) islsleep[i] = 0, last[i] = -1, minkey[i] = fkey(MAXF);
+    gsync(x);
     if (s.allow_sleep) {
         const float lin_tol = s.linear_sleep_tolerance * s.linear_sleep_tolerance;
         const float ang_tol = s.angular_sleep_tolerance * s.angular_sleep_tolerance;
-        for (int b = lane; b < B; b += 32) {
+        for (int b = lane; b < B; b += x.wl) {
             const bool nonstatic = bisl[b] >= 0 && w.type[b] != STATIC;
             const float t0 = w.sleep_time[b];
             float stb = t0;
@@ -782,10 +790,10 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
             }
             st[b] = stb;
         }
-        __syncwarp();
-        for (int i = lane; i < B; i += 32) islsleep[i] = fkey_inv(minkey[i]) >= s.time_to_sleep && done[i];
-        __syncwarp();
-        for (int b = lane; b < B; b += 32) {
+        gsync(x);
+        for (int i = lane; i < B; i += x.wl) islsleep[i] = fkey_inv(minkey[i]) >= s.time_to_sleep && done[i];
+        gsync(x);
+        for (int b = lane; b < B; b += x.wl) {
             const bool sl = bisl[b] >= 0 && w.type[b] != STATIC && islsleep[bisl[b]];
             w.sleep_time[b] = sl ? 0.0f : st[b];
             if (sl) {
@@ -795,21 +803,21 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
             }
         }
     }
-    for (int sl = lane; sl < C; sl += 32) {
+    for (int sl = lane; sl < C; sl += x.wl) {
         const int i = cisl[sl];
         if (i < 0) continue;
         atomicMax(last + m.fixture_body[w.fa[sl]], i), atomicMax(last + m.fixture_body[w.fb[sl]], i);
     }
-    for (int j = lane; j < J; j += 32) {
+    for (int j = lane; j < J; j += x.wl) {
         const int i = jisl[j];
         if (i < 0) continue;
         atomicMax(last + m.joint_a[j], i), atomicMax(last + m.joint_b[j], i);
     }
-    __syncwarp();
-    for (int b = lane; b < B; b += 32)
+    gsync(x);
+    for (int b = lane; b < B; b += x.wl)
         if (w.type[b] == STATIC && last[b] >= 0) w.awake[b] = !islsleep[last[b]], w.sleep_time[b] = 0.0f;
-    for (int b = lane; b < B; b += 32) moved[b] = bisl[b] >= 0 && w.type[b] != STATIC;
-    __syncwarp();
+    for (int b = lane; b < B; b += x.wl) moved[b] = bisl[b] >= 0 && w.type[b] != STATIC;
+    gsync(x);
     GB_PHASE(x, 6);
 }
 
@@ -852,7 +860,7 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
     // each round records, in parallel, every candidate up to the next advance, which lane 0 then performs.
     for (int k0 = 0;;) {
         int first = n_live;
-        for (int base = k0; base < n_live; base += 32) {
+        for (int base = k0; base < n_live; base += x.wl) {
             int k = base + lane, slot = -1, A = 0, Bb = 0;
             bool cand = false;
             float alA = 0.0f, alB = 0.0f;
@@ -861,7 +869,7 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
                 cand = toi_candidate(x, slot, A, Bb);
                 if (cand) alA = w.t_alpha0[A], alB = w.t_alpha0[Bb];
             }
-            unsigned mk = __ballot_sync(FULL, cand && alA != alB);
+            unsigned mk = gballot(x, cand && alA != alB);
             int f = mk ? base + __ffs(mk) - 1 : n_live;
             if (slot >= 0 && k < f) {
                 tneed[slot] = cand;
@@ -872,7 +880,7 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
                 break;
             }
         }
-        __syncwarp();
+        gsync(x);
         if (first == n_live) break;
         if (lane == 0) {
             int slot = order[first], A = 0, Bb = 0;
@@ -890,10 +898,10 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
             toi_record(w, A, Bb, common, rec + 8 * slot);
             tneed[slot] = 1;
         }
-        __syncwarp();
+        gsync(x);
         k0 = first + 1;
     }
-    for (int k = lane; k < n_live; k += 32) {  // b2TimeOfImpact per queued contact
+    for (int k = lane; k < n_live; k += x.wl) {  // b2TimeOfImpact per queued contact
         int slot = order[k];
         if (!tneed[slot]) continue;
         int A = m.fixture_body[w.fa[slot]], Bb = m.fixture_body[w.fb[slot]];
@@ -913,24 +921,24 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
         w.t_toi[slot] = st == E_TOUCHING ? bmin(common + (1.0f - common) * beta, 1.0f) : 1.0f;
         w.t_flag[slot] = 1;
     }
-    __syncwarp();
+    gsync(x);
     // The minimum, first (or last) in list order among exact ties (toi.py:550-557), as warp reductions.
     const bool oldest = x.s.toi_tie_oldest;
     float best = 1.0f;
-    for (int k = lane; k < n_live; k += 32) {
+    for (int k = lane; k < n_live; k += x.wl) {
         int slot = order[k];
         bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
         if (base && w.t_flag[slot] && w.t_toi[slot] < 1.0f) best = fminf(best, w.t_toi[slot]);
     }
-    for (int o = 16; o > 0; o >>= 1) best = fminf(best, __shfl_xor_sync(FULL, best, o));
+    for (int o = x.wl >> 1; o > 0; o >>= 1) best = fminf(best, __shfl_xor_sync(x.gmask, best, o, x.wl));
     int pos = oldest ? -1 : n_live;
-    for (int k = lane; k < n_live; k += 32) {
+    for (int k = lane; k < n_live; k += x.wl) {
         int slot = order[k];
         bool base = w.t_enabled[slot] && w.t_count[slot] <= MAX_SUB_STEPS;
         if (base && w.t_flag[slot] && w.t_toi[slot] < 1.0f && w.t_toi[slot] == best) pos = oldest ? k : min(pos, k);
     }
-    for (int o = 16; o > 0; o >>= 1) {
-        int q = __shfl_xor_sync(FULL, pos, o);
+    for (int o = x.wl >> 1; o > 0; o >>= 1) {
+        int q = __shfl_xor_sync(x.gmask, pos, o, x.wl);
         pos = oldest ? max(pos, q) : min(pos, q);
     }
     const float done_alpha = 1.0f - 10.0f * EPS;
@@ -959,7 +967,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
 #ifdef GOIB2D_PHASE_TIMERS
     long long ev_t0 = clock64();
 #endif
-    for (int b = lane; b < B; b += 32) {  // every body advanced to min_alpha, and its transform there
+    for (int b = lane; b < B; b += x.wl) {  // every body advanced to min_alpha, and its transform there
         float *d = adv + 8 * b;
         d[0] = w.c0[2 * b], d[1] = w.c0[2 * b + 1], d[2] = w.a0[b], d[3] = w.t_alpha0[b];
         sweep_advance(d[0], d[1], d[2], d[3], w.c[2 * b], w.c[2 * b + 1], w.a[b], min_alpha);
@@ -968,7 +976,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         flip_b[b] = in_other[b] = touched[b] = newbody[b] = 0;
     }
     int n_live = list_order(x, order, lpos);
-    for (int s_ = lane; s_ < C; s_ += 32) {  // manifolds at the advanced poses for the pair's contacts
+    for (int s_ = lane; s_ < C; s_ += x.wl) {  // manifolds at the advanced poses for the pair's contacts
         solved[s_] = 0;
         if (w.pair[s_] < 0) continue;
         int ba = m.fixture_body[w.fa[s_]], bb = m.fixture_body[w.fb[s_]];
@@ -977,7 +985,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         evaluate(m, w.fa[s_], w.fb[s_], Xf{{da[4], da[5]}, {da[6], da[7]}}, Xf{{db[4], db[5]}, {db[6], db[7]}},
                  s.linear_slop, s.angular_slop, man[s_]);
     }
-    __syncwarp();
+    gsync(x);
     // The island walk (toi.py:633-657): bodyA's contact list then bodyB's, newest first; each walked contact is
     // updated (b2Contact::Update, Begin / End events) and, when touching, joins the island. Its only order-dependent
     // rule is the cap (32 contacts, 64 bodies): when a side-effect-free count shows the island cannot reach it, the
@@ -1009,24 +1017,24 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         w.t_flag[min_slot] = 0;
         if (t_min) tisl[n_isl++] = min_slot;
     }
-    t_min = __shfl_sync(FULL, (int)t_min, 0);
-    ev_n = __shfl_sync(FULL, ev_n, 0);
-    n_isl = __shfl_sync(FULL, n_isl, 0);
-    __syncwarp();
+    t_min = gshfl(x, (int)t_min, 0);
+    ev_n = gshfl(x, ev_n, 0);
+    n_isl = gshfl(x, n_isl, 0);
+    gsync(x);
     if (t_min) {
         int total = 0;  // contacts the walk would add to the island
         for (int oi = 0; oi < 2; ++oi) {
             if (w.type[oi ? Bb : A] != DYNAMIC) continue;
-            for (int base = 0; base < n_live; base += 32) {
+            for (int base = 0; base < n_live; base += x.wl) {
                 int k = base + lane, other = 0;
                 bool add = k < n_live && walked(oi, order[k], other) && man[order[k]].count > 0;
-                total += __popc(__ballot_sync(FULL, add));
+                total += __popc(gballot(x, add));
             }
         }
         if (total + 1 < MAX_TOI_CONTACTS) {  // the cap cannot be reached: all lanes
             for (int oi = 0; oi < 2; ++oi) {
                 if (w.type[oi ? Bb : A] != DYNAMIC) continue;
-                for (int base = 0; base < n_live; base += 32) {
+                for (int base = 0; base < n_live; base += x.wl) {
                     int k = base + lane, other = 0, slot = k < n_live ? order[k] : -1;
                     bool upd = slot >= 0 && walked(oi, slot, other), flip = false, add = false;
                     if (upd) {
@@ -1040,7 +1048,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                             if (other != A && other != Bb) newbody[other] = 1;
                         }
                     }
-                    unsigned fm = __ballot_sync(FULL, flip), am = __ballot_sync(FULL, add);
+                    unsigned fm = gballot(x, flip), am = gballot(x, add);
                     const unsigned below = (1u << lane) - 1;
                     if (flip && x.p.events)
                         put_event(x.p, x.world, ev_n + __popc(fm & below), w.touching[slot] ? EV_BEGIN : EV_END,
@@ -1049,7 +1057,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                     ev_n += __popc(fm), n_isl += __popc(am);
                 }
             }
-            __syncwarp();
+            gsync(x);
         } else if (lane == 0) {  // near the cap: as listed
             int n_bodies = 2;
             bool stop = false;
@@ -1082,12 +1090,12 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
                 }
             }
         }
-        n_isl = __shfl_sync(FULL, n_isl, 0);
-        ev_n = __shfl_sync(FULL, ev_n, 0);
+        n_isl = gshfl(x, n_isl, 0);
+        ev_n = gshfl(x, ev_n, 0);
     }
     if (lane == 0 && x.p.events) x.p.event_count[x.world] = ev_n;
-    __syncwarp();
-    for (int b = lane; b < B; b += 32) {  // body sweeps after the walk (toi.py:667-681)
+    gsync(x);
+    for (int b = lane; b < B; b += x.wl) {  // body sweeps after the walk (toi.py:667-681)
         bool pair_b = b == A || b == Bb;
         bool keep = (pair_b && t_min) || in_other[b];
         bool restore = (pair_b && !t_min) || (touched[b] && !in_other[b]);
@@ -1104,10 +1112,10 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         if (flip_b[b] || (pair_b && t_min) || (newbody[b] && w.type[b] != STATIC)) wake_body(w, b);
         moved[b] = t_min && (pair_b || in_other[b]) && w.type[b] == DYNAMIC;
     }
-    __syncwarp();
+    gsync(x);
     if (!t_min) {
         if (lane == 0) *w.t_events += 1;
-        __syncwarp();
+        gsync(x);
         return;
     }
 #ifdef GOIB2D_PHASE_TIMERS
@@ -1117,19 +1125,19 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     // b2Island::SolveTOI: position passes moving only the TOI pair, then velocity passes, then integration; the
     // island's rows in the warp's shared rows region when they fit
     if (x.rows && n_isl <= L.sm_vc_cap) vc = reinterpret_cast<VCRow *>(x.rows + L.sm_vc);
-    for (int b = lane; b < B; b += 32) {
+    for (int b = lane; b < B; b += x.wl) {
         bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
         bd.vx[b] = w.v[2 * b], bd.vy[b] = w.v[2 * b + 1], bd.vw[b] = w.w[b];
         Rot q = rot_of(bd.ca[b]);
         bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = bd.ca[b];
     }
-    __syncwarp();
+    gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
     long long isl_t0 = clock64();
 #endif
-    for (int k = lane; k < n_isl; k += 32)  // position rows (the position-independent fields)
+    for (int k = lane; k < n_isl; k += x.wl)  // position rows (the position-independent fields)
         prepare_contact(m, w, tisl[k], bd, false, 1.0f, s.velocity_threshold, vc[k]);
-    __syncwarp();
+    gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
     if (lane == 0) atomicAdd(&g_toi_cycles[4], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
 #endif
@@ -1152,22 +1160,22 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         w.c0[2 * A] = bd.cx[A], w.c0[2 * A + 1] = bd.cy[A], w.a0[A] = bd.ca[A];
         w.c0[2 * Bb] = bd.cx[Bb], w.c0[2 * Bb + 1] = bd.cy[Bb], w.a0[Bb] = bd.ca[Bb];
     }
-    __syncwarp();
-    for (int b = lane; b < B; b += 32) body_rot(bd, b, bd.ca[b]);
-    __syncwarp();
+    gsync(x);
+    for (int b = lane; b < B; b += x.wl) body_rot(bd, b, bd.ca[b]);
+    gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
     if (lane == 0) atomicAdd(&g_toi_cycles[5], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
 #endif
-    for (int k = lane; k < n_isl; k += 32)  // velocity constraints at the solved poses, no warm start
+    for (int k = lane; k < n_isl; k += x.wl)  // velocity constraints at the solved poses, no warm start
         prepare_contact(m, w, tisl[k], bd, false, 1.0f, s.velocity_threshold, vc[k]);
-    __syncwarp();
+    gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
     if (lane == 0) atomicAdd(&g_toi_cycles[6], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
 #endif
     if (lane == 0)
         for (int it = 0; it < s.velocity_iterations; ++it)
             for (int k = 0; k < n_isl; ++k) contact_solve_velocity(vc[k], bd);
-    __syncwarp();
+    gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
     if (lane == 0) atomicAdd(&g_toi_cycles[7], (unsigned long long)(clock64() - isl_t0)), isl_t0 = clock64();
     if (lane == 0) atomicAdd(&g_toi_cycles[11], (unsigned long long)n_isl);
@@ -1175,7 +1183,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     const float h = (1.0f - min_alpha) * dt;
     const float max_t = s.clamps_per_second ? s.max_translation * dt : s.max_translation;
     const float max_r = s.clamps_per_second ? s.max_rotation * dt : s.max_rotation;
-    for (int b = lane; b < B; b += 32) {  // integrate the island bodies over the rest of the step
+    for (int b = lane; b < B; b += x.wl) {  // integrate the island bodies over the rest of the step
         bool pair_b = b == A || b == Bb;
         if (!(pair_b || in_other[b])) continue;
         float vx = bd.vx[b], vy = bd.vy[b], ww = bd.vw[b];
@@ -1193,7 +1201,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         w.xf_p[2 * b] = xf.p.x, w.xf_p[2 * b + 1] = xf.p.y, w.xf_q[2 * b] = xf.q.c, w.xf_q[2 * b + 1] = xf.q.s;
     }
     const int ev_base = x.p.events ? x.p.event_count[x.world] : 0;
-    for (int k = lane; k < n_isl; k += 32) {  // b2Island::Report (PostSolve per island contact)
+    for (int k = lane; k < n_isl; k += x.wl) {  // b2Island::Report (PostSolve per island contact)
         const VCRow &c = vc[k];
         solved[c.slot] = 1;
         w.t_solved[c.slot] = 1;
@@ -1203,26 +1211,26 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         }
         if (x.p.events) put_event(x.p, x.world, ev_base + k, EV_POST_SOLVE, w.fa[c.slot], w.fb[c.slot], c.count, c.ni, c.ti);
     }
-    __syncwarp();
+    gsync(x);
     if (lane == 0 && x.p.events) x.p.event_count[x.world] = ev_base + n_isl;
-    __syncwarp();
+    gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
     if (lane == 0) atomicAdd(&g_toi_cycles[13], (unsigned long long)(clock64() - ev_t0));
     ev_t0 = clock64();
 #endif
     synchronize_fixtures(x, moved, w.rows);
-    for (int s_ = lane; s_ < C; s_ += 32) {
+    for (int s_ = lane; s_ < C; s_ += x.wl) {
         if (moved[m.fixture_body[w.fa[s_]]] || moved[m.fixture_body[w.fb[s_]]]) w.t_flag[s_] = 0;  // every slot
         old_pair[s_] = w.pair[s_], old_key[s_] = w.key[s_];
     }
-    __syncwarp();
+    gsync(x);
     find_new_contacts(x);
-    for (int s_ = lane; s_ < C; s_ += 32) {
+    for (int s_ = lane; s_ < C; s_ += x.wl) {
         bool is_new = w.pair[s_] >= 0 && (old_pair[s_] < 0 || old_key[s_] != w.key[s_]);
         if (is_new) w.t_count[s_] = 0, w.t_flag[s_] = 0, w.t_enabled[s_] = 1;
     }
     if (lane == 0) *w.t_events += 1;
-    __syncwarp();
+    gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
     if (lane == 0) atomicAdd(&g_toi_cycles[14], (unsigned long long)(clock64() - ev_t0));
 #endif
@@ -1233,13 +1241,13 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
     const int C = w.C, B = w.B, lane = x.lane;
     if (C == 0 || x.m.P == 0) return;
     if (x.s.unity_toi && !x.m.any_toi_body) return;
-    for (int b = lane; b < B; b += 32) w.t_alpha0[b] = 0.0f;
-    for (int c = lane; c < C; c += 32) {
+    for (int b = lane; b < B; b += x.wl) w.t_alpha0[b] = 0.0f;
+    for (int c = lane; c < C; c += x.wl) {
         w.t_count[c] = 0, w.t_toi[c] = 1.0f, w.t_flag[c] = 0, w.t_enabled[c] = 1, w.t_solved[c] = 0;
         w.t_ni[2 * c] = w.t_ni[2 * c + 1] = w.t_ti[2 * c] = w.t_ti[2 * c + 1] = 0.0f;
     }
     if (lane == 0) *w.t_events = 0;
-    __syncwarp();
+    gsync(x);
     if (!(dt > 0)) return;
     const int max_events = C * (MAX_SUB_STEPS + 1) + 8;
     int min_slot = 0;
@@ -1273,45 +1281,29 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
 //      the sweeps between the first two run one world per thread (goib2d_constraints_kernel)
 //   5  SolveTOI, then the end of the step (inv_dt0, cleared forces; the status word after the last step)
 // Every value one part hands the next is in the State or the world's arena.
-// One part of one world's step on this warp: w is the world's bound State, hot / rows its shared-memory regions
-// (or null).
+// One part of one world's step on the world's group of lanes (Ctx x: the bound State and its regions).
 template <int PART>
-__device__ __forceinline__ void run_part(const StepParams &p, int64_t world, W &w_, char *hot, char *rows,
-                                         int nsync) {
-    Ctx x{p, p.m, p.s, w_, p.scratch + world * p.lay.stride, hot, rows, (int)(threadIdx.x & 31), 0, clock64(),
-          world, nsync};
+__device__ __forceinline__ void run_part(Ctx &x) {
+    const StepParams &p = x.p;
     W &w = x.w;
     const float dt = p.dt;
 #ifdef GOIB2D_PHASE_TIMERS
     const long long gb_span0_ = clock64();
 #endif
     if (PART == 0) {
-        if (p.actions && x.lane < p.n_action)  // action channels -> joint motor speeds
-            w.motor_speed[p.action_joint[x.lane]] = p.action_scale[x.lane] * p.actions[world * p.n_action + x.lane];
-        __syncwarp();
+        if (p.actions)  // action channels -> joint motor speeds
+            for (int c = x.lane; c < p.n_action; c += x.wl)
+                w.motor_speed[p.action_joint[c]] = p.action_scale[c] * p.actions[x.world * p.n_action + c];
+        gsync(x);
         GB_PHASE(x, 11);
         if (*w.new_fixture) find_new_contacts(x);
-        __syncwarp();
+        gsync(x);
         if (x.lane == 0) *w.new_fixture = 0;
-        __syncwarp();
+        gsync(x);
         GB_PHASE(x, 0);
         collide(x);
         GB_PHASE(x, 1);
         GB_SPAN(x, 9, false);
-    } else if (PART == 1) {  // the whole of b2World::Solve, the sweeps on lane 0
-        const IslandWork sw = solve(x, dt, *w.inv_dt0 * dt);
-        phase_sync(x);
-        if (x.lane == 0)
-            solve_constraints(p, world, sw,
-                              {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
-                               ap<int>(x, p.lay.jisl)});
-        __syncwarp();
-        GB_PHASE(x, 5);
-        phase_sync(x);
-        solve_finish(x, dt, sw);
-        phase_sync(x);
-        broadphase(x);
-        GB_SPAN(x, 6, false);
     } else if (PART == 2) {
         solve(x, dt, *w.inv_dt0 * dt);
     } else if (PART == 3) {
@@ -1320,28 +1312,33 @@ __device__ __forceinline__ void run_part(const StepParams &p, int64_t world, W &
         broadphase(x);
     } else {
         if (x.s.continuous_physics) solve_toi(x, dt);
-        __syncwarp();
+        gsync(x);
         GB_SPAN(x, 0, x.s.continuous_physics && *w.t_events > 0);
         if (x.lane == 0 && dt > 0) *w.inv_dt0 = 1.0f / dt;
         if (x.s.auto_clear_forces)
-            for (int b = x.lane; b < w.B; b += 32) w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
+            for (int b = x.lane; b < w.B; b += x.wl) w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
         if (p.step == p.n_steps - 1) {
             bool bad = false;  // non-finite body state
-            for (int b = x.lane; b < w.B; b += 32)
+            for (int b = x.lane; b < w.B; b += x.wl)
                 bad = bad || !isfinite(w.c[2 * b]) || !isfinite(w.c[2 * b + 1]) || !isfinite(w.a[b]) ||
                       !isfinite(w.v[2 * b]) || !isfinite(w.v[2 * b + 1]) || !isfinite(w.w[b]);
-            if (__any_sync(FULL, bad)) x.status |= ST_NONFINITE;
+            if (__any_sync(x.gmask, bad)) x.status |= ST_NONFINITE;
         }
-        __syncwarp();
-    }
-    if (x.lane == 0 && p.status) {
-        if (PART == 0 && p.step == 0)
-            p.status[world] = x.status;
-        else if (x.status)
-            p.status[world] |= x.status;
+        gsync(x);
     }
 }
 
+// the status word of the world after a part (part 0 of the first step starts it afresh)
+__device__ __forceinline__ void put_status(const Ctx &x, bool first) {
+    if (x.lane == 0 && x.p.status) {
+        if (first)
+            x.p.status[x.world] = x.status;
+        else if (x.status)
+            x.p.status[x.world] |= x.status;
+    }
+}
+
+// A part kernel (batches of THREAD_SWEEPS_MIN_WORLDS and more): one warp per world, 4 worlds per block.
 template <int PART>
 __device__ __forceinline__ void step_part(const StepParams &p) {
     const int warp = threadIdx.x >> 5;
@@ -1353,42 +1350,86 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     // the collide and TOI part kernels keep the arena's hot part in shared memory: every arena array
     // they use is written and read within the kernel; the large-batch split solve passes arrays between kernels
     extern __shared__ __align__(16) char dyn_smem[];
-    const bool hot = (PART == 0 || PART == 1 || PART == 5) && p.lay.hot_end > 0;
-    const bool rows = hot && (PART == 1 || PART == 5) && p.lay.rows_bytes;  // the solve's and the TOI island's rows
+    const bool hot = (PART == 0 || PART == 5) && p.lay.hot_end > 0;
+    const bool rows = hot && PART == 5 && p.lay.rows_bytes;  // the TOI island's rows
     const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
     char *mine = dyn_smem + warp * region;
-    run_part<PART>(p, world, s_world[warp], hot ? mine : nullptr, rows ? mine + p.lay.hot_end : nullptr, 0);
+    Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
+          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64(), world, FULL, 0, 32};
+    run_part<PART>(x);
+    put_status(x, PART == 0 && p.step == 0);
 }
 
-// The whole step in one launch (batches below THREAD_SWEEPS_MIN_WORLDS): one warp per world, one block of up to
-// STEP_MAX_WARPS worlds per SM, the block's warps starting each phase together (phase_sync: collide | islands | rows |
-// sweeps | write back and sleep | broadphase | TOI). Worlds are independent, so a phase's tail is the slowest of the
-// block's worlds rather than of the whole batch, and every warp of an SM runs the same phase at the same time (the
-// step's code does not fit the SM's instruction cache; warps spread over all phases thrash it). Per warp in dynamic
-// shared memory: the bound State, the arena's hot part and the rows region.
-constexpr int STEP_MAX_WARPS = 28;       // 72 registers per thread: 28 warps per SM
+// The whole step in one launch (batches below THREAD_SWEEPS_MIN_WORLDS): one block per SM where the batch allows,
+// the block's threads meeting between phases (step_sync: collide | islands | rows | sweeps | write back and sleep |
+// broadphase | TOI), and WPW worlds per warp.
+// - Phase barriers: worlds are independent, so a phase's tail is the slowest of the block's worlds rather than of
+//   the whole batch, and every warp of an SM runs the same phase at the same time (the step's code does not fit the
+//   SM's instruction cache; warps spread over all phases thrash it).
+// - WPW = 2 (goib2d_step_pair_kernel), one world per half-warp: the order-dependent sections run on each world's
+//   lane 0, so lanes 0 and 16 run two worlds' sequential work in the same instructions where their control flow
+//   agrees - half the issue slots per world, which pays when an SM holds many small worlds - and 16 warps per SM
+//   leave 128 registers per thread (28 single-world warps: 72, with spills). Where the two worlds' sequential work
+//   diverges (large islands, frequent TOI events) the warp runs both paths one after the other, so WPW = 1
+//   (goib2d_step_kernel, 28 warps of 72 registers) serves the other batches (launch_steps chooses).
+// Per world in dynamic shared memory: the bound State, the arena's hot part and the rows region. A group of lanes
+// without a world (the batch's tail) runs no phase but meets every barrier, so all threads reach every step_sync.
+constexpr int STEP_MAX_WARPS = 28;       // one world per warp: 72 registers per thread
+constexpr int PAIR_MAX_WARPS = 16;       // two worlds per warp: 128 registers per thread
 constexpr int STEP_MAX_SMEM = 232448;    // dynamic shared memory per block
 __host__ __device__ __forceinline__ int step_region(const Layout &L) {
     return (int)((sizeof(W) + 15) & ~size_t(15)) + L.hot_end + (L.hot_end > 0 ? L.rows_bytes : 0);
 }
+// the warp reconverges (all its lanes are at this same call), then the block's threads meet
+__device__ __forceinline__ void step_sync() {
+    __syncwarp();
+    __syncthreads();
+}
+template <int WPW>
 __device__ __forceinline__ void whole_step(const StepParams &p) {
-    const int warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
-    const int64_t first = p.world0 + (int64_t)blockIdx.x * wpb, world = first + warp;
-    if (world >= p.world_end) return;  // the block's spare warps (last block only) take no part
-    const int64_t left = p.world_end - first;
-    const int nsync = 32 * (int)(left < wpb ? left : wpb);
+    constexpr int WL = 32 / WPW;  // lanes per world
+    const int lane32 = threadIdx.x & 31, half = WPW == 2 ? lane32 >> 4 : 0;
+    const int slot = WPW * (int)(threadIdx.x >> 5) + half;  // the world's place in the block
+    const int64_t world = p.world0 + (int64_t)blockIdx.x * (WPW * (blockDim.x >> 5)) + slot;
+    const bool active = world < p.world_end;
     extern __shared__ __align__(16) char dyn_smem[];
-    char *mine = dyn_smem + warp * step_region(p.lay);
+    char *mine = dyn_smem + slot * step_region(p.lay);
     W &w = *reinterpret_cast<W *>(mine);
     char *hot = p.lay.hot_end > 0 ? mine + ((sizeof(W) + 15) & ~size_t(15)) : nullptr;
     char *rows = hot && p.lay.rows_bytes ? hot + p.lay.hot_end : nullptr;
-    if ((threadIdx.x & 31) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
+    if (active && (lane32 & (WL - 1)) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
-    run_part<0>(p, world, w, hot, nullptr, nsync);
-    asm volatile("bar.sync 1, %0;" ::"r"(nsync) : "memory");
-    run_part<1>(p, world, w, hot, rows, nsync);
-    asm volatile("bar.sync 1, %0;" ::"r"(nsync) : "memory");
-    run_part<5>(p, world, w, hot, rows, 0);
+    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, nullptr, lane32 & (WL - 1), 0, clock64(), world,
+          WPW == 2 ? 0xffffu << (16 * half) : FULL, WL * half, WL};
+    const float dt = p.dt;
+    if (active) run_part<0>(x);
+    step_sync();
+    x.rows = rows;
+    IslandOut isl{0, 0, 0};
+    if (active) {
+        isl = find_islands(x);
+        GB_PHASE(x, 2);
+    }
+    step_sync();
+    IslandWork sw{};
+    if (active) sw = solve_rows(x, dt, *w.inv_dt0 * dt, isl);
+    step_sync();
+    if (active && x.lane == 0)
+        solve_constraints(p, world, sw,
+                          {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
+                           ap<int>(x, p.lay.jisl)});
+    step_sync();
+    if (active) {
+        GB_PHASE(x, 5);
+        solve_finish(x, dt, sw);
+    }
+    step_sync();
+    if (active) broadphase(x);
+    step_sync();
+    if (active) {
+        run_part<5>(x);
+        put_status(x, p.step == 0);
+    }
 }
 
 }  // namespace gb
@@ -1429,10 +1470,15 @@ extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_toi_kernel(const __grid_constant__ StepParams p) {
     step_part<5>(p);
 }
-// the whole step, one warp per world, up to STEP_MAX_WARPS worlds per block (whole_step)
+// the whole step, one world per warp (whole_step)
 extern "C" __global__ void __launch_bounds__(32 * STEP_MAX_WARPS, 1)
     goib2d_step_kernel(const __grid_constant__ StepParams p) {
-    whole_step(p);
+    whole_step<1>(p);
+}
+// the whole step, two worlds per warp (whole_step)
+extern "C" __global__ void __launch_bounds__(32 * PAIR_MAX_WARPS, 1)
+    goib2d_step_pair_kernel(const __grid_constant__ StepParams p) {
+    whole_step<2>(p);
 }
 
 namespace gb {
@@ -1443,6 +1489,15 @@ constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = 16384;
 // p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: per step one goib2d_step_kernel, or for
 // large batches the collide part, the solve part in pieces (rows / thread sweeps / finish / broadphase), the TOI part
 int kernels_per_step(int64_t n_worlds) { return n_worlds < THREAD_SWEEPS_MIN_WORLDS ? 1 : 6; }
+// Two worlds per warp (goib2d_step_pair_kernel) for crowded batches of small worlds: more than PAIR_MIN_PER_SM
+// worlds per SM (fewer leave the SM's issue slots free, and a pair only adds the two worlds' divergence) and at most
+// PAIR_MAX_CONTACTS contact slots (worlds with more grow islands and TOI event chains that differ between the two
+// worlds of a warp). Measured: c1 (4096 worlds, 48 slots) +12 %; c0 (256 worlds) -7 %, c2 (1024 slots) -39 %,
+// c3 (256 slots) -21 % had they been paired.
+constexpr int PAIR_MIN_PER_SM = 16, PAIR_MAX_CONTACTS = 128;
+bool step_pairs(int64_t n_worlds, int sms, int contact_capacity) {
+    return n_worlds > (int64_t)PAIR_MIN_PER_SM * sms && contact_capacity <= PAIR_MAX_CONTACTS;
+}
 
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     p.world0 = 0, p.world_end = p.n_worlds;
@@ -1452,22 +1507,26 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const int region = step_region(p.lay);
-        int wpb = (int)((n + sms - 1) / sms);  // one block per SM where the batch allows
-        wpb = wpb < 1 ? 1 : (wpb > STEP_MAX_WARPS ? STEP_MAX_WARPS : wpb);
-        const int fit = STEP_MAX_SMEM / region;
-        wpb = wpb > fit ? fit : wpb;
-        const size_t smem = (size_t)wpb * region;
-        static int smem_set[64];  // the dynamic shared memory limit set per device
-        if (dev < 64 && smem > 48 * 1024 && (size_t)smem_set[dev] < smem) {
-            cudaError_t e = cudaFuncSetAttribute(goib2d_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem);
+        int per_sm = (int)((n + sms - 1) / sms);  // worlds per block: one block per SM where the batch allows
+        const bool pair = p.step_mode ? p.step_mode == 2 : step_pairs(n, sms, p.C);
+        const int wpw = pair ? 2 : 1, max_warps = pair ? PAIR_MAX_WARPS : STEP_MAX_WARPS;
+        int warps = (per_sm + wpw - 1) / wpw;
+        warps = warps < 1 ? 1 : (warps > max_warps ? max_warps : warps);
+        const int fit = STEP_MAX_SMEM / (wpw * region);
+        warps = warps > fit ? fit : warps;
+        const size_t smem = (size_t)wpw * warps * region;
+        auto kern = pair ? goib2d_step_pair_kernel : goib2d_step_kernel;
+        static int smem_set[2][64];  // the dynamic shared memory limit set per kernel and device
+        if (dev < 64 && smem > 48 * 1024 && (size_t)smem_set[pair][dev] < smem) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e != cudaSuccess) return e;
-            smem_set[dev] = (int)smem;
+            smem_set[pair][dev] = (int)smem;
         }
-        const unsigned sblocks = (unsigned)((n + wpb - 1) / wpb);
+        const int per_block = wpw * warps;
+        const unsigned sblocks = (unsigned)((n + per_block - 1) / per_block);
         for (int k = 0; k < p.n_steps; ++k) {
             p.step = k;
-            goib2d_step_kernel<<<sblocks, 32 * wpb, smem, stream>>>(p);
+            kern<<<sblocks, 32 * warps, smem, stream>>>(p);
         }
         return cudaGetLastError();
     }

@@ -151,6 +151,11 @@ class Engine:
                                              C.c_float(max_length), out.data_ptr(), self._stream(device)))
         return out
 
+    def set_step_mode(self, mode):
+        """Worlds per warp of the one-launch step (batches below 16384 worlds): 0 chosen per batch, 1 or 2. Results
+        are identical in every mode."""
+        native.check(self.lib.goib2d_set_step_mode(self.handle, int(mode)))
+
     def set_event_log(self, capacity):
         """Log each world's contact events (Begin / End / PostSolve, goib2d_event) of every step, capacity per world
         (0: off)."""

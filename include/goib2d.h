@@ -142,6 +142,12 @@ int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
  * world per thread, TOI). For launch accounting and profilers; no counterpart in the reference engine. */
 int goib2d_kernels_per_step(int64_t n_worlds);
 
+/* How the one-launch step (batches below 16384 worlds) maps worlds to warps: 0 (default) chosen per batch - two
+ * worlds per warp for batches of more than 16 worlds per SM with at most 128 contact slots, else one; 1 one world
+ * per warp; 2 two worlds per warp (one per half-warp). Results are identical in every mode; only the speed differs.
+ * No counterpart in the reference engine. */
+int goib2d_set_step_mode(goib2d_model *model, int32_t mode);
+
 /* ---- Env helpers around the step (no counterpart in the reference engine, whose RL env is outside it). Same
  * contact_capacity / fixture_rows / leaves conventions as goib2d_step; asynchronous on `stream`. */
 

@@ -112,6 +112,45 @@ def test_gpu_matches_oracle_on_edge_workloads(api, cfg, n, steps):
     assert ((eng.status() & 0b1011) == 0).all()
 
 
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("cfg,n,steps", [("c0", 63, 40), ("c1", 255, 30), ("c2", 7, 8), ("c3", 127, 20),
+                                         ("c4", 63, 20), ("c1e", 129, 20)])
+def test_step_modes_match_oracle(api, mode, cfg, n, steps):
+    """The one-launch step with one world per warp (mode 1) and with two worlds per warp, one per half-warp (mode 2),
+    equals the oracle world for world; odd batches leave a half-warp without a world."""
+    from goib2d import configs
+    sc, model, host = configs.batch(cfg, n)
+    dev = api.to_device(host)
+    eng = api.Engine(model, host.bodies.type.shape[1])
+    try:
+        eng.set_step_mode(mode)
+        eng.step_(dev, sc.settings, configs.DT, n_steps=steps)
+        status = eng.status()
+    finally:
+        eng.close()
+    want = oracle_lib.step(model, host, sc.settings, configs.DT, steps, threads=8)
+    assert_states_equal(api.to_host(dev), want, f"{cfg} mode {mode}")
+    assert ((status & 0b1011) == 0).all()
+
+
+def test_bench_batch_matches_oracle(api):
+    """The benchmark's batch (c1, 4096 worlds: two worlds per warp by the per-batch choice) equals the oracle on
+    worlds from both ends of the batch."""
+    from goib2d import configs
+    from goib2d.world import map_state
+    n, steps = 4096, 12
+    sc, model, host = configs.batch("c1", n)
+    dev = api.to_device(host)
+    eng = api.engine_for(model, host.bodies.type.shape[1])
+    eng.step_(dev, sc.settings, configs.DT, n_steps=steps)
+    got = api.to_host(dev)
+    pick = np.r_[0:64, 2048:2080, n - 64:n]
+    want = oracle_lib.step(model, map_state(lambda x: np.ascontiguousarray(np.asarray(x)[pick]), host), sc.settings,
+                           configs.DT, steps, threads=8)
+    assert_states_equal(map_state(lambda x: np.asarray(x)[pick], got), want, f"c1 n={n}")
+    assert ((eng.status() & 0b1011) == 0).all()
+
+
 @pytest.mark.parametrize("cfg,steps", [("c1", 12), ("c4", 6)])
 def test_large_batches_match_oracle(api, cfg, steps):
     """A batch large enough that the constraint sweeps run one world per thread (16384 worlds and up) equals the
