@@ -298,7 +298,7 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                          "algorithmic_bytes_per_world_step": bytes_ws,
-                         "kernel": (f"one step's launch group ({native.load().goib2d_kernels_per_step(n)} "
+                         "kernel": (f"one step's launch group ({eng.kernels_per_step(n)} "
                                     f"kernel(s){' + the reset kernel' if resets else ''}), timed as one unit by the "
                                     "per-step CUDA events"),
                          "traffic_source": f"profiles/traffic_{args.config}.json (ncu dram bytes of the launch group)"
@@ -307,7 +307,7 @@ def main():
                     "d2h_bytes_per_step": n * 6 * 4 * world_size, "steps": Ke,
                     "path": "actions read from pinned host memory by the step kernel; goib2d_observe writes the pot's "
                             "pose and velocity to pinned host memory"},
-            "gpu_launches": K * (native.load().goib2d_kernels_per_step(n) + int(resets)), "clocks": clk,
+            "gpu_launches": K * (eng.kernels_per_step(n) + int(resets)), "clocks": clk,
             "wall_s_timed": wall,
             "nonfinite_worlds": nonfinite,
             "cpu_baseline": cpu}

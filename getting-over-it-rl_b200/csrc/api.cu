@@ -14,7 +14,7 @@
 
 namespace gb {
 cudaError_t launch_steps(StepParams p, cudaStream_t stream);  // step.cu
-int kernels_per_step(int64_t n_worlds);                       // step.cu
+int kernels_per_step(int64_t n_worlds, int n_joints);         // step.cu
 cudaError_t launch_reset(const EnvParams &p, cudaStream_t s);    // env.cuh (compiled in step.cu)
 cudaError_t launch_observe(const EnvParams &p, cudaStream_t s);  // env.cuh
 cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s);  // env.cuh
@@ -250,7 +250,10 @@ static int device_view(const void *ptr, const void **out) {
 
 int goib2d_version(void) { return GOIB2D_ABI_VERSION; }
 
-int goib2d_kernels_per_step(int64_t n_worlds) { return gb::kernels_per_step(n_worlds); }
+int goib2d_kernels_per_step(const goib2d_model *model, int64_t n_worlds) {
+    if (!model) return fail(GOIB2D_EINVAL, "null argument");
+    return gb::kernels_per_step(n_worlds, model->full.J);
+}
 
 const char *goib2d_last_error(void) { return g_err.c_str(); }
 

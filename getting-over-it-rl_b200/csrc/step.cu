@@ -1272,8 +1272,9 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
 #endif
 }
 
-// b2World::Step (step.py:28-47) in parts; one warp per world. Below THREAD_SWEEPS_MIN_WORLDS a step is one launch
-// (goib2d_step_kernel: parts 0, 1, 5 with a block barrier between them); above it each part is a kernel of its own.
+// b2World::Step (step.py:28-47) in parts. A step is one launch (goib2d_step_kernel / goib2d_step_pair_kernel,
+// whole_step: the parts' phases with block barriers between them) or, for the batches part_kernels() picks, each part
+// a kernel of its own (one warp per world).
 //   0  the action channels, FindNewContacts for new fixtures, b2ContactManager::Collide
 //   1  b2World::Solve: islands, velocity integration, the constraint rows (solve), the constraint sweeps on lane 0
 //      (solve_constraints), write back and sleep (solve_finish), SynchronizeFixtures and FindNewContacts
@@ -1338,7 +1339,7 @@ __device__ __forceinline__ void put_status(const Ctx &x, bool first) {
     }
 }
 
-// A part kernel (batches of THREAD_SWEEPS_MIN_WORLDS and more): one warp per world, 4 worlds per block.
+// A part kernel (the batches part_kernels() picks): one warp per world, 4 worlds per block.
 template <int PART>
 __device__ __forceinline__ void step_part(const StepParams &p) {
     const int warp = threadIdx.x >> 5;
@@ -1360,7 +1361,8 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     put_status(x, PART == 0 && p.step == 0);
 }
 
-// The whole step in one launch (batches below THREAD_SWEEPS_MIN_WORLDS): one block per SM where the batch allows,
+// The whole step in one launch (see part_kernels for the batches that run part kernels instead): one block per SM
+// where the batch allows,
 // the block's threads meeting between phases (step_sync: collide | islands | rows | sweeps | write back and sleep |
 // broadphase | TOI), and WPW worlds per warp.
 // - Phase barriers: worlds are independent, so a phase's tail is the slowest of the block's worlds rather than of
@@ -1482,13 +1484,20 @@ extern "C" __global__ void __launch_bounds__(32 * PAIR_MAX_WARPS, 1)
 }
 
 namespace gb {
-// From this many worlds the constraint sweeps run one world per thread: 32 worlds' sweeps share a warp's issue
-// slots, which pays once the batch fills the SMs with warps of sweeps; below it a warp per world keeps more warps in
-// flight per SM. (Both run the same code, in the same order within a world.)
+// Batches of at least THREAD_SWEEPS_MIN_WORLDS worlds whose model has at least THREAD_SWEEPS_MIN_JOINTS joints run
+// a step as six part kernels with the constraint sweeps one world per THREAD (goib2d_constraints_kernel): 32
+// worlds' long sequential joint sweeps share one warp instruction. Everything else is the one-launch step. Both run
+// the same code in the same order within a world, so results are identical. Measured: c4 (22 joints, 65536
+// worlds) 11.1 M world-steps/s as part kernels, 9.1 M as one launch; c1 (2 joints, 16384 worlds) 21.1 M as part
+// kernels, 23.2 M as one launch.
 constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = 16384;
-// p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: per step one goib2d_step_kernel, or for
-// large batches the collide part, the solve part in pieces (rows / thread sweeps / finish / broadphase), the TOI part
-int kernels_per_step(int64_t n_worlds) { return n_worlds < THREAD_SWEEPS_MIN_WORLDS ? 1 : 6; }
+constexpr int THREAD_SWEEPS_MIN_JOINTS = 8;
+bool part_kernels(int64_t n_worlds, int n_joints) {
+    return n_worlds >= THREAD_SWEEPS_MIN_WORLDS && n_joints >= THREAD_SWEEPS_MIN_JOINTS;
+}
+// p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: per step one goib2d_step(_pair)_kernel,
+// or the collide part, the solve part in pieces (rows / thread sweeps / finish / broadphase) and the TOI part
+int kernels_per_step(int64_t n_worlds, int n_joints) { return part_kernels(n_worlds, n_joints) ? 6 : 1; }
 // Two worlds per warp (goib2d_step_pair_kernel) for crowded batches of small worlds: more than PAIR_MIN_PER_SM
 // worlds per SM (fewer leave the SM's issue slots free, and a pair only adds the two worlds' divergence) and at most
 // PAIR_MAX_CONTACTS contact slots (worlds with more grow islands and TOI event chains that differ between the two
@@ -1502,7 +1511,7 @@ bool step_pairs(int64_t n_worlds, int sms, int contact_capacity) {
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     p.world0 = 0, p.world_end = p.n_worlds;
     const int64_t n = p.n_worlds;
-    if (n < THREAD_SWEEPS_MIN_WORLDS) {  // one launch per step
+    if (!part_kernels(n, p.m.J)) {  // one launch per step
         int dev = 0, sms = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -151,6 +151,12 @@ class Engine:
                                              C.c_float(max_length), out.data_ptr(), self._stream(device)))
         return out
 
+    def kernels_per_step(self, n_worlds):
+        """Kernel launches one step of n_worlds worlds of this model makes (goib2d_kernels_per_step)."""
+        k = self.lib.goib2d_kernels_per_step(self.handle, int(n_worlds))
+        native.check(min(k, 0))
+        return k
+
     def set_step_mode(self, mode):
         """Worlds per warp of the one-launch step (batches below 16384 worlds): 0 chosen per batch, 1 or 2. Results
         are identical in every mode."""

@@ -201,7 +201,7 @@ def load():
         "goib2d_status_copy": (C.c_int, [vp, _i, C.c_int64]),
         "goib2d_step_noalloc": (C.c_int, [vp, vp, C.c_float, C.c_int32, C.c_int32, C.c_int64, C.c_int32,
                                           C.POINTER(vp), vp, vp]),
-        "goib2d_kernels_per_step": (C.c_int, [C.c_int64]),
+        "goib2d_kernels_per_step": (C.c_int, [vp, C.c_int64]),
         "goib2d_candidate_pairs": (C.c_int, [C.POINTER(PairDesc), _i, _i, C.c_int64, C.POINTER(C.c_int64)]),
         "goib2d_set_event_log": (C.c_int, [vp, C.c_int32]),
         "goib2d_set_step_mode": (C.c_int, [vp, C.c_int32]),

@@ -137,12 +137,13 @@ int goib2d_status(goib2d_model *model, const int32_t **device_status, int64_t *n
 /* The same status words copied to host memory (n <= the last step's n_worlds); synchronises the device. */
 int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
 
-/* Kernel launches one goib2d_step step makes for a batch of n_worlds worlds: 1 (the whole step in one launch), or
- * 6 for batches of 16384 worlds and more (collide, the solve in four pieces with the constraint sweeps run one
- * world per thread, TOI). For launch accounting and profilers; no counterpart in the reference engine. */
-int goib2d_kernels_per_step(int64_t n_worlds);
+/* Kernel launches one goib2d_step step makes for a batch of n_worlds worlds of this model: 1 (the whole step in one
+ * launch), or 6 for batches of 16384 worlds and more of models with 8 joints or more (collide, the solve in four
+ * pieces with the constraint sweeps run one world per thread, TOI). For launch accounting and profilers; no
+ * counterpart in the reference engine. */
+int goib2d_kernels_per_step(const goib2d_model *model, int64_t n_worlds);
 
-/* How the one-launch step (batches below 16384 worlds) maps worlds to warps: 0 (default) chosen per batch - two
+/* How the one-launch step (goib2d_kernels_per_step 1) maps worlds to warps: 0 (default) chosen per batch - two
  * worlds per warp for batches of more than 16 worlds per SM with at most 128 contact slots, else one; 1 one world
  * per warp; 2 two worlds per warp (one per half-warp). Results are identical in every mode; only the speed differs.
  * No counterpart in the reference engine. */

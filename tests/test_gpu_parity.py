@@ -133,6 +133,18 @@ def test_step_modes_match_oracle(api, mode, cfg, n, steps):
     assert ((status & 0b1011) == 0).all()
 
 
+def test_kernels_per_step(api):
+    """One launch per step, except large batches of models with many joints (six part kernels)."""
+    from goib2d import configs
+    for cfg, n, want in (("c1", 4096, 1), ("c1", 1 << 16, 1), ("c4", 8192, 1), ("c4", 1 << 16, 6)):
+        sc, model, host = configs.batch(cfg, 2)
+        eng = api.Engine(model, host.bodies.type.shape[1])
+        try:
+            assert eng.kernels_per_step(n) == want, (cfg, n)
+        finally:
+            eng.close()
+
+
 def test_bench_batch_matches_oracle(api):
     """The benchmark's batch (c1, 4096 worlds: two worlds per warp by the per-batch choice) equals the oracle on
     worlds from both ends of the batch."""
@@ -153,8 +165,8 @@ def test_bench_batch_matches_oracle(api):
 
 @pytest.mark.parametrize("cfg,steps", [("c1", 12), ("c4", 6)])
 def test_large_batches_match_oracle(api, cfg, steps):
-    """A batch large enough that the constraint sweeps run one world per thread (16384 worlds and up) equals the
-    oracle on worlds taken from both ends of the batch."""
+    """Large batches (16384 worlds) equal the oracle on worlds taken from both ends of the batch: c1 as one launch
+    per step (two worlds per warp), c4 (22 joints) as part kernels with the constraint sweeps one world per thread."""
     from goib2d import configs
     from goib2d.world import map_state
     n = 16384
