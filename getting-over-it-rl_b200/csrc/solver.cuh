@@ -19,31 +19,39 @@ __device__ __forceinline__ Rot body_rot(const Bodies &bd, int b, float angle) {
     return q;
 }
 
-// b2ContactSolver constructor + InitializeVelocityConstraints for one ordered contact (contact_solver.py:32-147)
+// b2ContactSolver constructor + InitializeVelocityConstraints for one ordered contact (contact_solver.py:32-147).
+// Every load comes first (three dependent levels: the slot's fields, its fixtures, their bodies), then the
+// arithmetic, then the row's stores: to the compiler a store to the row may alias the State's float arrays, so a
+// load placed after one could not be hoisted above it and would wait for all the arithmetic before it.
 __device__ __noinline__ void prepare_contact(const DevModel &m, const W &w, int slot, const Bodies &bd, bool warm,
                                              float dt_ratio, float velocity_threshold, VCRow &c) {
-    int fa = w.fa[slot], fb = w.fb[slot];
-    int ia = m.fixture_body[fa], ib = m.fixture_body[fb];
-    c.slot = slot, c.ia = ia, c.ib = ib;
-    c.mA = w.inv_mass[ia], c.mB = w.inv_mass[ib], c.iA = w.inv_inertia[ia], c.iB = w.inv_inertia[ib];
-    c.lcA = w.blc(ia), c.lcB = w.blc(ib);
-    float rA_ = m.radius[fa], rB_ = m.radius[fb];
-    c.radA = rA_, c.radB = rB_;
-    c.mtype = w.mtype[slot];
-    int count = w.count[slot];
-    c.ln = {w.local_normal[2 * slot], w.local_normal[2 * slot + 1]};
-    c.lp = {w.local_point[2 * slot], w.local_point[2 * slot + 1]};
-    for (int j = 0; j < 2; ++j) c.pl[j] = {w.point_local[4 * slot + 2 * j], w.point_local[4 * slot + 2 * j + 1]};
+    const int fa = w.fa[slot], fb = w.fb[slot];
+    const int mtype = w.mtype[slot], count = w.count[slot];
+    const V2 ln{w.local_normal[2 * slot], w.local_normal[2 * slot + 1]};
+    const V2 lp{w.local_point[2 * slot], w.local_point[2 * slot + 1]};
+    V2 pl[2];
+    float ni[2], ti[2];
     for (int j = 0; j < 2; ++j) {
-        c.ni[j] = warm ? dt_ratio * w.normal_impulse[2 * slot + j] : 0.0f;
-        c.ti[j] = warm ? dt_ratio * w.tangent_impulse[2 * slot + j] : 0.0f;
+        pl[j] = {w.point_local[4 * slot + 2 * j], w.point_local[4 * slot + 2 * j + 1]};
+        ni[j] = warm ? dt_ratio * w.normal_impulse[2 * slot + j] : 0.0f;
+        ti[j] = warm ? dt_ratio * w.tangent_impulse[2 * slot + j] : 0.0f;
     }
-    V2 cA{bd.cx[ia], bd.cy[ia]}, cB{bd.cx[ib], bd.cy[ib]};
-    Xf xfA = xf_from_q(cA, Rot{bd.qc[ia], bd.qs[ia]}, c.lcA);
-    Xf xfB = xf_from_q(cB, Rot{bd.qc[ib], bd.qs[ib]}, c.lcB);
+    const float friction = w.friction[slot], tangent_speed = w.tangent_speed[slot];
+    const float restitution = w.restitution[slot];
+    const int ia = m.fixture_body[fa], ib = m.fixture_body[fb];
+    const float rA_ = m.radius[fa], rB_ = m.radius[fb];
+    const float mA = w.inv_mass[ia], mB = w.inv_mass[ib], iA = w.inv_inertia[ia], iB = w.inv_inertia[ib];
+    const V2 lcA = w.blc(ia), lcB = w.blc(ib);
+    const V2 cA{bd.cx[ia], bd.cy[ia]}, cB{bd.cx[ib], bd.cy[ib]};
+    const Rot qA{bd.qc[ia], bd.qs[ia]}, qB{bd.qc[ib], bd.qs[ib]};
+    const V2 vA{bd.vx[ia], bd.vy[ia]}, vB{bd.vx[ib], bd.vy[ib]};
+    const float wA = bd.vw[ia], wB = bd.vw[ib];
+
+    const Xf xfA = xf_from_q(cA, qA, lcA);
+    const Xf xfB = xf_from_q(cB, qB, lcB);
     V2 nrm, pts[2];
-    if (c.mtype == CIRCLES) {  // b2WorldManifold::Initialize
-        V2 pA = xf_mul(xfA, c.lp), pB = xf_mul(xfB, c.pl[0]);
+    if (mtype == CIRCLES) {  // b2WorldManifold::Initialize
+        V2 pA = xf_mul(xfA, lp), pB = xf_mul(xfB, pl[0]);
         V2 d = sub(pB, pA);
         bool far = dot(d, d) > EPS * EPS;
         V2 nn = normalize(d);
@@ -51,10 +59,10 @@ __device__ __noinline__ void prepare_contact(const DevModel &m, const W &w, int 
         V2 ccA{pA.x + rA_ * cn.x, pA.y + rA_ * cn.y}, ccB{pB.x - rB_ * cn.x, pB.y - rB_ * cn.y};
         V2 cp{0.5f * (ccA.x + ccB.x), 0.5f * (ccA.y + ccB.y)};
         nrm = cn, pts[0] = pts[1] = cp;
-    } else if (c.mtype == FACE_A) {
-        V2 fn = rot(xfA.q, c.ln), fpl = xf_mul(xfA, c.lp);
+    } else if (mtype == FACE_A) {
+        V2 fn = rot(xfA.q, ln), fpl = xf_mul(xfA, lp);
         for (int j = 0; j < 2; ++j) {
-            V2 qp = xf_mul(xfB, c.pl[j]);
+            V2 qp = xf_mul(xfB, pl[j]);
             float d = dot(sub(qp, fpl), fn);
             float s_ = rA_ - d;
             V2 aA{qp.x + s_ * fn.x, qp.y + s_ * fn.y}, aB{qp.x - rB_ * fn.x, qp.y - rB_ * fn.y};
@@ -62,9 +70,9 @@ __device__ __noinline__ void prepare_contact(const DevModel &m, const W &w, int 
         }
         nrm = fn;
     } else {
-        V2 fn = rot(xfB.q, c.ln), fpl = xf_mul(xfB, c.lp);
+        V2 fn = rot(xfB.q, ln), fpl = xf_mul(xfB, lp);
         for (int j = 0; j < 2; ++j) {
-            V2 qp = xf_mul(xfA, c.pl[j]);
+            V2 qp = xf_mul(xfA, pl[j]);
             float d = dot(sub(qp, fpl), fn);
             float s_ = rB_ - d;
             V2 bB{qp.x + s_ * fn.x, qp.y + s_ * fn.y}, bA{qp.x - rA_ * fn.x, qp.y - rA_ * fn.y};
@@ -72,40 +80,50 @@ __device__ __noinline__ void prepare_contact(const DevModel &m, const W &w, int 
         }
         nrm = neg(fn);
     }
-    c.n = nrm;
-    V2 t = cross_vs(nrm, 1.0f);
-    V2 vA{bd.vx[ia], bd.vy[ia]}, vB{bd.vx[ib], bd.vy[ib]};
-    float wA = bd.vw[ia], wB = bd.vw[ib];
-    c.friction = w.friction[slot], c.tangent_speed = w.tangent_speed[slot];
-    float restitution = w.restitution[slot];
+    const V2 t = cross_vs(nrm, 1.0f);
+    V2 ra[2], rb[2];
+    float nmass[2], tmass[2], bias[2];
     for (int j = 0; j < 2; ++j) {
-        V2 ra = sub(pts[j], cA), rb = sub(pts[j], cB);
-        float rnA = cross(ra, nrm), rnB = cross(rb, nrm);
-        float kn = ((c.mA + c.mB) + (c.iA * rnA) * rnA) + (c.iB * rnB) * rnB;
-        float rtA = cross(ra, t), rtB = cross(rb, t);
-        float kt = ((c.mA + c.mB) + (c.iA * rtA) * rtA) + (c.iB * rtB) * rtB;
-        V2 wBr = cross_sv(wB, rb), wAr = cross_sv(wA, ra);
+        ra[j] = sub(pts[j], cA), rb[j] = sub(pts[j], cB);
+        float rnA = cross(ra[j], nrm), rnB = cross(rb[j], nrm);
+        float kn = ((mA + mB) + (iA * rnA) * rnA) + (iB * rnB) * rnB;
+        float rtA = cross(ra[j], t), rtB = cross(rb[j], t);
+        float kt = ((mA + mB) + (iA * rtA) * rtA) + (iB * rtB) * rtB;
+        V2 wBr = cross_sv(wB, rb[j]), wAr = cross_sv(wA, ra[j]);
         float vrel = dot(nrm, V2{((vB.x + wBr.x) - vA.x) - wAr.x, ((vB.y + wBr.y) - vA.y) - wAr.y});
-        c.rA[j] = ra, c.rB[j] = rb;
-        c.nmass[j] = inv_if_pos(kn);
-        c.tmass[j] = inv_if_pos(kt);
-        c.bias[j] = vrel < -velocity_threshold ? -restitution * vrel : 0.0f;
+        nmass[j] = inv_if_pos(kn);
+        tmass[j] = inv_if_pos(kt);
+        bias[j] = vrel < -velocity_threshold ? -restitution * vrel : 0.0f;
     }
-    float rn1A = cross(c.rA[0], nrm), rn1B = cross(c.rB[0], nrm);
-    float rn2A = cross(c.rA[1], nrm), rn2B = cross(c.rB[1], nrm);
-    float k11 = ((c.mA + c.mB) + (c.iA * rn1A) * rn1A) + (c.iB * rn1B) * rn1B;
-    float k22 = ((c.mA + c.mB) + (c.iA * rn2A) * rn2A) + (c.iB * rn2B) * rn2B;
-    float k12 = ((c.mA + c.mB) + (c.iA * rn1A) * rn2A) + (c.iB * rn1B) * rn2B;
+    float rn1A = cross(ra[0], nrm), rn1B = cross(rb[0], nrm);
+    float rn2A = cross(ra[1], nrm), rn2B = cross(rb[1], nrm);
+    float k11 = ((mA + mB) + (iA * rn1A) * rn1A) + (iB * rn1B) * rn1B;
+    float k22 = ((mA + mB) + (iA * rn2A) * rn2A) + (iB * rn2B) * rn2B;
+    float k12 = ((mA + mB) + (iA * rn1A) * rn2A) + (iB * rn1B) * rn2B;
     bool safe = k11 * k11 < MAX_COND * (k11 * k22 - k12 * k12);
     bool two = count == 2;
-    c.count = (two && !safe) ? 1 : count;
-    c.pc_count = count;
     float det = inv_or_zero(k11 * k22 - k12 * k12);
     bool use_k = two && safe;
+
+    c.slot = slot, c.ia = ia, c.ib = ib;
+    c.count = (two && !safe) ? 1 : count;
+    c.pc_count = count;
+    c.mtype = mtype;
+    c.mA = mA, c.mB = mB, c.iA = iA, c.iB = iB;
+    c.n = nrm;
+    c.friction = friction, c.tangent_speed = tangent_speed;
+    for (int j = 0; j < 2; ++j) {
+        c.rA[j] = ra[j], c.rB[j] = rb[j];
+        c.nmass[j] = nmass[j], c.tmass[j] = tmass[j], c.bias[j] = bias[j];
+        c.ni[j] = ni[j], c.ti[j] = ti[j];
+        c.pl[j] = pl[j];
+    }
     c.K[0] = use_k ? k11 : 0.0f, c.K[1] = use_k ? k12 : 0.0f, c.K[2] = use_k ? k12 : 0.0f;
     c.K[3] = use_k ? k22 : 0.0f;
     c.NM[0] = use_k ? det * k22 : 0.0f, c.NM[1] = use_k ? -det * k12 : 0.0f;
     c.NM[2] = use_k ? -det * k12 : 0.0f, c.NM[3] = use_k ? det * k11 : 0.0f;
+    c.ln = ln, c.lp = lp, c.lcA = lcA, c.lcB = lcB;
+    c.radA = rA_, c.radB = rB_;
 }
 
 __device__ __forceinline__ void contact_warm_start(const VCRow &c, const Bodies &bd) {  // contact_solver.py:165-184
@@ -260,29 +278,34 @@ __device__ __forceinline__ void k_prism(float mA, float mB, float iA, float iB, 
 // InitVelocityConstraints for one ordered joint, without the velocity writes (joints.py:61-174)
 __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int jid, const Bodies &bd,
                                            const goib2d_settings &s, float dt, float dt_ratio, bool warm, JRow &r) {
+    // every load first (the joint's fields, then its bodies), then the arithmetic, then the row's stores (see
+    // prepare_contact)
     const bool v24 = s.revolute_v24;
-    r.jid = jid;
-    r.type = m.joint_type[jid];
-    int ia = m.joint_a[jid], ib = m.joint_b[jid];
-    r.ia = ia, r.ib = ib;
-    float mA = w.inv_mass[ia], mB = w.inv_mass[ib], iA = w.inv_inertia[ia], iB = w.inv_inertia[ib];
-    r.mA = mA, r.mB = mB, r.iA = iA, r.iB = iB;
-    V2 lcA = w.blc(ia), lcB = w.blc(ib);
-    V2 cA{bd.cx[ia], bd.cy[ia]}, cB{bd.cx[ib], bd.cy[ib]};
-    float aA = bd.ca[ia], aB = bd.ca[ib];
-    Rot qA{bd.qc[ia], bd.qs[ia]}, qB{bd.qc[ib], bd.qs[ib]};
-    V2 la{m.local_anchor_a[2 * jid] - lcA.x, m.local_anchor_a[2 * jid + 1] - lcA.y};
-    V2 lb{m.local_anchor_b[2 * jid] - lcB.x, m.local_anchor_b[2 * jid + 1] - lcB.y};
-    V2 rA = rot(qA, la), rB = rot(qB, lb);
-    r.rA = rA, r.rB = rB, r.la = la, r.lb = lb;
-    float ref = m.reference_angle[jid];
-    r.ref = ref;
-    bool en_motor = w.enable_motor[jid], en_limit = w.enable_limit[jid];
-    float lower = w.lower[jid], upper = w.upper[jid];
-    int state_in = w.limit_state[jid];
+    const int type = m.joint_type[jid];
+    const int ia = m.joint_a[jid], ib = m.joint_b[jid];
+    const V2 laa{m.local_anchor_a[2 * jid], m.local_anchor_a[2 * jid + 1]};
+    const V2 lab{m.local_anchor_b[2 * jid], m.local_anchor_b[2 * jid + 1]};
+    const float ref = m.reference_angle[jid];
+    const V2 lxa{m.local_axis_a[2 * jid], m.local_axis_a[2 * jid + 1]};
+    const V2 lya{m.local_yaxis_a[2 * jid], m.local_yaxis_a[2 * jid + 1]};
+    const bool en_motor = w.enable_motor[jid], en_limit = w.enable_limit[jid];
+    const float lower = w.lower[jid], upper = w.upper[jid];
+    const int state_in = w.limit_state[jid];
     float ix = w.impulse[3 * jid], iy = w.impulse[3 * jid + 1], iz = w.impulse[3 * jid + 2];
     float mimp = w.motor_impulse[jid];
-    bool is_rev = r.type == REVOLUTE, is_pri = r.type == PRISMATIC;
+    const float frequency = w.frequency[jid], damping = w.damping[jid];
+    const float motor_speed = w.motor_speed[jid], max_motor = w.max_motor[jid];
+    const float lower_imp = w.lower_impulse[jid], upper_imp = w.upper_impulse[jid];
+    const float mA = w.inv_mass[ia], mB = w.inv_mass[ib], iA = w.inv_inertia[ia], iB = w.inv_inertia[ib];
+    const V2 lcA = w.blc(ia), lcB = w.blc(ib);
+    const V2 cA{bd.cx[ia], bd.cy[ia]}, cB{bd.cx[ib], bd.cy[ib]};
+    const float aA = bd.ca[ia], aB = bd.ca[ib];
+    const Rot qA{bd.qc[ia], bd.qs[ia]}, qB{bd.qc[ib], bd.qs[ib]};
+
+    const V2 la{laa.x - lcA.x, laa.y - lcA.y};
+    const V2 lb{lab.x - lcB.x, lab.y - lcB.y};
+    const V2 rA = rot(qA, la), rB = rot(qB, lb);
+    const bool is_rev = type == REVOLUTE, is_pri = type == PRISMATIC;
     V3 revx, revy, revz;
     k_rev(mA, mB, iA, iB, rA, rB, revx, revy, revz);
     bool fixed = (iA + iB) == 0;
@@ -298,9 +321,6 @@ __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int ji
                                      : INACTIVE_LIMIT;
     bool rev_zero_z = lim_on && !equal && (rev_state == INACTIVE_LIMIT || rev_state != state_in);
     float dx = ((cB.x - cA.x) + rB.x) - rA.x, dy = ((cB.y - cA.y) + rB.y) - rA.y;
-    V2 lxa{m.local_axis_a[2 * jid], m.local_axis_a[2 * jid + 1]};
-    V2 lya{m.local_yaxis_a[2 * jid], m.local_yaxis_a[2 * jid + 1]};
-    r.lx = lxa, r.ly = lya;
     V2 ax = rot(qA, lxa);
     float a1 = cross(V2{dx + rA.x, dy + rA.y}, ax), a2 = cross(rB, ax);
     float pri_mm = ((mA + mB) + (iA * a1) * a1) + (iB * a2) * a2;
@@ -318,7 +338,7 @@ __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int ji
                                      : INACTIVE_LIMIT;
     bool pri_zero_z = !en_limit || (!pequal && (pri_state == INACTIVE_LIMIT || pri_state != state_in));
     float pri_mimp = en_motor ? mimp : 0.0f;
-    bool soft = w.frequency[jid] > 0;
+    bool soft = frequency > 0;
     V3 i22x, i22y, i22z, symx, symy, symz;
     inverse22_of33(revx, revy, i22x, i22y, i22z);
     sym_inverse33(revx, revy, revz, symx, symy, symz);
@@ -326,8 +346,8 @@ __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int ji
     float wm = inv_if_pos(invM);
     float C = (aB - aA) - ref;
     const float two_pi = 2.0f * PI_F;
-    float omega = two_pi * w.frequency[jid];
-    float d = ((2.0f * wm) * w.damping[jid]) * omega;
+    float omega = two_pi * frequency;
+    float d = ((2.0f * wm) * damping) * omega;
     float kk = (wm * omega) * omega;
     float h = dt;
     float gamma = inv_or_zero(h * (d + h * kk));
@@ -336,33 +356,42 @@ __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int ji
     bool use22 = soft || revz.z == 0;
     V3 wmx = use22 ? i22x : symx, wmy = use22 ? i22y : symy, wmz = use22 ? i22z : symz;
     if (soft) wmz.z = ezz_soft;
-    if (is_rev)
-        r.Kx = revx, r.Ky = revy, r.Kz = revz;
-    else if (is_pri)
-        r.Kx = prx, r.Ky = pry, r.Kz = prz;
-    else
-        r.Kx = wmx, r.Ky = wmy, r.Kz = wmz;
-    r.limit_state = is_rev ? rev_state : is_pri ? pri_state : INACTIVE_LIMIT;
+    const V3 Kx = is_rev ? revx : is_pri ? prx : wmx;
+    const V3 Ky = is_rev ? revy : is_pri ? pry : wmy;
+    const V3 Kz = is_rev ? revz : is_pri ? prz : wmz;
+    const int limit_state = is_rev ? rev_state : is_pri ? pri_state : INACTIVE_LIMIT;
     bool zero_z = is_rev ? (v24 ? false : rev_zero_z) : is_pri ? pri_zero_z : false;
     if (zero_z) iz = 0.0f;
     mimp = is_rev ? rev_mimp : is_pri ? pri_mimp : 0.0f;
+    float imp[5];
 #define SC(x) (warm ? (x) * dt_ratio : 0.0f)
     if (v24) {
-        float lo = (is_rev && lim_on) ? w.lower_impulse[jid] : 0.0f;
-        float up = (is_rev && lim_on) ? w.upper_impulse[jid] : 0.0f;
-        r.imp[0] = SC(ix), r.imp[1] = SC(iy), r.imp[2] = is_rev ? iz : SC(iz), r.imp[3] = SC(lo), r.imp[4] = SC(up);
+        float lo = (is_rev && lim_on) ? lower_imp : 0.0f;
+        float up = (is_rev && lim_on) ? upper_imp : 0.0f;
+        imp[0] = SC(ix), imp[1] = SC(iy), imp[2] = is_rev ? iz : SC(iz), imp[3] = SC(lo), imp[4] = SC(up);
     } else {
-        r.imp[0] = SC(ix), r.imp[1] = SC(iy), r.imp[2] = SC(iz), r.imp[3] = 0.0f, r.imp[4] = 0.0f;
+        imp[0] = SC(ix), imp[1] = SC(iy), imp[2] = SC(iz), imp[3] = 0.0f, imp[4] = 0.0f;
     }
-    r.d33 = det33_inv(r.Kx, r.Ky, r.Kz);
-    r.d22 = det22_inv(r.Kx.x, r.Ky.x, r.Kx.y, r.Ky.y);
-    r.mimp = SC(mimp);
+    const float mimp_row = SC(mimp);
 #undef SC
+    const float d33 = det33_inv(Kx, Ky, Kz);
+    const float d22 = det22_inv(Kx.x, Ky.x, Kx.y, Ky.y);
+
+    r.jid = jid, r.type = type, r.ia = ia, r.ib = ib;
+    r.mA = mA, r.mB = mB, r.iA = iA, r.iB = iB;
+    r.rA = rA, r.rB = rB, r.la = la, r.lb = lb;
+    r.ref = ref;
+    r.lx = lxa, r.ly = lya;
+    r.Kx = Kx, r.Ky = Ky, r.Kz = Kz;
+    r.limit_state = limit_state;
+    for (int k = 0; k < 5; ++k) r.imp[k] = imp[k];
+    r.d33 = d33, r.d22 = d22;
+    r.mimp = mimp_row;
     r.inv_dt = dt > 0 ? 1.0f / dt : 0.0f;
     r.motor_mass = is_rev ? rev_mm : is_pri ? pri_mm : 0.0f;
     r.enable_motor = en_motor, r.enable_limit = en_limit;
-    r.motor_speed = w.motor_speed[jid];
-    r.max_impulse = dt * w.max_motor[jid];
+    r.motor_speed = motor_speed;
+    r.max_impulse = dt * max_motor;
     r.ax = ax, r.pe = pe, r.a1 = a1, r.a2 = a2, r.s1 = s1, r.s2 = s2;
     r.soft = soft, r.gamma = soft ? gamma : 0.0f, r.bias = soft ? bias : 0.0f, r.angle = angle;
     r.lower = lower, r.upper = upper;
