@@ -504,19 +504,23 @@ __device__ __noinline__ void evaluate(const DevModel &m, int fa, int fb, Xf xfa,
 }
 
 // b2Contact::Update's manifold write: impulses carried over by feature key, touching flag (pairs.py:55-83)
-__device__ __forceinline__ bool apply_manifold(W &w, int s, const Man &mn) {
-    int old_n = w.count[s];
+__device__ __forceinline__ bool apply_manifold(W &w, int s, const Man &mn_) {
+    const Man mn = mn_;  // every load first (the manifold, then the slot's old state), the stores last
+    const int old_n = w.count[s], pid0 = w.point_id[2 * s], pid1 = w.point_id[2 * s + 1];
+    const float on0 = w.normal_impulse[2 * s], on1 = w.normal_impulse[2 * s + 1];
+    const float ot0 = w.tangent_impulse[2 * s], ot1 = w.tangent_impulse[2 * s + 1];
+    const bool was_touching = w.touching[s];
     float ni[2], ti[2];
     for (int i = 0; i < 2; ++i) {
         int nid = mn.id[i];
-        bool m0 = old_n > 0 && w.point_id[2 * s] == nid;
-        bool m1 = old_n > 1 && w.point_id[2 * s + 1] == nid && !m0;
-        ni[i] = m0 ? w.normal_impulse[2 * s] : m1 ? w.normal_impulse[2 * s + 1] : 0.0f;
-        ti[i] = m0 ? w.tangent_impulse[2 * s] : m1 ? w.tangent_impulse[2 * s + 1] : 0.0f;
+        bool m0 = old_n > 0 && pid0 == nid;
+        bool m1 = old_n > 1 && pid1 == nid && !m0;
+        ni[i] = m0 ? on0 : m1 ? on1 : 0.0f;
+        ti[i] = m0 ? ot0 : m1 ? ot1 : 0.0f;
         if (!(i < mn.count)) ni[i] = ti[i] = 0.0f;
     }
     bool touching = mn.count > 0;
-    bool flip = touching != (bool)w.touching[s];
+    bool flip = touching != was_touching;
     w.touching[s] = touching;
     w.count[s] = mn.count;
     if (mn.count > 0) {

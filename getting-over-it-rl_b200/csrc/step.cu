@@ -140,18 +140,20 @@ __device__ __forceinline__ void wake_body(W &w, int b) {  // b2Body::SetAwake(tr
 __device__ __forceinline__ void place_contact(Ctx &x, int s, int p, int key) {
     const DevModel &m = x.m;
     W &w = x.w;
-    int fa = m.pair_a[p], fb = m.pair_b[p];
+    const int fa = m.pair_a[p], fb = m.pair_b[p];  // every load first, the stores last
+    const float fra = fixture_friction(m, w, fa), frb = fixture_friction(m, w, fb);
+    const float ra = fixture_restitution(m, w, fa), rb = fixture_restitution(m, w, fb);
+    const int ba = m.fixture_body[fa], bb = m.fixture_body[fb];
     w.pair[s] = p, w.fa[s] = fa, w.fb[s] = fb, w.key[s] = key;
     w.touching[s] = 0, w.count[s] = 0;
     w.normal_impulse[2 * s] = w.normal_impulse[2 * s + 1] = 0.0f;
     w.tangent_impulse[2 * s] = w.tangent_impulse[2 * s + 1] = 0.0f;
     w.point_id[2 * s] = w.point_id[2 * s + 1] = 0;
-    w.friction[s] = sqrtf(fixture_friction(m, w, fa) * fixture_friction(m, w, fb));
-    float ra = fixture_restitution(m, w, fa), rb = fixture_restitution(m, w, fb);
+    w.friction[s] = sqrtf(fra * frb);
     w.restitution[s] = ra > rb ? ra : rb;
     w.tangent_speed[s] = 0.0f;
-    wake_body(w, m.fixture_body[fa]);
-    wake_body(w, m.fixture_body[fb]);
+    wake_body(w, ba);
+    wake_body(w, bb);
 }
 
 // is candidate p a new pair (overlap, ShouldCollide, no contact yet)?
@@ -314,12 +316,17 @@ __device__ void collide(Ctx &x) {
     int *over = ap<int>(x, L.over), *aw = ap<int>(x, L.aw);
     Man *man = ap<Man>(x, L.man);
     int n_live = list_order(x, order, lpos);
-    for (int s = lane; s < C; s += x.wl) {
+    for (int s = lane; s < C; s += x.wl) {  // loads first, stores last
+        const bool live = w.pair[s] >= 0;
+        if (live) {
+            const int fa = w.fa[s], fb = w.fb[s];
+            const int ba = m.fixture_body[fa], bb = m.fixture_body[fb];
+            const Xf xfa = w.bxf(ba), xfb = w.bxf(bb);
+            const int ov = overlap(fixture_fat(m, w, fa), fixture_fat(m, w, fb));
+            evaluate(m, fa, fb, xfa, xfb, x.s.linear_slop, x.s.angular_slop, man[s]);
+            over[s] = ov;
+        }
         active[s] = 0;
-        if (w.pair[s] < 0) continue;
-        int ba = m.fixture_body[w.fa[s]], bb = m.fixture_body[w.fb[s]];
-        over[s] = overlap(fixture_fat(m, w, w.fa[s]), fixture_fat(m, w, w.fb[s]));
-        evaluate(m, w.fa[s], w.fb[s], w.bxf(ba), w.bxf(bb), x.s.linear_slop, x.s.angular_slop, man[s]);
     }
     for (int b = lane; b < B; b += x.wl) aw[b] = w.awake[b];
     gsync(x);
@@ -600,24 +607,27 @@ __device__ IslandWork solve_rows(Ctx &x, float dt, float dt_ratio, const IslandO
     JRow *jr = sw.jr;
     const float h = dt;
     const float gx = w.gravity[0], gy = w.gravity[1];
-    for (int b = lane; b < B; b += x.wl) {  // integrate velocities (step.py:83-100)
-        bool in_isl = bisl[b] >= 0;
-        float gs = w.gravity_scale[b];
-        float ax = gs * gx + w.inv_mass[b] * w.force[2 * b];
-        float ay = gs * gy + w.inv_mass[b] * w.force[2 * b + 1];
-        float vx = w.v[2 * b] + h * ax, vy = w.v[2 * b + 1] + h * ay;
-        float ww = w.w[b] + (h * w.inv_inertia[b]) * w.torque[b];
-        float ld = 1.0f / (1.0f + h * w.linear_damping[b]);
-        float ad = 1.0f / (1.0f + h * w.angular_damping[b]);
+    for (int b = lane; b < B; b += x.wl) {  // integrate velocities (step.py:83-100); loads first, stores last
+        const bool in_isl = bisl[b] >= 0;
+        const float gs = w.gravity_scale[b], im = w.inv_mass[b], fx = w.force[2 * b], fy = w.force[2 * b + 1];
+        const float v0x = w.v[2 * b], v0y = w.v[2 * b + 1], w0 = w.w[b], ii = w.inv_inertia[b], tq = w.torque[b];
+        const float lin_d = w.linear_damping[b], ang_d = w.angular_damping[b];
+        const bool dyn = in_isl && w.type[b] == DYNAMIC;
+        const float cx = w.c[2 * b], cy = w.c[2 * b + 1], ca = w.a[b];
+        float ax = gs * gx + im * fx;
+        float ay = gs * gy + im * fy;
+        float vx = v0x + h * ax, vy = v0y + h * ay;
+        float ww = w0 + (h * ii) * tq;
+        float ld = 1.0f / (1.0f + h * lin_d);
+        float ad = 1.0f / (1.0f + h * ang_d);
         vx = vx * ld, vy = vy * ld, ww = ww * ad;
-        bool dyn = in_isl && w.type[b] == DYNAMIC;
-        bd.vx[b] = dyn ? vx : w.v[2 * b];
-        bd.vy[b] = dyn ? vy : w.v[2 * b + 1];
-        bd.vw[b] = dyn ? ww : w.w[b];
-        bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
-        if (in_isl) w.c0[2 * b] = w.c[2 * b], w.c0[2 * b + 1] = w.c[2 * b + 1], w.a0[b] = w.a[b];
-        Rot q = rot_of(bd.ca[b]);
-        bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = bd.ca[b];
+        const Rot q = rot_of(ca);
+        bd.vx[b] = dyn ? vx : v0x;
+        bd.vy[b] = dyn ? vy : v0y;
+        bd.vw[b] = dyn ? ww : w0;
+        bd.cx[b] = cx, bd.cy[b] = cy, bd.ca[b] = ca;
+        if (in_isl) w.c0[2 * b] = cx, w.c0[2 * b + 1] = cy, w.a0[b] = ca;
+        bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = ca;
     }
     gsync(x);
     const bool warm = s.warm_starting;
@@ -757,11 +767,12 @@ __device__ void solve_finish(Ctx &x, float dt, const IslandWork &sw) {
     int *moved = ap<int>(x, L.moved);
     const int *done = sw.done;
     const Bodies &bd = sw.bd;
-    for (int b = lane; b < B; b += x.wl) {  // write back + SynchronizeTransform (step.py:141-151)
+    for (int b = lane; b < B; b += x.wl) {  // write back + SynchronizeTransform (step.py:141-151); loads first
         if (bisl[b] < 0) continue;
-        w.c[2 * b] = bd.cx[b], w.c[2 * b + 1] = bd.cy[b], w.a[b] = bd.ca[b];
-        w.v[2 * b] = bd.vx[b], w.v[2 * b + 1] = bd.vy[b], w.w[b] = bd.vw[b];
-        Xf xf = xf_from(V2{bd.cx[b], bd.cy[b]}, bd.ca[b], w.blc(b));
+        const float cx = bd.cx[b], cy = bd.cy[b], ca = bd.ca[b], vx = bd.vx[b], vy = bd.vy[b], vw = bd.vw[b];
+        const Xf xf = xf_from(V2{cx, cy}, ca, w.blc(b));
+        w.c[2 * b] = cx, w.c[2 * b + 1] = cy, w.a[b] = ca;
+        w.v[2 * b] = vx, w.v[2 * b + 1] = vy, w.w[b] = vw;
         w.xf_p[2 * b] = xf.p.x, w.xf_p[2 * b + 1] = xf.p.y, w.xf_q[2 * b] = xf.q.c, w.xf_q[2 * b + 1] = xf.q.s;
     }
     gsync(x);
@@ -968,10 +979,13 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     long long ev_t0 = clock64();
 #endif
     for (int b = lane; b < B; b += x.wl) {  // every body advanced to min_alpha, and its transform there
+        float c0x = w.c0[2 * b], c0y = w.c0[2 * b + 1], a0 = w.a0[b], al0 = w.t_alpha0[b];
+        const float cx = w.c[2 * b], cy = w.c[2 * b + 1], ca = w.a[b];
+        const V2 lc = w.blc(b);
+        sweep_advance(c0x, c0y, a0, al0, cx, cy, ca, min_alpha);
+        const Xf xf = xf_from(V2{c0x, c0y}, a0, lc);
         float *d = adv + 8 * b;
-        d[0] = w.c0[2 * b], d[1] = w.c0[2 * b + 1], d[2] = w.a0[b], d[3] = w.t_alpha0[b];
-        sweep_advance(d[0], d[1], d[2], d[3], w.c[2 * b], w.c[2 * b + 1], w.a[b], min_alpha);
-        Xf xf = xf_from(V2{d[0], d[1]}, d[2], w.blc(b));
+        d[0] = c0x, d[1] = c0y, d[2] = a0, d[3] = al0;
         d[4] = xf.p.x, d[5] = xf.p.y, d[6] = xf.q.c, d[7] = xf.q.s;
         flip_b[b] = in_other[b] = touched[b] = newbody[b] = 0;
     }
@@ -1126,10 +1140,12 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
     // island's rows in the warp's shared rows region when they fit
     if (x.rows && n_isl <= L.sm_vc_cap) vc = reinterpret_cast<VCRow *>(x.rows + L.sm_vc);
     for (int b = lane; b < B; b += x.wl) {
-        bd.cx[b] = w.c[2 * b], bd.cy[b] = w.c[2 * b + 1], bd.ca[b] = w.a[b];
-        bd.vx[b] = w.v[2 * b], bd.vy[b] = w.v[2 * b + 1], bd.vw[b] = w.w[b];
-        Rot q = rot_of(bd.ca[b]);
-        bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = bd.ca[b];
+        const float cx = w.c[2 * b], cy = w.c[2 * b + 1], ca = w.a[b];
+        const float vx = w.v[2 * b], vy = w.v[2 * b + 1], vw = w.w[b];
+        const Rot q = rot_of(ca);
+        bd.cx[b] = cx, bd.cy[b] = cy, bd.ca[b] = ca;
+        bd.vx[b] = vx, bd.vy[b] = vy, bd.vw[b] = vw;
+        bd.qc[b] = q.c, bd.qs[b] = q.s, bd.qa[b] = ca;
     }
     gsync(x);
 #ifdef GOIB2D_PHASE_TIMERS
