@@ -1379,8 +1379,9 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
 
 // The whole step in one launch (see part_kernels for the batches that run part kernels instead): one block per SM
 // where the batch allows,
-// the block's threads meeting between phases (step_sync: collide | islands | rows | sweeps | write back and sleep |
-// broadphase | TOI), and WPW worlds per warp.
+// the block's threads meeting between phases (step_sync: collide | islands and rows | sweeps | write back, sleep and
+// broadphase | TOI; two more barriers, between islands and rows and before the broadphase, measured 1 % slower),
+// and WPW worlds per warp.
 // - Phase barriers: worlds are independent, so a phase's tail is the slowest of the block's worlds rather than of
 //   the whole batch, and every warp of an SM runs the same phase at the same time (the step's code does not fit the
 //   SM's instruction cache; warps spread over all phases thrash it).
@@ -1428,7 +1429,6 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
         isl = find_islands(x);
         GB_PHASE(x, 2);
     }
-    step_sync();
     IslandWork sw{};
     if (active) sw = solve_rows(x, dt, *w.inv_dt0 * dt, isl);
     step_sync();
@@ -1441,7 +1441,6 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
         GB_PHASE(x, 5);
         solve_finish(x, dt, sw);
     }
-    step_sync();
     if (active) broadphase(x);
     step_sync();
     if (active) {
