@@ -30,18 +30,28 @@ __global__ void __launch_bounds__(128) goib2d_reset_kernel(const __grid_constant
     if (lane == 0 && p.reset_count) p.reset_count[w] += 1;
 }
 
-// One thread per (world, observed body): position, angle, linear and angular velocity.
-__global__ void goib2d_observe_kernel(const __grid_constant__ EnvParams p) {
-    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= p.n_worlds * p.n_obs) return;
-    const int64_t w = t / p.n_obs;
-    const int b = p.obs_body[t % p.n_obs];
-    const float *c = (const float *)p.L.p[GOIB2D_B_C] + w * 2 * p.B;
-    const float *a = (const float *)p.L.p[GOIB2D_B_A] + w * p.B;
-    const float *v = (const float *)p.L.p[GOIB2D_B_V] + w * 2 * p.B;
-    const float *av = (const float *)p.L.p[GOIB2D_B_W] + w * p.B;
-    float *o = p.out + t * 6;
-    o[0] = c[2 * b], o[1] = c[2 * b + 1], o[2] = a[b], o[3] = v[2 * b], o[4] = v[2 * b + 1], o[5] = av[b];
+// One thread per (world, observed body): position, angle, linear and angular velocity. A block's rows are gathered
+// in shared memory and written out as consecutive floats (each warp store a whole 128-byte line), which matters
+// when out is pinned host memory written over the bus.
+constexpr int OBS_THREADS = 256;
+__global__ void __launch_bounds__(OBS_THREADS) goib2d_observe_kernel(const __grid_constant__ EnvParams p) {
+    __shared__ float stage[OBS_THREADS * 6];
+    const int64_t total = p.n_worlds * p.n_obs;
+    const int64_t t = (int64_t)blockIdx.x * OBS_THREADS + threadIdx.x;
+    if (t < total) {
+        const int64_t w = t / p.n_obs;
+        const int b = p.obs_body[t % p.n_obs];
+        const float *c = (const float *)p.L.p[GOIB2D_B_C] + w * 2 * p.B;
+        const float *a = (const float *)p.L.p[GOIB2D_B_A] + w * p.B;
+        const float *v = (const float *)p.L.p[GOIB2D_B_V] + w * 2 * p.B;
+        const float *av = (const float *)p.L.p[GOIB2D_B_W] + w * p.B;
+        float *o = stage + threadIdx.x * 6;
+        o[0] = c[2 * b], o[1] = c[2 * b + 1], o[2] = a[b], o[3] = v[2 * b], o[4] = v[2 * b + 1], o[5] = av[b];
+    }
+    __syncthreads();
+    const int64_t base = (int64_t)blockIdx.x * OBS_THREADS * 6, end = total * 6;
+    for (int i = threadIdx.x; i < OBS_THREADS * 6; i += OBS_THREADS)
+        if (base + i < end) p.out[base + i] = stage[i];
 }
 
 // ---- ray casts (b2RayCastInput p1 -> p2, maxFraction 1; each shape's hit fraction along p1 -> p2)
@@ -141,7 +151,7 @@ cudaError_t launch_reset(const EnvParams &p, cudaStream_t s) {
 }
 cudaError_t launch_observe(const EnvParams &p, cudaStream_t s) {
     int64_t n = p.n_worlds * p.n_obs;
-    if (n > 0) goib2d_observe_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);
+    if (n > 0) goib2d_observe_kernel<<<(unsigned)((n + OBS_THREADS - 1) / OBS_THREADS), OBS_THREADS, 0, s>>>(p);
     return cudaGetLastError();
 }
 cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s) {
