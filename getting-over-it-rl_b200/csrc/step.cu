@@ -28,11 +28,11 @@ __device__ unsigned long long g_phase_max[16];  // the longest single warp's tim
 // 0 events, 1 TOI position passes, 2 TOI solves, 3 searches, 4 max events, 5 TOI cycles, 6 outer iterations,
 // 7 push-backs, 8 root-finder steps, 9 GJK iterations, 10-13 TOI outcomes
 __device__ unsigned long long g_counts[16];
-// cycles in the TOI parts (0 sweep_xf, 1 GJK, 2 sep_init, 3 sep_find_min) and the island solver's calls (4 contact
-// velocity, 5 joint velocity, 6 contact position, 7 joint position; their counts at 8-11)
+// cycles in the TOI parts (0 sweep_xf, 1 GJK, 2 sep_init, 3 sep_find_min), in a TOI event's island solve (4 position
+// rows, 5 position passes, 6 velocity rows, 7 velocity passes; 11 its contacts) and in a TOI event (12 the walk,
+// 13 the island solve, 14 synchronize and FindNewContacts)
 __device__ unsigned long long g_toi_cycles[16];
-// per-warp cycles in a part kernel (sum, warps, max): 0-2 TOI without events, 3-5 TOI with events, 6-8 solve,
-// 9-11 collide
+// per-world cycles in a part (sum, worlds, max): 0-2 TOI without events, 3-5 TOI with events, 9-11 collide
 __device__ unsigned long long g_span[16];
 }  // namespace gb
 #define GB_SPAN(x, k, ev)                                                                   \
