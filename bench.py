@@ -246,7 +246,7 @@ def main():
     value = world_size * n * K / (ms_max / 1e3)
 
     # e2e through the public API with host buffers: per step, this step's actions read from pinned host memory by
-    # the step's first kernel (mapped memory: the host->device transfer, no separate copy), the step, and the pot's
+    # the step kernel (mapped memory: the host->device transfer, no separate copy), the step, and the pot's
     # observation (position, angle, velocities) written by goib2d_observe into pinned host memory; the host
     # synchronises at the end of the timed region before reading it
     Ke = max(3, min(K, 20))
