@@ -31,6 +31,7 @@ def test_library_exports_every_declared_symbol():
     lib = native.load()
     assert lib.goib2d_version() == 2
     assert lib.goib2d_kernels_per_step(None, 4096) < 0  # a null model is an error, not a count
+    assert lib.goib2d_set_step_mode(None, 1) < 0 and b"null" in lib.goib2d_last_error()
     for leaf in range(71):  # the leaf table agrees with the Python one (no device needed)
         B, rows, J, C = 5, 7, 3, 11
         spec = native.leaf_spec(B, rows, J, C)[leaf]
