@@ -135,6 +135,20 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+def workload_config(args, sc, model, n_bodies, n, world_size):
+    """The `config` object of both arms' lines: the workload BASELINE.json names, n worlds per GPU (the reference
+    arm times a bounded sample of it, described in its cpu_baseline.sample)."""
+    from goib2d import configs
+    resets = args.config.startswith("c4")
+    return {"workload": WORKLOADS.get(args.config, sc.name),
+            "reset_on_fall": "pot below y = -5 -> the world's seeded initial state" if resets else None,
+            "worlds_per_gpu": n, "global_worlds": n * world_size, "dt": float(configs.DT),
+            "iterations": "8/3", "continuous_physics": True, "contact_capacity": sc.capacity,
+            "bodies": int(n_bodies), "fixtures": int(model.fixture_body.shape[0]),
+            "candidate_pairs": int(model.pair_a.shape[0]), "parallelism": f"worlds sharded x{world_size}",
+            "l2": "flushed between timed steps (256 MiB write), per-step CUDA events summed"}
+
+
 def cpu_baseline(sc, model, host, n_sample, steps, threads=0):
     """The parity oracle on the host cores over a bounded sample (the first n_sample worlds, `steps` steps)."""
     import oracle_lib
@@ -171,8 +185,8 @@ def run_reference(args, rank):
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * n / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded, goib2d/configs.py)", "impl": "reference",
-            "config": {"workload": WORKLOADS.get(args.config, sc.name),
-                       "worlds": n, "dt": float(configs.DT), "iterations": "8/3", "continuous_physics": True},
+            "config": workload_config(args, sc, model, host.bodies.type.shape[1],
+                                      args.worlds or configs.DEFAULT_N[args.config], args.gpus),
             "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's JAX engine is not installed here; its algorithm runs as the bit-identical C++ "
                     "parity oracle (oracle/), all host threads"}
@@ -287,13 +301,7 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": K, "warmup": Wm,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded worlds, goib2d/configs.py)",
-            "config": {"workload": WORKLOADS.get(args.config, sc.name),
-                       "reset_on_fall": "pot below y = -5 -> the world's seeded initial state" if resets else None,
-                       "worlds_per_gpu": n, "global_worlds": n * world_size, "dt": float(configs.DT),
-                       "iterations": "8/3", "continuous_physics": True, "contact_capacity": sc.capacity,
-                       "bodies": int(host.bodies.type.shape[1]), "fixtures": int(model.fixture_body.shape[0]),
-                       "candidate_pairs": int(model.pair_a.shape[0]), "parallelism": f"worlds sharded x{world_size}",
-                       "l2": "flushed between timed steps (256 MiB write), per-step CUDA events summed"},
+            "config": workload_config(args, sc, model, host.bodies.type.shape[1], n, world_size),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
