@@ -39,7 +39,7 @@ def parse():
     ap.add_argument("--worlds", type=int, default=None, help="worlds per GPU (default: the config's N)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--cpu-sample-worlds", type=int, default=256)
+    ap.add_argument("--cpu-sample-worlds", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -149,42 +149,59 @@ def workload_config(args, sc, model, n_bodies, n, world_size):
             "l2": "flushed between timed steps (256 MiB write), per-step CUDA events summed"}
 
 
-def cpu_baseline(sc, model, host, n_sample, steps, threads=0):
-    """The parity oracle on the host cores over a bounded sample (the first n_sample worlds, `steps` steps)."""
+# The bounded CPU sample, the same in both arms: the workload's first worlds (CPU_SAMPLE_WORLDS, fewer for c2's
+# 256-body worlds), stepped until CPU_SAMPLE_SECONDS have passed or CPU_SAMPLE_MAX_STEPS steps are done.
+CPU_SAMPLE_WORLDS = {"c2": 128}
+CPU_SAMPLE_SECONDS, CPU_SAMPLE_MAX_STEPS = 10.0, 200
+
+
+def cpu_sample_worlds(args, n):
+    want = args.cpu_sample_worlds or CPU_SAMPLE_WORLDS.get(args.config[:2], 1024)
+    return max(1, min(want, n))
+
+
+def cpu_baseline(sc, model, host, n_sample, threads=0, warmup=True):
+    """The parity oracle on the host cores over a bounded sample: the first n_sample worlds, stepped (each step with
+    its own actions) until CPU_SAMPLE_SECONDS have passed or CPU_SAMPLE_MAX_STEPS steps are done. Both arms call
+    this with the same sample, so their CPU figures are the same measurement."""
     import oracle_lib
     from goib2d import configs
     from goib2d.world import map_state
     sample = map_state(lambda x: np.ascontiguousarray(np.asarray(x)[:n_sample]), host)
     lib = oracle_lib.load(build=False)
     threads = threads or lib.oracle_max_threads()
-    acts = actions_for(n_sample, steps, 0)
+    acts = actions_for(n_sample, CPU_SAMPLE_MAX_STEPS, 0)
+    if warmup:  # one untimed step of a copy (thread pool start-up, first touches)
+        warm = map_state(lambda x: np.array(x, copy=True), sample)
+        oracle_lib.step(model, warm, sc.settings, configs.DT, 1, threads=threads, actions=acts[0],
+                        action_joints=sc.action_joints, action_scale=sc.action_scale)
     t0 = time.perf_counter()
-    st = sample
-    for k in range(steps):
-        st = oracle_lib.step(model, st, sc.settings, configs.DT, 1, threads=threads, actions=acts[k],
+    st, steps = sample, 0
+    while steps < CPU_SAMPLE_MAX_STEPS and (steps < 2 or time.perf_counter() - t0 < CPU_SAMPLE_SECONDS):
+        st = oracle_lib.step(model, st, sc.settings, configs.DT, 1, threads=threads, actions=acts[steps],
                              action_joints=sc.action_joints, action_scale=sc.action_scale)
+        steps += 1
     dt = time.perf_counter() - t0
-    return {"value": n_sample * steps / dt, "unit": UNIT, "cores": int(threads), "kind": "port",
-            "sample": f"{n_sample} worlds x {steps} steps of {sc.name} (the first worlds of the workload)"}
+    return {"value": n_sample * steps / dt, "unit": UNIT, "cores": int(threads), "kind": "port", "steps": steps,
+            "seconds": dt, "sample": f"{n_sample} worlds x {steps} steps of {sc.name} (the first worlds of the "
+                                     f"workload; stepped for {CPU_SAMPLE_SECONDS:.0f} s or {CPU_SAMPLE_MAX_STEPS} steps)"}
 
 
 def run_reference(args, rank):
-    """--impl reference: rank 0 times the oracle (the reference's algorithm, C++) on the host cores."""
+    """--impl reference: rank 0 times the oracle (the reference's algorithm, C++) on the host cores. This process
+    loads no CUDA library of this repository: the batch's candidate list is built by the host scan."""
     if rank != 0:
         return
     import oracle_lib
     from goib2d import configs
-    n = args.cpu_sample_worlds
-    sc, model, host = configs.batch(args.config, n, args.seed)
+    n = cpu_sample_worlds(args, args.worlds or configs.DEFAULT_N[args.config])
+    sc, model, host = configs.batch(args.config, n, args.seed, device_pairs=False)
     oracle_lib.load(build=not (ROOT / "oracle" / "liboracle_goib2d.so").exists())
-    steps = max(1, min(args.steps, 20))
-    for _ in range(min(args.warmup, 1)):
-        cpu_baseline(sc, model, host, min(n, 32), 1)
-    cb = cpu_baseline(sc, model, host, n, steps)
+    cb = cpu_baseline(sc, model, host, n)
     v = cb["value"]
-    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * n / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded, goib2d/configs.py)", "impl": "reference",
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": cb["steps"],
+            "warmup": args.warmup, "ms_per_step": 1000.0 * n / v, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, goib2d/configs.py)", "impl": "reference",
             "config": workload_config(args, sc, model, host.bodies.type.shape[1],
                                       args.worlds or configs.DEFAULT_N[args.config], args.gpus),
             "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -296,7 +313,7 @@ def main():
             traffic = td.get("dram_bytes_per_world_step", 0) * n
         cpu = None
         if not args.no_cpu_baseline:
-            cpu = cpu_baseline(sc, model, host, min(args.cpu_sample_worlds, n), 5)
+            cpu = cpu_baseline(sc, model, host, cpu_sample_worlds(args, n))
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": K, "warmup": Wm,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

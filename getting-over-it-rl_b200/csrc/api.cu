@@ -15,6 +15,7 @@
 namespace gb {
 cudaError_t launch_steps(StepParams p, cudaStream_t stream);  // step.cu
 int kernels_per_step(int64_t n_worlds, int n_joints);         // step.cu
+int64_t launches_per_call(int64_t n_worlds, int n_joints, int n_steps);  // step.cu
 cudaError_t launch_reset(const EnvParams &p, cudaStream_t s);    // env.cuh (compiled in step.cu)
 cudaError_t launch_observe(const EnvParams &p, cudaStream_t s);  // env.cuh
 cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s);  // env.cuh
@@ -255,6 +256,12 @@ int goib2d_kernels_per_step(const goib2d_model *model, int64_t n_worlds) {
     return gb::kernels_per_step(n_worlds, model->full.J);
 }
 
+int64_t goib2d_launches(const goib2d_model *model, int64_t n_worlds, int32_t n_steps) {
+    if (!model) return fail(GOIB2D_EINVAL, "null argument");
+    if (n_worlds < 0 || n_steps < 0) return fail(GOIB2D_EINVAL, "negative size");
+    return gb::launches_per_call(n_worlds, model->full.J, n_steps);
+}
+
 const char *goib2d_last_error(void) { return g_err.c_str(); }
 
 int goib2d_leaf_dtype(int leaf) {
@@ -423,10 +430,12 @@ int goib2d_model_set_action_map(goib2d_model *m, int32_t n, const int32_t *joint
     return 0;
 }
 
-int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, int32_t rows, int64_t n_worlds,
-                int32_t n_steps, void *const *leaves, const float *actions, void *stream) {
+int goib2d_step_seq(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, int32_t rows, int64_t n_worlds,
+                    int32_t n_steps, void *const *leaves, const float *actions, int64_t action_step_stride,
+                    void *stream) {
     if (!m || !s || !leaves) return fail(GOIB2D_EINVAL, "null argument");
     if (C < 0 || n_worlds < 0 || n_steps < 0) return fail(GOIB2D_EINVAL, "negative size");
+    if (action_step_stride < 0) return fail(GOIB2D_EINVAL, "negative action step stride");
     if (s->velocity_iterations < 0 || s->position_iterations < 0) return fail(GOIB2D_EINVAL, "negative iterations");
     std::lock_guard<std::mutex> lk(m->mu);
     int dev = 0;
@@ -480,11 +489,16 @@ int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, 
         int arc = device_view(actions, &a);
         if (arc) return arc;
         p.actions = (const float *)a, p.n_action = m->n_action, p.action_joint = m->action_joint;
-        p.action_scale = m->action_scale;
+        p.action_scale = m->action_scale, p.action_stride = action_step_stride;
     }
     if ((n_worlds + 3) / 4 > 0x7fffffff) return fail(GOIB2D_ELIMIT, "too many worlds");
     CUDA_TRY(gb::launch_steps(p, (cudaStream_t)stream));
     return 0;
+}
+
+int goib2d_step(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, int32_t rows, int64_t n_worlds,
+                int32_t n_steps, void *const *leaves, const float *actions, void *stream) {
+    return goib2d_step_seq(m, s, dt, C, rows, n_worlds, n_steps, leaves, actions, 0, stream);
 }
 
 int goib2d_set_step_mode(goib2d_model *m, int32_t mode) {
@@ -608,7 +622,9 @@ int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int
     p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
     p.step_mode = m->step_mode;
     p.scratch = scratch;
-    p.status = nullptr;  // no per-world status words (their buffer would need an allocation)
+    p.status = nullptr;  // no per-world status words (their buffer would need an allocation) ...
+    p.events = nullptr;  // ... and no event log: neither reports an earlier call's results as this one's
+    m->status_n = 0, m->event_n = 0;
     if (actions && m->n_action > 0) {
         const void *a = nullptr;
         int arc = device_view(actions, &a);

@@ -126,10 +126,11 @@ struct StepParams {
     int64_t n_worlds;
     int n_steps;
     int step_mode;   // below 16384 worlds: 0 chosen per batch, 1 one world per warp, 2 two worlds per warp
-    int step;        // index of the step a launch belongs to
+    int step;        // index of the step a per-step launch belongs to (the one-launch step runs all n_steps)
     int64_t world0;  // a launch covers worlds world0 .. world_end - 1
     int64_t world_end;
-    const float *actions;
+    const float *actions;   // step k of a launch reads actions + k * action_stride (stride 0: the same every step)
+    int64_t action_stride;
     int n_action;
     const int32_t *action_joint;
     const float *action_scale;

@@ -9,6 +9,7 @@
 // exactly the reference's order (goi_jax/box2d/step.py, island.py, pairs.py, toi.py), so results are bit-identical
 // to it. Per-world working arrays live in a scratch arena (L1/L2-resident), laid out by scratch_layout().
 #include <cstdio>
+#include <mutex>
 
 // Optional per-phase cycle counters for profiling builds (-DGOIB2D_PHASE_TIMERS): lane 0 of every warp adds the
 // clock64 cycles spent in each phase; goib2d_debug_phase_cycles() reads them. Compiled out otherwise.
@@ -88,6 +89,7 @@ struct Ctx {
     char *rows;  // this world's shared constraint rows (solve and TOI phases), or null
     int lane;    // the thread's lane in the world's group, 0 .. wl - 1
     int status;
+    int step;      // the step of the call being run (0 .. n_steps - 1)
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
     int64_t world;
     unsigned gmask;  // the world's lanes in the warp: all 32, or one half (the step kernel: two worlds per warp)
@@ -1308,9 +1310,10 @@ __device__ __forceinline__ void run_part(Ctx &x) {
     const long long gb_span0_ = clock64();
 #endif
     if (PART == 0) {
-        if (p.actions)  // action channels -> joint motor speeds
-            for (int c = x.lane; c < p.n_action; c += x.wl)
-                w.motor_speed[p.action_joint[c]] = p.action_scale[c] * p.actions[x.world * p.n_action + c];
+        if (p.actions) {  // action channels -> joint motor speeds, from this step's row of the actions
+            const float *a = p.actions + x.step * p.action_stride + x.world * p.n_action;
+            for (int c = x.lane; c < p.n_action; c += x.wl) w.motor_speed[p.action_joint[c]] = p.action_scale[c] * a[c];
+        }
         gsync(x);
         GB_PHASE(x, 11);
         if (*w.new_fixture) find_new_contacts(x);
@@ -1334,7 +1337,7 @@ __device__ __forceinline__ void run_part(Ctx &x) {
         if (x.lane == 0 && dt > 0) *w.inv_dt0 = 1.0f / dt;
         if (x.s.auto_clear_forces)
             for (int b = x.lane; b < w.B; b += x.wl) w.force[2 * b] = w.force[2 * b + 1] = 0.0f, w.torque[b] = 0.0f;
-        if (p.step == p.n_steps - 1) {
+        if (x.step == p.n_steps - 1) {
             bool bad = false;  // non-finite body state
             for (int b = x.lane; b < w.B; b += x.wl)
                 bad = bad || !isfinite(w.c[2 * b]) || !isfinite(w.c[2 * b + 1]) || !isfinite(w.a[b]) ||
@@ -1372,19 +1375,25 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
     char *mine = dyn_smem + warp * region;
     Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
-          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, clock64(), world, FULL, 0, 32};
+          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, p.step, clock64(), world, FULL, 0, 32};
     run_part<PART>(x);
     put_status(x, PART == 0 && p.step == 0);
 }
 
-// The whole step in one launch (see part_kernels for the batches that run part kernels instead): one block per SM
-// where the batch allows,
-// the block's threads meeting between phases (step_sync: collide | islands and rows | sweeps | write back, sleep and
-// broadphase | TOI; two more barriers, between islands and rows and before the broadphase, measured 1 % slower),
+// Every step of a call in one launch (see part_kernels for the batches that run part kernels instead): one block
+// per SM where the batch allows, each block running all p.n_steps steps of its worlds before it exits, the block's
+// threads meeting between the phases of a step (step_sync: collide | islands and rows | sweeps | write back, sleep
+// and broadphase | TOI; two more barriers, between islands and rows and before the broadphase, measured 1 % slower),
 // and WPW worlds per warp.
-// - Phase barriers: worlds are independent, so a phase's tail is the slowest of the block's worlds rather than of
-//   the whole batch, and every warp of an SM runs the same phase at the same time (the step's code does not fit the
-//   SM's instruction cache; warps spread over all phases thrash it).
+// - Persistent over the steps: worlds are independent, so a block runs its worlds' steps back to back with no
+//   grid-wide boundary between them. A step no longer waits for the slowest block of the batch (a TOI event chain in
+//   one of its worlds), only the block's own phases do; the per-world binding, shared-memory regions and the State
+//   rows and arena lines the block's worlds touch stay on the SM and in L2 across the steps, and per-step launch gaps
+//   vanish. There is no barrier between a step's TOI phase and the next step's collide: a world without a TOI event
+//   starts its next step while another world of the block finishes its event chain.
+// - Phase barriers: a phase's tail is the slowest of the block's worlds rather than of the whole batch, and every
+//   warp of an SM runs the same phase at the same time (the step's code does not fit the SM's instruction cache;
+//   warps spread over all phases thrash it).
 // - WPW = 2 (goib2d_step_pair_kernel), one world per half-warp: the order-dependent sections run on each world's
 //   lane 0, so lanes 0 and 16 run two worlds' sequential work in the same instructions where their control flow
 //   agrees - half the issue slots per world, which pays when an SM holds many small worlds - and 16 warps per SM
@@ -1418,34 +1427,36 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
     char *rows = hot && p.lay.rows_bytes ? hot + p.lay.hot_end : nullptr;
     if (active && (lane32 & (WL - 1)) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
-    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, nullptr, lane32 & (WL - 1), 0, clock64(), world,
+    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, clock64(), world,
           WPW == 2 ? 0xffffu << (16 * half) : FULL, WL * half, WL};
     const float dt = p.dt;
-    if (active) run_part<0>(x);
-    step_sync();
-    x.rows = rows;
-    IslandOut isl{0, 0, 0};
-    if (active) {
-        isl = find_islands(x);
-        GB_PHASE(x, 2);
-    }
-    IslandWork sw{};
-    if (active) sw = solve_rows(x, dt, *w.inv_dt0 * dt, isl);
-    step_sync();
-    if (active && x.lane == 0)
-        solve_constraints(p, world, sw,
-                          {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
-                           ap<int>(x, p.lay.jisl)});
-    step_sync();
-    if (active) {
-        GB_PHASE(x, 5);
-        solve_finish(x, dt, sw);
-    }
-    if (active) broadphase(x);
-    step_sync();
-    if (active) {
-        run_part<5>(x);
-        put_status(x, p.step == 0);
+    for (int k = 0; k < p.n_steps; ++k) {
+        x.step = k;
+        if (active) run_part<0>(x);
+        step_sync();
+        IslandOut isl{0, 0, 0};
+        if (active) {
+            isl = find_islands(x);
+            GB_PHASE(x, 2);
+        }
+        IslandWork sw{};
+        if (active) sw = solve_rows(x, dt, *w.inv_dt0 * dt, isl);
+        step_sync();
+        if (active && x.lane == 0)
+            solve_constraints(p, world, sw,
+                              {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
+                               ap<int>(x, p.lay.jisl)});
+        step_sync();
+        if (active) {
+            GB_PHASE(x, 5);
+            solve_finish(x, dt, sw);
+        }
+        if (active) broadphase(x);
+        step_sync();
+        if (active) {
+            run_part<5>(x);
+            put_status(x, k == 0);
+        }
     }
 }
 
@@ -1510,9 +1521,14 @@ constexpr int THREAD_SWEEPS_MIN_JOINTS = 8;
 bool part_kernels(int64_t n_worlds, int n_joints) {
     return n_worlds >= THREAD_SWEEPS_MIN_WORLDS && n_joints >= THREAD_SWEEPS_MIN_JOINTS;
 }
-// p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: per step one goib2d_step(_pair)_kernel,
-// or the collide part, the solve part in pieces (rows / thread sweeps / finish / broadphase) and the TOI part
+// p.n_steps steps of worlds world0 .. world_end - 1, in order on one stream: one goib2d_step(_pair)_kernel running
+// every step, or per step the collide part, the solve part in pieces (rows / thread sweeps / finish / broadphase)
+// and the TOI part
 int kernels_per_step(int64_t n_worlds, int n_joints) { return part_kernels(n_worlds, n_joints) ? 6 : 1; }
+int64_t launches_per_call(int64_t n_worlds, int n_joints, int n_steps) {
+    if (n_worlds <= 0 || n_steps <= 0) return 0;
+    return part_kernels(n_worlds, n_joints) ? 6 * (int64_t)n_steps : 1;
+}
 // Two worlds per warp (goib2d_step_pair_kernel) for crowded batches of small worlds: more than PAIR_MIN_PER_SM
 // worlds per SM (fewer leave the SM's issue slots free, and a pair only adds the two worlds' divergence) and at most
 // PAIR_MAX_CONTACTS contact slots (worlds with more grow islands and TOI event chains that differ between the two
@@ -1526,7 +1542,7 @@ bool step_pairs(int64_t n_worlds, int sms, int contact_capacity) {
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     p.world0 = 0, p.world_end = p.n_worlds;
     const int64_t n = p.n_worlds;
-    if (!part_kernels(n, p.m.J)) {  // one launch per step
+    if (!part_kernels(n, p.m.J)) {  // one launch for every step of the call
         int dev = 0, sms = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1540,18 +1556,21 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
         warps = warps > fit ? fit : warps;
         const size_t smem = (size_t)wpw * warps * region;
         auto kern = pair ? goib2d_step_pair_kernel : goib2d_step_kernel;
-        static int smem_set[2][64];  // the dynamic shared memory limit set per kernel and device
-        if (dev < 64 && smem > 48 * 1024 && (size_t)smem_set[pair][dev] < smem) {
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-            smem_set[pair][dev] = (int)smem;
+        // the dynamic shared memory limit set per kernel and device (host threads may launch concurrently)
+        static std::mutex smem_mu;
+        static int smem_set[2][64];
+        if (smem > 48 * 1024) {
+            std::lock_guard<std::mutex> lk(smem_mu);
+            if (dev >= 64 || (size_t)smem_set[pair][dev] < smem) {
+                cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                if (e != cudaSuccess) return e;
+                if (dev < 64) smem_set[pair][dev] = (int)smem;
+            }
         }
         const int per_block = wpw * warps;
         const unsigned sblocks = (unsigned)((n + per_block - 1) / per_block);
-        for (int k = 0; k < p.n_steps; ++k) {
-            p.step = k;
-            kern<<<sblocks, 32 * warps, smem, stream>>>(p);
-        }
+        p.step = 0;
+        kern<<<sblocks, 32 * warps, smem, stream>>>(p);  // every step in this one launch (whole_step)
         return cudaGetLastError();
     }
     const int wpb = 4;  // worlds (warps) per block

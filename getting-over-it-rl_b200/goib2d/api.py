@@ -85,24 +85,38 @@ class Engine:
         return bound
 
     def step_(self, state, settings, dt, n_steps=1, actions=None, stream=None):
-        """Step every world of a batched device State n_steps times, in place; returns the State."""
+        """Step every world of a batched device State n_steps times, in place; returns the State. actions: None, a
+        float32 (N, n_action) tensor used before every step, or (n_steps, N, n_action) with one row per step
+        (goib2d_step_seq); on the device or in pinned host memory. All n_steps steps run in one launch where the
+        batch takes the one-kernel step (launches())."""
         n, C_, rows, device, ptrs = self._bind(state)
         if self._settings is None or self._settings[0] is not settings:
             self._settings = (settings, settings_struct(settings))
         ss = self._settings[1]
-        act = None
+        act, stride = None, 0
         if actions is not None:
             if not (isinstance(actions, torch.Tensor) and actions.dtype == torch.float32 and
                     (actions.is_cuda or actions.is_pinned())):
-                raise TypeError("actions must be a float32 tensor (N, n_action) on the device or in pinned host memory")
-            if tuple(actions.shape) != (n, self.n_action) or not actions.is_contiguous():
-                raise ValueError(f"actions must be contiguous ({n}, {self.n_action})")
+                raise TypeError("actions must be a float32 tensor on the device or in pinned host memory")
+            per_step = (int(n_steps), n, self.n_action)
+            if tuple(actions.shape) == per_step:
+                stride = n * self.n_action
+            elif tuple(actions.shape) != (n, self.n_action):
+                raise ValueError(f"actions must be ({n}, {self.n_action}) or {per_step}")
+            if not actions.is_contiguous():
+                raise ValueError("actions must be contiguous")
             act = actions.data_ptr()
         if stream is None:
             stream = torch.cuda.current_stream(device).cuda_stream
-        native.check(self.lib.goib2d_step(self.handle, C.addressof(ss), C.c_float(float(dt)), C_, rows, n,
-                                          int(n_steps), ptrs, act, stream))
+        native.check(self.lib.goib2d_step_seq(self.handle, C.addressof(ss), C.c_float(float(dt)), C_, rows, n,
+                                              int(n_steps), ptrs, act, stride, stream))
         return state
+
+    def launches(self, n_worlds, n_steps):
+        """Kernel launches one step_ call of n_steps steps over n_worlds worlds makes (goib2d_launches)."""
+        k = self.lib.goib2d_launches(self.handle, int(n_worlds), int(n_steps))
+        native.check(min(k, 0))
+        return k
 
     # ---- env helpers (goib2d_reset_*, goib2d_observe, goib2d_raycast): device tensors in and out, on the State's
     # current stream; no counterpart in the reference engine.

@@ -197,6 +197,9 @@ def load():
         "goib2d_model_set_action_map": (C.c_int, [vp, C.c_int32, _i, _f]),
         "goib2d_step": (C.c_int, [vp, vp, C.c_float, C.c_int32, C.c_int32, C.c_int64, C.c_int32,
                                   C.POINTER(vp), vp, vp]),
+        "goib2d_step_seq": (C.c_int, [vp, vp, C.c_float, C.c_int32, C.c_int32, C.c_int64, C.c_int32,
+                                      C.POINTER(vp), vp, C.c_int64, vp]),
+        "goib2d_launches": (C.c_int64, [vp, C.c_int64, C.c_int32]),
         "goib2d_status": (C.c_int, [vp, C.POINTER(vp), C.POINTER(C.c_int64)]),
         "goib2d_status_copy": (C.c_int, [vp, _i, C.c_int64]),
         "goib2d_step_noalloc": (C.c_int, [vp, vp, C.c_float, C.c_int32, C.c_int32, C.c_int64, C.c_int32,

@@ -129,6 +129,16 @@ int goib2d_step(goib2d_model *model, const goib2d_settings *settings, float dt, 
                 int32_t fixture_rows, int64_t n_worlds, int32_t n_steps, void *const *leaves, const float *actions,
                 void *stream);
 
+/* goib2d_step with its own row of actions for every step: step k of the call reads the float32 [n_worlds][n_action]
+ * row at actions + k * action_step_stride (a [n_steps][n_worlds][n_action] buffer has stride n_worlds * n_action;
+ * stride 0 reuses one row for every step, which is goib2d_step). Same memory rules for actions as goib2d_step.
+ * The K steps of a call run in one persistent launch (goib2d_launches): each block steps its worlds K times with
+ * no grid-wide boundary between the steps. Replaces a Python loop of K reference step() calls under jax.jit
+ * (goi_jax/box2d/step.py:28-47 per step); the reference has no multi-step entry. */
+int goib2d_step_seq(goib2d_model *model, const goib2d_settings *settings, float dt, int32_t contact_capacity,
+                    int32_t fixture_rows, int64_t n_worlds, int32_t n_steps, void *const *leaves,
+                    const float *actions, int64_t action_step_stride, void *stream);
+
 /* Per-world status words of the last goib2d_step on this model (device int32 [n_worlds]; bit 0 contact table
  * overflow in this step, bit 1 non-finite body state, bit 2 an iteration cap was reached, bit 3 a capacity of the
  * kernels' on-chip tables was exceeded). Valid until the next goib2d_step with this model. */
@@ -137,11 +147,15 @@ int goib2d_status(goib2d_model *model, const int32_t **device_status, int64_t *n
 /* The same status words copied to host memory (n <= the last step's n_worlds); synchronises the device. */
 int goib2d_status_copy(goib2d_model *model, int32_t *host_status, int64_t n);
 
-/* Kernel launches one goib2d_step step makes for a batch of n_worlds worlds of this model: 1 (the whole step in one
- * launch), or 6 for batches of 16384 worlds and more of models with 8 joints or more (collide, the solve in four
- * pieces with the constraint sweeps run one world per thread, TOI). For launch accounting and profilers; no
- * counterpart in the reference engine. */
+/* Kernels one step runs for a batch of n_worlds worlds of this model: 1 (the whole step in one kernel, which also
+ * runs every other step of the call), or 6 for batches of 16384 worlds and more of models with 8 joints or more
+ * (collide, the solve in four pieces with the constraint sweeps run one world per thread, TOI; six launches per
+ * step). For launch accounting and profilers; no counterpart in the reference engine. */
 int goib2d_kernels_per_step(const goib2d_model *model, int64_t n_worlds);
+
+/* Kernel launches one goib2d_step / goib2d_step_seq call of n_steps steps makes: 1 when the kernel runs every step
+ * (goib2d_kernels_per_step 1), else 6 * n_steps; 0 for an empty call. No counterpart in the reference engine. */
+int64_t goib2d_launches(const goib2d_model *model, int64_t n_worlds, int32_t n_steps);
 
 /* How the one-launch step (goib2d_kernels_per_step 1) maps worlds to warps: 0 (default) chosen per batch - two
  * worlds per warp for batches of more than 16 worlds per SM with at most 128 contact slots, else one; 1 one world
@@ -223,8 +237,10 @@ int goib2d_events_copy(goib2d_model *model, goib2d_event *host_events, int32_t *
  * bytes one world needs (which grow with bodies, contact slots, joints and candidate pairs); larger batches return
  * GOIB2D_ELIMIT with a message and launch nothing. The first call on each device looks the array's address up
  * (cudaGetSymbolAddress): make that call before any stream capture. All calls share the array, so calls that
- * overlap on the GPU race and must be serialised by the caller; earlier contents never affect a call. goib2d_status
- * does not report these calls. */
+ * overlap on the GPU race and must be serialised by the caller; earlier contents never affect a call. It sets no
+ * status words and records no contact events (even with goib2d_set_event_log on): after it, goib2d_status and
+ * goib2d_events report zero worlds until the next goib2d_step. The first call on a device also raises the kernel's
+ * shared-memory limit (cudaFuncSetAttribute, no allocation), another reason to make it before any capture. */
 int goib2d_step_noalloc(goib2d_model *model, const goib2d_settings *settings, float dt, int32_t contact_capacity,
                         int32_t fixture_rows, int64_t n_worlds, int32_t n_steps, void *const *leaves,
                         const float *actions, void *stream);

@@ -121,13 +121,19 @@ def run_job(job):
     names = leaf_names()
     if kind in ("game", "stock", "toi"):
         if kind == "toi":
-            import test_toi
-            maker = test_toi.SCENES[name]
+            import test_toi as scenes
         else:
-            import box2d_scenes
-            maker = box2d_scenes.SCENES[name]
+            import box2d_scenes as scenes
+        # The scene module binds the harness's Twin when it is first imported. Each job runs in a fresh interpreter
+        # (maxtasksperchild=1), so that Twin is this job's Recorder; the assertion keeps a reused worker from
+        # handing one job's default settings to the next.
+        assert scenes.Twin is Recorder, "scene module bound another job's recorder"
+        maker = scenes.SCENES[name]
         Recorder.default_settings = jb.Settings.stock() if kind == "stock" else None
         rec = maker()
+        expect = jb.Settings.stock() if kind == "stock" else jb.Settings.game()
+        if kind != "toi":  # the TOI scenes pass their own settings (continuous physics, the pair rule)
+            assert _settings_dict(rec.settings) == _settings_dict(expect), f"{kind}_{name}: settings differ"
         settings, cap, dt = rec.settings, rec.capacity, jb.GAME_DT
         model, state = rec.defn.build(cap)
         steps = {"game": 240 if name == "late_wake" else 60, "stock": 60, "toi": 40}[kind]
@@ -203,7 +209,7 @@ def main():
     # slowest first
     weight = {"late_wake": 9, "pile": 8, "c2": 7, "c3": 6, "c4": 6, "island_walk": 5, "multi_event": 5}
     jobs.sort(key=lambda j: -weight.get(j[1], 1))
-    with mp.get_context("spawn").Pool(args.jobs) as pool:
+    with mp.get_context("spawn").Pool(args.jobs, maxtasksperchild=1) as pool:
         for msg in pool.imap_unordered(run_job, jobs):
             print(msg, flush=True)
 

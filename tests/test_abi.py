@@ -31,6 +31,8 @@ def test_library_exports_every_declared_symbol():
     lib = native.load()
     assert lib.goib2d_version() == 2
     assert lib.goib2d_kernels_per_step(None, 4096) < 0  # a null model is an error, not a count
+    assert lib.goib2d_launches(None, 4096, 10) < 0
+    assert lib.goib2d_step_seq(None, None, 0.02, 8, 1, 1, 1, None, None, 0, None) == -1
     assert lib.goib2d_set_step_mode(None, 1) < 0 and b"null" in lib.goib2d_last_error()
     for leaf in range(71):  # the leaf table agrees with the Python one (no device needed)
         B, rows, J, C = 5, 7, 3, 11

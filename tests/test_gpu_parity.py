@@ -53,6 +53,8 @@ def _perturbed(g, n, seed, scale):
 
 @pytest.mark.parametrize("name,n,steps", [("stock_pile", 64, 40), ("game_pile", 16, 20), ("game_revolute", 32, 20),
                                           ("game_prismatic", 32, 20), ("game_weld", 32, 20), ("game_misc", 32, 20),
+                                          ("game_limits_mid_run", 32, 30), ("game_polygons_at_angles", 32, 20),
+                                          ("game_polygon_circle", 32, 20), ("game_box_on_ground", 32, 20),
                                           ("toi_island_walk", 32, 15), ("toi_multi_event", 32, 15),
                                           ("toi_poly_angles", 32, 15), ("toi_hammer_chain", 32, 15)])
 def test_gpu_matches_oracle_on_perturbed_batches(api, name, n, steps):
