@@ -5,9 +5,13 @@
 Workload: BASELINE.json configs[1] (the character rig: pot, hub and bullet hammer on a revolute motor and a
 prismatic slide, over a 2000-segment chain level with 60 rocks), polygon-terrain variant (the reference engine has
 no edge/chain shapes), seeded synthetic worlds (goib2d/configs.py), 4096 worlds per GPU, dt 0.02, 8/3 iterations,
-continuous physics on. A step = one b2World::Step of every world (one kernel launch), with per-world actions from a
-disc of radius 2 driving the two joint motors. L2 is flushed (a 256 MiB write) between timed steps; each step is
-timed with CUDA events on the launching stream and the K durations are summed; max over ranks.
+continuous physics on. A bench step = one call of the public step (goib2d_step_seq) running --substeps (default 10)
+b2World::Steps of every world in one persistent launch, each physics step with its own per-world action from a disc
+of radius 2 driving the two joint motors; the value counts world-steps (worlds x physics steps). The first --skip
+(default 100) physics steps of the episode run untimed before the warm-up, so that the timed steps lie in the
+episode's steady part (c1's first ~50 steps, the rig falling onto the level, run faster than the rest). L2 is flushed
+(a 256 MiB write) between timed calls; each call is timed with CUDA events on the launching stream and the K
+durations are summed; max over ranks.
 
 --impl reference: the reference engine's algorithm on the host cores - the parity oracle (oracle/, a C++
 restatement of goi_jax/box2d, bit-identical to it on every golden vector) on all host threads, over a bounded sample
@@ -37,6 +41,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c1", choices=("c0", "c1", "c2", "c3", "c4", "c0e", "c1e", "c3e", "c4e"))
     ap.add_argument("--worlds", type=int, default=None, help="worlds per GPU (default: the config's N)")
+    ap.add_argument("--substeps", type=int, default=10,
+                    help="physics steps per call (goib2d_step_seq: one launch, one row of actions per step)")
+    ap.add_argument("--skip", type=int, default=100, help="untimed physics steps before the warm-up, so that the "
+                                                           "timed steps lie in the episode's steady part")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-sample-worlds", type=int, default=None)
@@ -146,7 +154,8 @@ def workload_config(args, sc, model, n_bodies, n, world_size):
             "iterations": "8/3", "continuous_physics": True, "contact_capacity": sc.capacity,
             "bodies": int(n_bodies), "fixtures": int(model.fixture_body.shape[0]),
             "candidate_pairs": int(model.pair_a.shape[0]), "parallelism": f"worlds sharded x{world_size}",
-            "l2": "flushed between timed steps (256 MiB write), per-step CUDA events summed"}
+            "physics_steps_per_call": args.substeps, "untimed_steps_first": args.skip,
+            "l2": "flushed between timed calls (256 MiB write), per-call CUDA events summed"}
 
 
 # The bounded CPU sample, the same in both arms: the workload's first worlds (CPU_SAMPLE_WORLDS, fewer for c2's
@@ -233,8 +242,6 @@ def main():
     state = api.to_device(host, dev)
     K, Wm = args.steps, args.warmup
     na = len(sc.action_joints)
-    acts_host = actions_for(n, K + Wm, args.seed, first) if na else None
-    acts = torch.from_numpy(acts_host).to(dev) if na else None
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     # BASELINE c4: every world resets to its seeded initial state when the pot (body 1) falls below y = -5
@@ -242,11 +249,21 @@ def main():
     init_state = api.to_device(host, dev) if resets else None
     reset_count = torch.zeros(n, dtype=torch.int32, device=dev) if resets else None
 
-    def world_step(a):
-        eng.step_(state, sc.settings, configs.DT, 1, a)
+    S = args.substeps
+    acts = torch.from_numpy(actions_for(n, (K + Wm) * S, args.seed, first).reshape(K + Wm, S, n, na)).to(dev) \
+        if na else None
+
+    def world_step(a):  # one call: S physics steps of every world (one launch), then the resets (c4)
+        eng.step_(state, sc.settings, configs.DT, S, a)
         if resets:
             eng.reset_below(state, init_state, 1, -5.0, reset_count)
 
+    for k0 in range(0, args.skip, S):  # the episode's start, untimed, in calls of S steps like the timed ones
+        k1 = min(args.skip, k0 + S)
+        skip_acts = torch.from_numpy(actions_for(n, k1 - k0, args.seed + 1000 + k0, first)).to(dev) if na else None
+        eng.step_(state, sc.settings, configs.DT, k1 - k0, skip_acts)
+        if resets:
+            eng.reset_below(state, init_state, 1, -5.0, reset_count)
     for k in range(Wm):
         world_step(acts[k] if na else None)
     torch.cuda.synchronize(dev)
@@ -274,14 +291,15 @@ def main():
     if world_size > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world_size * n * K / (ms_max / 1e3)
+    value = world_size * n * K * S / (ms_max / 1e3)
 
-    # e2e through the public API with host buffers: per step, this step's actions read from pinned host memory by
-    # the step kernel (mapped memory: the host->device transfer, no separate copy), the step, and the pot's
+    # e2e through the public API with host buffers: per call, its S rows of actions read from pinned host memory by
+    # the step kernel (mapped memory: the host->device transfer, no separate copy), the S steps, and the pot's
     # observation (position, angle, velocities) written by goib2d_observe into pinned host memory; the host
     # synchronises at the end of the timed region before reading it
     Ke = max(3, min(K, 20))
-    a_pin = torch.from_numpy(actions_for(n, Ke, args.seed + 1, first)).pin_memory() if na else None
+    a_pin = torch.from_numpy(actions_for(n, Ke * S, args.seed + 1, first).reshape(Ke, S, n, na)).pin_memory() \
+        if na else None
     obs_pin = torch.empty((n, 1, 6), dtype=torch.float32).pin_memory()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -296,7 +314,7 @@ def main():
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world_size > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world_size * n * Ke / (float(te.item()) / 1e3)
+    e2e_value = world_size * n * Ke * S / (float(te.item()) / 1e3)
 
     # episode statistics gathered over NCCL (off the timed path): body 1's position / velocity and the status word
     stats = shard.gather_stats(shard.episode_stats(state, 1, status))
@@ -305,7 +323,7 @@ def main():
     if rank == 0:
         bytes_ws = state_bytes(state) + (8 if na else 0)
         peak, peak_kind = measured_peak()
-        achieved = bytes_ws * n / (ms_max / 1e3 / K) / 1e9
+        achieved = bytes_ws * n * S / (ms_max / 1e3 / K) / 1e9
         traffic = None
         tp = ROOT / "profiles" / f"traffic_{args.config}.json"
         if tp.exists():
@@ -316,23 +334,23 @@ def main():
             cpu = cpu_baseline(sc, model, host, cpu_sample_worlds(args, n))
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": K, "warmup": Wm,
-            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms_max / K, "physics_steps_per_step": S, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded worlds, goib2d/configs.py)",
             "config": workload_config(args, sc, model, host.bodies.type.shape[1], n, world_size),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                          "algorithmic_bytes_per_world_step": bytes_ws,
-                         "kernel": (f"one step's launch group ({eng.kernels_per_step(n)} "
-                                    f"kernel(s){' + the reset kernel' if resets else ''}), timed as one unit by the "
-                                    "per-step CUDA events"),
+                         "kernel": (f"one call's launch group ({eng.launches(n, S)} launch(es) for {S} physics "
+                                    f"step(s){' + the reset kernel' if resets else ''}), timed as one unit by the "
+                                    "per-call CUDA events"),
                          "traffic_source": f"profiles/traffic_{args.config}.json (ncu dram bytes of the launch group)"
                                            if traffic is not None else None},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": n * na * 4 * world_size,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": n * na * 4 * S * world_size,
                     "d2h_bytes_per_step": n * 6 * 4 * world_size, "steps": Ke,
                     "path": "actions read from pinned host memory by the step kernel; goib2d_observe writes the pot's "
                             "pose and velocity to pinned host memory"},
-            "gpu_launches": K * (eng.kernels_per_step(n) + int(resets)), "clocks": clk,
+            "gpu_launches": K * (eng.launches(n, S) + int(resets)), "clocks": clk,
             "wall_s_timed": wall,
             "nonfinite_worlds": nonfinite,
             "cpu_baseline": cpu}
