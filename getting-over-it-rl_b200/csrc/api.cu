@@ -81,6 +81,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
     L.isl = take(16);
     L.adj_start = take(4 * (int64_t)(B + 1)), L.adj_cur = take(b4), L.adj = take(2 * 8 * (int64_t)(C > 0 ? C : 1));
+    L.lkey = take(8 * (int64_t)(C > 0 ? C : 1));
 #ifndef GOIB2D_HOT_MAX_BYTES
 #define GOIB2D_HOT_MAX_BYTES 6144
 #endif

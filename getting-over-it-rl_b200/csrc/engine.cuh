@@ -106,6 +106,7 @@ struct Layout {
     int64_t isl;  // [3] island counts: contacts, joints, islands
     // island graph: [B + 1] CSR start and [B] fill cursor over bodies, [2C] (contact slot, other body) pairs
     int64_t adj_start, adj_cur, adj;
+    int64_t lkey;  // [C] int64: the live slots' packed list-order keys (list_order)
     // [ceil(P/32)]
     int64_t bitmap;
     int64_t hits;  // [max_hits] new-pair candidates of the grid path

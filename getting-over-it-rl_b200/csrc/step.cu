@@ -90,6 +90,7 @@ struct Ctx {
     int lane;    // the thread's lane in the world's group, 0 .. wl - 1
     int status;
     int step;      // the step of the call being run (0 .. n_steps - 1)
+    int fnc_clean; // the world's last FindNewContacts placed every new pair (no overflow); 0 at a kernel's start
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
     int64_t world;
     unsigned gmask;  // the world's lanes in the warp: all 32, or one half (the step kernel: two worlds per warp)
@@ -169,48 +170,99 @@ __device__ __forceinline__ bool is_new_pair(Ctx &x, int p, const uint32_t *bitma
     return can && !((bitmap[p >> 5] >> (p & 31)) & 1u);
 }
 
-// the grid path's hits (candidate indices, any order); returns the count, or -1 when the buffer overflowed
-__device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits) {
+// does candidate p join a fixture of a moved body?
+__device__ __forceinline__ bool pair_moved(const DevModel &m, int p, const int *moved) {
+    return moved[m.fixture_body[m.pair_a[p]]] || moved[m.fixture_body[m.pair_b[p]]];
+}
+
+// Exclusive scan of v over the world's lanes; *total = the sum.
+__device__ __forceinline__ int gscan(const Ctx &x, int v, int *total) {
+    int inc = v;
+    for (int o = 1; o < x.wl; o <<= 1) {
+        const int t = __shfl_up_sync(x.gmask, inc, o, x.wl);
+        if (x.lane >= o) inc += t;
+    }
+    *total = gshfl(x, inc, x.wl - 1);
+    return inc - v;
+}
+// The lane whose range [off, off + cnt) of an exclusive scan holds position q (q below the total): the last lane
+// with a non-empty range starting at or before q. Every lane of the world runs it (its own q).
+__device__ __forceinline__ int gowner(const Ctx &x, int off, int cnt, int q) {
+    int owner = 0;
+    for (int j = 1; j < x.wl; ++j) {
+        const int oj = gshfl(x, off, j), cj = gshfl(x, cnt, j);
+        if (cj > 0 && oj <= q) owner = j;
+    }
+    return owner;
+}
+
+// the grid path's hits (candidate indices, any order); returns the count, or -1 when the buffer overflowed.
+// The query is dealt across the world's lanes in rounds rather than walked cell by cell: per round of WL fixture
+// rows, each lane takes a row's cell rectangle; the (row, cell) pairs are then dealt one per lane, each lane reading
+// its cell's range of listed static fixtures; and the listed (row, static fixture) items are dealt one per lane for
+// the overlap tests. A world's query is thus a few chains of dependent loads instead of one chain per cell.
+__device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits, const int *moved) {
     const DevModel &m = x.m;
     const W &w = x.w;
-    const int lane = x.lane, cap = m.max_hits;
+    const int lane = x.lane, cap = m.max_hits, WL = x.wl;
     int n = 0;
-    for (int r = 0; r < m.n_rows; ++r) {
-        const float *dp = w.fx_fat + 4 * r;
-        AABB D{dp[0], dp[1], dp[2], dp[3]};
-        int cx0 = grid_cell(D.lx, m.gx0, m.inv_cell, m.nx), cx1 = grid_cell(D.ux, m.gx0, m.inv_cell, m.nx);
-        int cy0 = grid_cell(D.ly, m.gy0, m.inv_cell, m.ny), cy1 = grid_cell(D.uy, m.gy0, m.inv_cell, m.ny);
-        const int32_t *cand = m.cand_rs + (int64_t)r * m.n_static;
-        for (int cy = cy0; cy <= cy1; ++cy)
-            for (int cx = cx0; cx <= cx1; ++cx) {
-                int c = cy * m.nx + cx;
-                int b0 = m.cell_start[c], b1 = m.cell_start[c + 1];
-                for (int base = b0; base < b1; base += x.wl) {
-                    int i = base + lane, p = -1;
-                    if (i < b1) {
-                        int si = m.cell_items[i];
-                        const float *sf = m.sfat + 4 * si;
-                        AABB S{sf[0], sf[1], sf[2], sf[3]};
-                        // report the pair only in the cell holding the lower corner of the two boxes' overlap
-                        bool here = grid_cell(fmaxf(D.lx, S.lx), m.gx0, m.inv_cell, m.nx) == cx &&
-                                    grid_cell(fmaxf(D.ly, S.ly), m.gy0, m.inv_cell, m.ny) == cy;
-                        if (here && overlap(D, S)) {
-                            int pc = cand[si];
-                            if (pc >= 0 && is_new_pair(x, pc, bitmap)) p = pc;
-                        }
-                    }
-                    unsigned mk = gballot(x, p >= 0);
-                    if (p >= 0) {
-                        int k = n + __popc(mk & ((1u << lane) - 1));
-                        if (k < cap) hits[k] = p;
-                    }
-                    n += __popc(mk);
-                }
+    for (int r0 = 0; r0 < m.n_rows; r0 += WL) {
+        const int r = r0 + lane;
+        int cx0 = 0, cy0 = 0, ncx = 1, nq = 0;
+        if (r < m.n_rows && (!moved || moved[m.fixture_body[m.row_fixture[r]]])) {
+            const float *dp = w.fx_fat + 4 * r;
+            const int ax = grid_cell(dp[0], m.gx0, m.inv_cell, m.nx), bx = grid_cell(dp[2], m.gx0, m.inv_cell, m.nx);
+            const int ay = grid_cell(dp[1], m.gy0, m.inv_cell, m.ny), by = grid_cell(dp[3], m.gy0, m.inv_cell, m.ny);
+            cx0 = ax, cy0 = ay, ncx = bx - ax + 1, nq = ncx * (by - ay + 1);
+        }
+        int Q = 0;
+        const int qoff = gscan(x, nq, &Q);
+        for (int q0 = 0; q0 < Q; q0 += WL) {  // (row, cell) pairs, one per lane
+            const int q = q0 + lane;
+            const int ro = gowner(x, qoff, nq, q);
+            const int o_off = gshfl(x, qoff, ro), o_cx0 = gshfl(x, cx0, ro), o_cy0 = gshfl(x, cy0, ro);
+            const int o_ncx = gshfl(x, ncx, ro);
+            int row = r0 + ro, cx = 0, cy = 0, b0 = 0, ni = 0;
+            if (q < Q) {
+                const int l = q - o_off;
+                cx = o_cx0 + l % o_ncx, cy = o_cy0 + l / o_ncx;
+                const int c = cy * m.nx + cx;
+                b0 = m.cell_start[c], ni = m.cell_start[c + 1] - b0;
             }
+            int T = 0;
+            const int ioff = gscan(x, ni, &T);
+            for (int t0 = 0; t0 < T; t0 += WL) {  // listed static fixtures of those cells, one per lane
+                const int t = t0 + lane;
+                const int co = gowner(x, ioff, ni, t);
+                const int c_off = gshfl(x, ioff, co), c_b0 = gshfl(x, b0, co), c_cx = gshfl(x, cx, co);
+                const int c_cy = gshfl(x, cy, co), c_row = gshfl(x, row, co);
+                int p = -1;
+                if (t < T) {
+                    const int si = m.cell_items[c_b0 + (t - c_off)];
+                    const float *dp = w.fx_fat + 4 * c_row;
+                    const AABB D{dp[0], dp[1], dp[2], dp[3]};
+                    const float *sf = m.sfat + 4 * si;
+                    const AABB S{sf[0], sf[1], sf[2], sf[3]};
+                    // report the pair only in the cell holding the lower corner of the two boxes' overlap
+                    const bool here = grid_cell(fmaxf(D.lx, S.lx), m.gx0, m.inv_cell, m.nx) == c_cx &&
+                                      grid_cell(fmaxf(D.ly, S.ly), m.gy0, m.inv_cell, m.ny) == c_cy;
+                    if (here && overlap(D, S)) {
+                        const int pc = m.cand_rs[(int64_t)c_row * m.n_static + si];
+                        if (pc >= 0 && is_new_pair(x, pc, bitmap)) p = pc;
+                    }
+                }
+                const unsigned mk = gballot(x, p >= 0);
+                if (p >= 0) {
+                    const int k = n + __popc(mk & ((1u << lane) - 1));
+                    if (k < cap) hits[k] = p;
+                }
+                n += __popc(mk);
+            }
+        }
     }
     for (int base = 0; base < m.n_dd; base += x.wl) {  // pairs of two non-static fixtures: every one, in order
         int i = base + lane, p = -1;
-        if (i < m.n_dd && is_new_pair(x, m.dd[i], bitmap)) p = m.dd[i];
+        if (i < m.n_dd && (!moved || pair_moved(m, m.dd[i], moved)) && is_new_pair(x, m.dd[i], bitmap)) p = m.dd[i];
         unsigned mk = gballot(x, p >= 0);
         if (p >= 0) {
             int k = n + __popc(mk & ((1u << lane) - 1));
@@ -222,7 +274,11 @@ __device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits) {
     return n <= cap ? n : -1;
 }
 
-__device__ void find_new_contacts(Ctx &x) {
+// moved (or null): the call follows a FindNewContacts of this world that placed every new pair, and since then only
+// the fixtures of the bodies flagged in moved were re-fattened (a TOI event: b2Island::SolveTOI's bodies) and no
+// contact was destroyed. Every other candidate pair then kept its overlap and already has its contact, so only pairs
+// joining a moved body's fixture are tested: the same new contacts, slots and keys as testing every pair.
+__device__ void find_new_contacts(Ctx &x, const int *moved = nullptr) {
     const DevModel &m = x.m;
     W &w = x.w;
     const int P = m.P, C = w.C, lane = x.lane;
@@ -249,7 +305,7 @@ __device__ void find_new_contacts(Ctx &x) {
     int n_new = -1;
     if (m.grid) {
         int *hits = ap<int>(x, x.p.lay.hits), *sorted = hits + m.max_hits;
-        n_new = grid_new_pairs(x, bitmap, hits);
+        n_new = grid_new_pairs(x, bitmap, hits, moved);
         if (n_new > 0) {  // into candidate order (the hits are distinct), then into the lowest free slots
             for (int i = lane; i < n_new; i += x.wl) {
                 int h = hits[i], rank = 0;
@@ -264,7 +320,7 @@ __device__ void find_new_contacts(Ctx &x) {
         n_new = 0;
         for (int base = 0; base < P; base += x.wl) {
             int p = base + lane;
-            bool nw_ = p < P && is_new_pair(x, p, bitmap);
+            bool nw_ = p < P && (!moved || pair_moved(m, p, moved)) && is_new_pair(x, p, bitmap);
             unsigned mk = gballot(x, nw_);
             if (nw_) {
                 int rank = n_new + __popc(mk & ((1u << lane) - 1));
@@ -280,31 +336,43 @@ __device__ void find_new_contacts(Ctx &x) {
         *w.overflow += n_new - placed;
         if (n_new > placed) x.status |= ST_OVERFLOW;
     }
+    x.fnc_clean = n_new <= n_free;  // both are the same on every lane of the world
     gsync(x);
 }
 
-// Live slots in contact-list order (descending key): order[0..n) and each slot's position lpos[slot] (C if dead)
+// Live slots in contact-list order (descending key): order[0..n) and each slot's position lpos[slot] (C if dead).
+// The live slots are first compacted with their packed keys (key in the high word, the slot's complement in the low
+// word: a larger packed key is a larger key, or the same key - never in a valid State - at a lower slot, the order
+// of a stable sort), then each live slot's position is the number of live packed keys above its own: the work grows
+// with the live contacts, not with the capacity.
+__device__ __forceinline__ long long list_key(int key, int slot) {
+    return (long long)key * 4294967296LL + (long long)(~(unsigned)slot);
+}
 __device__ int list_order(Ctx &x, int *order, int *lpos) {
+    GB_TOI_T0();
     W &w = x.w;
     const int C = w.C, lane = x.lane;
+    long long *lk = ap<long long>(x, x.p.lay.lkey);
     int n_live = 0;
     for (int base = 0; base < C; base += x.wl) {
-        int s = base + lane;
-        bool live = s < C && w.pair[s] >= 0;
-        if (s < C) {
-            int pos = C;
-            if (live) {
-                int k = w.key[s], cnt = 0;
-                for (int t = 0; t < C; ++t)  // ties (never in a valid State) by slot, as a stable sort
-                    cnt += (w.pair[t] >= 0 && (w.key[t] > k || (w.key[t] == k && t < s)));
-                pos = cnt;
-                order[cnt] = s;
-            }
-            lpos[s] = pos;
-        }
-        n_live += __popc(gballot(x, live));
+        const int s = base + lane;
+        const bool live = s < C && w.pair[s] >= 0;
+        const unsigned mk = gballot(x, live);
+        if (live) lk[n_live + __popc(mk & ((1u << lane) - 1))] = list_key(w.key[s], s);
+        else if (s < C) lpos[s] = C;
+        n_live += __popc(mk);
     }
     gsync(x);
+    for (int j = lane; j < n_live; j += x.wl) {
+        const long long k = lk[j];
+        int cnt = 0;
+        for (int i = 0; i < n_live; ++i) cnt += lk[i] > k;
+        const int s = (int)~(unsigned)(k & 0xffffffffLL);
+        order[cnt] = s;
+        lpos[s] = cnt;
+    }
+    gsync(x);
+    if (x.lane == 0) GB_TOI_T1(15);
     return n_live;
 }
 
@@ -1242,7 +1310,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         old_pair[s_] = w.pair[s_], old_key[s_] = w.key[s_];
     }
     gsync(x);
-    find_new_contacts(x);
+    find_new_contacts(x, x.fnc_clean ? moved : nullptr);
     for (int s_ = lane; s_ < C; s_ += x.wl) {
         bool is_new = w.pair[s_] >= 0 && (old_pair[s_] < 0 || old_key[s_] != w.key[s_]);
         if (is_new) w.t_count[s_] = 0, w.t_flag[s_] = 0, w.t_enabled[s_] = 1;
@@ -1375,7 +1443,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
     char *mine = dyn_smem + warp * region;
     Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
-          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, p.step, clock64(), world, FULL, 0, 32};
+          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, p.step, 0, clock64(), world, FULL, 0, 32};
     run_part<PART>(x);
     put_status(x, PART == 0 && p.step == 0);
 }
@@ -1438,7 +1506,7 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
     char *rows = hot && p.lay.rows_bytes ? hot + p.lay.hot_end : nullptr;
     if (active && (lane32 & (WL - 1)) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
-    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, clock64(), world,
+    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, 0, clock64(), world,
           WPW == 2 ? 0xffffu << (16 * half) : FULL, WL * half, WL};
     const float dt = p.dt;
     for (int k = 0; k < p.n_steps; ++k) {
@@ -1561,7 +1629,11 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const int region = step_region(p.lay);
-        int per_sm = (int)((n + sms - 1) / sms);  // worlds per block: one block per SM where the batch allows
+#ifndef GOIB2D_BLOCKS_PER_SM
+#define GOIB2D_BLOCKS_PER_SM 1
+#endif
+        // worlds per block: GOIB2D_BLOCKS_PER_SM blocks per SM where the batch allows
+        int per_sm = (int)((n + (int64_t)sms * GOIB2D_BLOCKS_PER_SM - 1) / ((int64_t)sms * GOIB2D_BLOCKS_PER_SM));
         const bool pair = p.step_mode ? p.step_mode == 2 : step_pairs(n, sms, p.C);
         const int wpw = pair ? 2 : 1, max_warps = pair ? PAIR_MAX_WARPS : STEP_MAX_WARPS;
         int warps = (per_sm + wpw - 1) / wpw;
