@@ -68,24 +68,31 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
         return o;
     };
     const int64_t b4 = 4 * (int64_t)(B > 0 ? B : 1), c4 = 4 * (int64_t)(C > 0 ? C : 1), j4 = 4 * (int64_t)(J > 0 ? J : 1);
-    // the hot part first: the small arrays the sequential phases write and read back (see Layout::hot_end)
-    L.vx = take(b4), L.vy = take(b4), L.vw = take(b4), L.cx = take(b4), L.cy = take(b4), L.ca = take(b4);
-    L.qc = take(b4), L.qs = take(b4), L.qa = take(b4);
-    L.aw = take(b4), L.bisl = take(b4), L.stack = take(b4), L.bflag = take(b4), L.last = take(b4);
-    L.moved = take(b4), L.done = take(b4), L.minsep = take(b4), L.jok = take(b4), L.islsleep = take(b4);
-    L.minst = take(b4), L.st = take(b4);
-    L.adv = take(8 * b4);
-    L.order = take(c4), L.lpos = take(c4), L.corder = take(c4), L.cisl = take(c4), L.cflag = take(c4);
-    L.freeslot = take(c4), L.active = take(c4), L.over = take(c4), L.edges = take(c4), L.tneed = take(c4);
-    L.tisl = take(c4), L.solved = take(c4);
-    L.jorder = take(j4), L.jisl = take(j4), L.jflag = take(j4);
-    L.isl = take(16);
-    L.adj_start = take(4 * (int64_t)(B + 1)), L.adj_cur = take(b4), L.adj = take(2 * 8 * (int64_t)(C > 0 ? C : 1));
-    L.lkey = take(8 * (int64_t)(C > 0 ? C : 1));
+    // the hot part first: the small arrays the sequential phases write and read back (see Layout::hot_end), the
+    // most used first, so that the prefix a kernel keeps in shared memory holds them when the whole part does not fit
 #ifndef GOIB2D_HOT_MAX_BYTES
 #define GOIB2D_HOT_MAX_BYTES 6144
 #endif
-    L.hot_end = off <= GOIB2D_HOT_MAX_BYTES ? (int)off : 0;
+    int64_t fits = 0;  // the largest array boundary within the shared-memory budget
+    auto hot = [&](int64_t bytes) {
+        int64_t o = take(bytes);
+        if (off <= GOIB2D_HOT_MAX_BYTES) fits = off;
+        return o;
+    };
+    L.vx = hot(b4), L.vy = hot(b4), L.vw = hot(b4), L.cx = hot(b4), L.cy = hot(b4), L.ca = hot(b4);
+    L.qc = hot(b4), L.qs = hot(b4), L.qa = hot(b4);
+    L.aw = hot(b4), L.bisl = hot(b4), L.stack = hot(b4), L.bflag = hot(b4), L.last = hot(b4);
+    L.moved = hot(b4), L.done = hot(b4), L.minsep = hot(b4), L.jok = hot(b4), L.islsleep = hot(b4);
+    L.minst = hot(b4), L.st = hot(b4);
+    L.isl = hot(16);
+    L.order = hot(c4), L.lpos = hot(c4), L.lkey = hot(8 * (int64_t)(C > 0 ? C : 1));
+    L.adv = hot(8 * b4);
+    L.corder = hot(c4), L.cisl = hot(c4), L.cflag = hot(c4);
+    L.freeslot = hot(c4), L.active = hot(c4), L.over = hot(c4), L.edges = hot(c4), L.tneed = hot(c4);
+    L.tisl = hot(c4), L.solved = hot(c4);
+    L.jorder = hot(j4), L.jisl = hot(j4), L.jflag = hot(j4);
+    L.adj_start = hot(4 * (int64_t)(B + 1)), L.adj_cur = hot(b4), L.adj = hot(2 * 8 * (int64_t)(C > 0 ? C : 1));
+    L.hot_end = (int)fits;
     // the cold part: rows, manifolds, records and the broadphase buffers
     L.man = take((int64_t)sizeof(gb::Man) * (C > 0 ? C : 1));
     L.vc = take((int64_t)sizeof(gb::VCRow) * (C > 0 ? C : 1));

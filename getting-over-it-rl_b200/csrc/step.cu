@@ -91,6 +91,7 @@ struct Ctx {
     int status;
     int step;      // the step of the call being run (0 .. n_steps - 1)
     int fnc_clean; // the world's last FindNewContacts placed every new pair (no overflow); 0 at a kernel's start
+    int order_n;   // live contacts of the list order in the arena's order / lpos, if still valid; else -1
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
     int64_t world;
     unsigned gmask;  // the world's lanes in the warp: all 32, or one half (the step kernel: two worlds per warp)
@@ -337,6 +338,7 @@ __device__ void find_new_contacts(Ctx &x, const int *moved = nullptr) {
         if (n_new > placed) x.status |= ST_OVERFLOW;
     }
     x.fnc_clean = n_new <= n_free;  // both are the same on every lane of the world
+    if (n_new > 0 && n_free > 0) x.order_n = -1;  // contacts were placed
     gsync(x);
 }
 
@@ -373,7 +375,13 @@ __device__ int list_order(Ctx &x, int *order, int *lpos) {
     }
     gsync(x);
     if (x.lane == 0) GB_TOI_T1(15);
+    x.order_n = n_live;
     return n_live;
+}
+// The list order, recomputed only when a contact was created or destroyed since the last list_order: the TOI loop
+// (a search, then an event, then a search ...) changes the slots only where an event creates contacts.
+__device__ __forceinline__ int list_order_kept(Ctx &x, int *order, int *lpos) {
+    return x.order_n >= 0 ? x.order_n : list_order(x, order, lpos);
 }
 
 // ---------------------------------------------------------------- b2ContactManager::Collide (pairs.py:38-117)
@@ -448,6 +456,7 @@ __device__ void collide(Ctx &x) {
         }
         active[s] = ev + 1;  // reused: the event of each visited slot
     }
+    x.order_n = -1;  // contacts may have been destroyed
     if (x.p.events) {  // the step's log starts with Collide's events, in contact-list order
         gsync(x);
         int n = 0;
@@ -935,7 +944,7 @@ __device__ bool toi_search(Ctx &x, int *min_slot, float *min_alpha) {
     const Layout &L = x.p.lay;
     int *order = ap<int>(x, L.order), *lpos = ap<int>(x, L.lpos), *tneed = ap<int>(x, L.tneed);
     float *rec = ap<float>(x, L.rec);
-    int n_live = list_order(x, order, lpos);
+    int n_live = list_order_kept(x, order, lpos);
     // Sweep alignment in list order (toi.py:500-536): a candidate whose bodies' sweeps sit at different alpha0
     // advances the one behind, which every later candidate of that body sees. Between two advances nothing moves, so
     // each round records, in parallel, every candidate up to the next advance, which lane 0 then performs.
@@ -1059,7 +1068,7 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         d[4] = xf.p.x, d[5] = xf.p.y, d[6] = xf.q.c, d[7] = xf.q.s;
         flip_b[b] = in_other[b] = touched[b] = newbody[b] = 0;
     }
-    int n_live = list_order(x, order, lpos);
+    int n_live = list_order_kept(x, order, lpos);
     for (int s_ = lane; s_ < C; s_ += x.wl) {  // manifolds at the advanced poses for the pair's contacts
         solved[s_] = 0;
         if (w.pair[s_] < 0) continue;
@@ -1333,6 +1342,7 @@ __device__ void solve_toi(Ctx &x, float dt) {  // toi.py:827-865
         w.t_ni[2 * c] = w.t_ni[2 * c + 1] = w.t_ti[2 * c] = w.t_ti[2 * c + 1] = 0.0f;
     }
     if (lane == 0) *w.t_events = 0;
+    x.order_n = -1;
     gsync(x);
     if (!(dt > 0)) return;
     const int max_events = C * (MAX_SUB_STEPS + 1) + 8;
@@ -1443,7 +1453,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
     char *mine = dyn_smem + warp * region;
     Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
-          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, p.step, 0, clock64(), world, FULL, 0, 32};
+          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, p.step, 0, -1, clock64(), world, FULL, 0, 32};
     run_part<PART>(x);
     put_status(x, PART == 0 && p.step == 0);
 }
@@ -1506,7 +1516,7 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
     char *rows = hot && p.lay.rows_bytes ? hot + p.lay.hot_end : nullptr;
     if (active && (lane32 & (WL - 1)) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
-    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, 0, clock64(), world,
+    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, 0, -1, clock64(), world,
           WPW == 2 ? 0xffffu << (16 * half) : FULL, WL * half, WL};
     const float dt = p.dt;
     for (int k = 0; k < p.n_steps; ++k) {
