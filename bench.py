@@ -328,7 +328,7 @@ def main():
         tp = ROOT / "profiles" / f"traffic_{args.config}.json"
         if tp.exists():
             td = json.loads(tp.read_text())
-            traffic = td.get("dram_bytes_per_world_step", 0) * n
+            traffic = td.get("dram_bytes_per_world_step", 0) * n * S  # per launch group of one call
         cpu = None
         if not args.no_cpu_baseline:
             cpu = cpu_baseline(sc, model, host, cpu_sample_worlds(args, n))

@@ -85,7 +85,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.moved = hot(b4), L.done = hot(b4), L.minsep = hot(b4), L.jok = hot(b4), L.islsleep = hot(b4);
     L.minst = hot(b4), L.st = hot(b4);
     L.isl = hot(16);
-    L.order = hot(c4), L.lpos = hot(c4), L.lkey = hot(8 * (int64_t)(C > 0 ? C : 1));
+    L.order = hot(c4), L.lpos = hot(c4), L.lkey = hot(8 * (int64_t)(C > 0 ? C : 1)), L.order2 = hot(c4);
     L.adv = hot(8 * b4);
     L.corder = hot(c4), L.cisl = hot(c4), L.cflag = hot(c4);
     L.freeslot = hot(c4), L.active = hot(c4), L.over = hot(c4), L.edges = hot(c4), L.tneed = hot(c4);
@@ -98,6 +98,10 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.vc = take((int64_t)sizeof(gb::VCRow) * (C > 0 ? C : 1));
     L.rec = take(8 * c4);
     L.jr = take((int64_t)sizeof(gb::JRow) * (J > 0 ? J : 1));
+    const int64_t n_rows4 = 4 * (int64_t)((C > 0 ? C : 0) + (J > 0 ? J : 0) + 2);
+    L.lv_level = take(n_rows4), L.lv_items = take(n_rows4), L.lv_start = take(n_rows4), L.lv_cur = take(n_rows4);
+    L.lv_items2 = take(n_rows4), L.lv_start2 = take(n_rows4);
+    L.lv_last = take(b4), L.lv_sep = take(c4), L.lv_ok = take(j4);
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);

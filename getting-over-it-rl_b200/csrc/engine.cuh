@@ -106,8 +106,12 @@ struct Layout {
     int64_t isl;  // [3] island counts: contacts, joints, islands
     // island graph: [B + 1] CSR start and [B] fill cursor over bodies, [2C] (contact slot, other body) pairs
     int64_t adj_start, adj_cur, adj;
-    int64_t lkey;  // [C] int64: the live slots' packed list-order keys (list_order)
+    int64_t lkey;    // [C] int64: the live slots' packed list-order keys (list_order)
+    int64_t order2;  // [C] list_order's staging copy of the new list
     // [ceil(P/32)]
+    // levelled sweeps (solve_constraints_levelled): per pass position its level and the positions sorted by level,
+    // the level starts, fill cursors, each body's next free level, and the position passes' per-row results
+    int64_t lv_level, lv_items, lv_start, lv_items2, lv_start2, lv_cur, lv_last, lv_sep, lv_ok;
     int64_t bitmap;
     int64_t hits;  // [max_hits] new-pair candidates of the grid path
     int64_t stride;  // bytes per world (multiple of 256)

@@ -8,6 +8,7 @@
 // wake walk, the island DFS, the Gauss-Seidel velocity / position sweeps and the TOI island walk - run on lane 0 in
 // exactly the reference's order (goi_jax/box2d/step.py, island.py, pairs.py, toi.py), so results are bit-identical
 // to it. Per-world working arrays live in a scratch arena (L1/L2-resident), laid out by scratch_layout().
+#include <climits>
 #include <cstdio>
 #include <mutex>
 
@@ -92,6 +93,8 @@ struct Ctx {
     int step;      // the step of the call being run (0 .. n_steps - 1)
     int fnc_clean; // the world's last FindNewContacts placed every new pair (no overflow); 0 at a kernel's start
     int order_n;   // live contacts of the list order in the arena's order / lpos, if still valid; else -1
+    int base_n;    // the arena's order holds the list as of next_key == kref (base_n contacts), or -1 (list_order)
+    int kref;
     long long t0;  // phase timer origin (GOIB2D_PHASE_TIMERS builds only)
     int64_t world;
     unsigned gmask;  // the world's lanes in the warp: all 32, or one half (the step kernel: two worlds per warp)
@@ -343,40 +346,80 @@ __device__ void find_new_contacts(Ctx &x, const int *moved = nullptr) {
 }
 
 // Live slots in contact-list order (descending key): order[0..n) and each slot's position lpos[slot] (C if dead).
-// The live slots are first compacted with their packed keys (key in the high word, the slot's complement in the low
-// word: a larger packed key is a larger key, or the same key - never in a valid State - at a lower slot, the order
-// of a stable sort), then each live slot's position is the number of live packed keys above its own: the work grows
-// with the live contacts, not with the capacity.
+// A list is ranked from the packed keys (key in the high word, the slot's complement in the low word: a larger
+// packed key is a larger key, or the same key - never in a valid State - at a lower slot, the order of a stable
+// sort): each entry's position is the number of packed keys above its own. The first list of a kernel ranks every
+// live slot. Later lists are the earlier one brought up to date: new contacts get keys from next_key upwards, so the
+// contacts with a key at or above the earlier list's next_key (kref) are the ones created since - ranked among
+// themselves, they come first - and the earlier list's entries that still hold a contact with a key below kref
+// follow in their order (a destroyed contact drops out; a slot reused since holds a key at or above kref). A State
+// whose live keys reach its next_key (never made by a step) is ranked in full every time.
 __device__ __forceinline__ long long list_key(int key, int slot) {
     return (long long)key * 4294967296LL + (long long)(~(unsigned)slot);
+}
+// rank lk[0 .. n) (packed keys) into out[0 .. n) (slots), descending
+__device__ __forceinline__ void rank_desc(const Ctx &x, const long long *lk, int n, int *out) {
+    for (int j = x.lane; j < n; j += x.wl) {
+        const long long k = lk[j];
+        int cnt = 0;
+        for (int i = 0; i < n; ++i) cnt += lk[i] > k;
+        out[cnt] = (int)~(unsigned)(k & 0xffffffffLL);
+    }
 }
 __device__ int list_order(Ctx &x, int *order, int *lpos) {
     GB_TOI_T0();
     W &w = x.w;
     const int C = w.C, lane = x.lane;
     long long *lk = ap<long long>(x, x.p.lay.lkey);
-    int n_live = 0;
-    for (int base = 0; base < C; base += x.wl) {
+    int *staged = ap<int>(x, x.p.lay.order2);
+    const int kref = x.kref, next_key = *w.next_key;
+    const bool incremental = x.base_n >= 0;
+    int n_new = 0, max_key = INT_MIN;
+    for (int base = 0; base < C; base += x.wl) {  // the live slots (all of them, or those created since kref)
         const int s = base + lane;
-        const bool live = s < C && w.pair[s] >= 0;
-        const unsigned mk = gballot(x, live);
-        if (live) lk[n_live + __popc(mk & ((1u << lane) - 1))] = list_key(w.key[s], s);
-        else if (s < C) lpos[s] = C;
-        n_live += __popc(mk);
+        bool pick = false;
+        if (s < C && w.pair[s] >= 0) {
+            const int k = w.key[s];
+            max_key = k > max_key ? k : max_key;
+            pick = !incremental || k >= kref;
+        }
+        const unsigned mk = gballot(x, pick);
+        if (pick) lk[n_new + __popc(mk & ((1u << lane) - 1))] = list_key(w.key[s], s);
+        n_new += __popc(mk);
     }
     gsync(x);
-    for (int j = lane; j < n_live; j += x.wl) {
-        const long long k = lk[j];
-        int cnt = 0;
-        for (int i = 0; i < n_live; ++i) cnt += lk[i] > k;
-        const int s = (int)~(unsigned)(k & 0xffffffffLL);
-        order[cnt] = s;
-        lpos[s] = cnt;
+    rank_desc(x, lk, n_new, staged);
+    int n = n_new;
+    if (incremental) {  // the earlier list's surviving contacts, in their order, after the new ones
+        for (int base = 0; base < x.base_n; base += x.wl) {
+            const int j = base + lane;
+            int s = -1;
+            if (j < x.base_n) {
+                s = order[j];
+                if (!(w.pair[s] >= 0 && w.key[s] < kref)) s = -1;
+            }
+            const unsigned mk = gballot(x, s >= 0);
+            if (s >= 0) staged[n + __popc(mk & ((1u << lane) - 1))] = s;
+            n += __popc(mk);
+        }
+    }
+    gsync(x);
+    for (int s = lane; s < C; s += x.wl) lpos[s] = C;
+    gsync(x);
+    for (int j = lane; j < n; j += x.wl) {
+        const int s = staged[j];
+        order[j] = s, lpos[s] = j;
+    }
+    for (int o = x.wl >> 1; o > 0; o >>= 1) {
+        const int t = __shfl_xor_sync(x.gmask, max_key, o, x.wl);
+        max_key = t > max_key ? t : max_key;
     }
     gsync(x);
     if (x.lane == 0) GB_TOI_T1(15);
-    x.order_n = n_live;
-    return n_live;
+    x.order_n = n;
+    const bool keys_below = n == 0 || max_key < next_key;  // a State made by steps: every key below next_key
+    x.base_n = keys_below ? n : -1, x.kref = next_key;
+    return n;
 }
 // The list order, recomputed only when a contact was created or destroyed since the last list_order: the TOI loop
 // (a search, then an event, then a search ...) changes the slots only where an event creates contacts.
@@ -824,6 +867,226 @@ __device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t w
         }
         for (int i = 0; i < n_islands; ++i)
             if (minsep[i] >= -3.0f * s.linear_slop && jok[i]) done[i] = 1;
+    }
+}
+
+// ---------------------------------------------------------------- the island sweeps over the world's lanes
+// A pass of the sweeps solves the island constraints one after another in a fixed order: the contacts then the
+// joints (warm start, each position iteration) or the joints then the contacts (each velocity iteration). A
+// constraint reads and writes the velocities (positions) of its two bodies only, so its result depends only on the
+// earlier constraints of the pass that share a body with it. Level l of a pass holds the constraints whose earlier
+// neighbours all sit on levels below l (greedy levelling in pass order): the constraints of one level share no body,
+// and solving the levels one after another, each level's constraints at once on the world's lanes, gives every
+// constraint the same inputs as the sequential pass - the same floats. Bodies that are not dynamic (inverse mass and
+// inertia 0) are no dependency: a solve adds or subtracts 0 * impulse to their values, which leaves a finite value
+// that is not -0 unchanged; a world with a -0 among those values takes the sequential pass.
+constexpr int LV_MIN_CONSTRAINTS = 12;  // smaller islands: lane 0, one constraint after another
+
+struct LvPass {  // one pass's order: element e is a contact (row e or e - nj) or a joint (row e - nc or e)
+    int nc, nj;  // contacts and joints in the pass
+    bool joints_first;
+    __device__ __forceinline__ bool is_joint(int e) const { return joints_first ? e < nj : e >= nc; }
+    __device__ __forceinline__ int row(int e) const { return joints_first ? (e < nj ? e : e - nj) : (e < nc ? e : e - nc); }
+};
+
+// The levels of a pass: items[start[l] .. start[l + 1]) are the pass elements of level l; returns the level count.
+__device__ int lv_levels(Ctx &x, const IslandWork &sw, const LvPass &ps, int *level, int *items, int *start,
+                         int *cur, int *last) {
+    W &w = x.w;
+    const int n = ps.nc + ps.nj, lane = x.lane;
+    for (int b = lane; b < w.B; b += x.wl) last[b] = 0;
+    gsync(x);
+    int nl = 0;
+    if (lane == 0) {  // greedy levelling in pass order (sequential by nature: each level depends on earlier ones)
+        for (int e = 0; e < n; ++e) {
+            const bool jt = ps.is_joint(e);
+            const int r = ps.row(e);
+            const int a = jt ? sw.jr[r].ia : sw.vc[r].ia, b = jt ? sw.jr[r].ib : sw.vc[r].ib;
+            const bool da = w.type[a] == DYNAMIC, db = w.type[b] == DYNAMIC;
+            const int la = da ? last[a] : 0, lb = db ? last[b] : 0;
+            const int l = la > lb ? la : lb;
+            level[e] = l;
+            if (da) last[a] = l + 1;
+            if (db) last[b] = l + 1;
+            nl = nl > l + 1 ? nl : l + 1;
+        }
+    }
+    nl = gshfl(x, nl, 0);
+    gsync(x);
+    for (int l = lane; l <= nl; l += x.wl) start[l] = 0;
+    gsync(x);
+    for (int e = lane; e < n; e += x.wl) atomicAdd(&start[level[e] + 1], 1);
+    gsync(x);
+    if (lane == 0)
+        for (int l = 0; l < nl; ++l) start[l + 1] += start[l];
+    gsync(x);
+    for (int l = lane; l < nl; l += x.wl) cur[l] = start[l];
+    gsync(x);
+    for (int e = lane; e < n; e += x.wl) items[atomicAdd(&cur[level[e]], 1)] = e;
+    gsync(x);
+    return nl;
+}
+
+// Does a body that is not dynamic hold -0 in the values the sweeps read (velocities, or positions)? Then the world
+// takes the sequential sweeps (see above).
+__device__ __forceinline__ bool lv_minus_zero(const Ctx &x, const Bodies &bd) {
+    bool bad = false;
+    for (int b = x.lane; b < x.w.B; b += x.wl) {
+        if (x.w.type[b] == DYNAMIC) continue;
+        const float v[6] = {bd.vx[b], bd.vy[b], bd.vw[b], bd.cx[b], bd.cy[b], bd.ca[b]};
+        for (int k = 0; k < 6; ++k) bad = bad || __float_as_uint(v[k]) == 0x80000000u;
+    }
+    return gballot(x, bad) != 0;
+}
+
+// solve_constraints with the passes levelled over the world's lanes: the same results, bit for bit (every lane of
+// the world calls it). Islands below LV_MIN_CONSTRAINTS constraints, and those whose velocity pass has fewer than
+// two constraints per level on average (a joint chain), run sequentially on lane 0.
+__device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const IslandIds &ids) {
+    const StepParams &p = x.p;
+    const goib2d_settings &s = x.s;
+    const int nc = ids.cnt[0], nj = ids.cnt[1], n_islands = ids.cnt[2], lane = x.lane;
+    const Layout &L = p.lay;
+    int *level = sp<int>(x.scr, L.lv_level), *cur = sp<int>(x.scr, L.lv_cur), *last = sp<int>(x.scr, L.lv_last);
+    int *vitems = sp<int>(x.scr, L.lv_items), *vstart = sp<int>(x.scr, L.lv_start);  // velocity pass
+    int *citems = sp<int>(x.scr, L.lv_items2), *cstart = sp<int>(x.scr, L.lv_start2);  // contacts-first passes
+    const LvPass vps{nc, nj, true}, cps{nc, nj, false};
+    int vnl = 0;
+    bool seq = nc + nj < LV_MIN_CONSTRAINTS || lv_minus_zero(x, sw.bd);
+    if (!seq) {
+        vnl = lv_levels(x, sw, vps, level, vitems, vstart, cur, last);
+        seq = 2 * vnl > nc + nj;
+    }
+    if (seq) {
+        if (lane == 0) solve_constraints(p, x.world, sw, ids);
+        gsync(x);
+        return;
+    }
+    if (lane == 0) {
+        GB_COUNT(14, 1);
+        GB_COUNT(15, vnl);
+    }
+    const int cnl = lv_levels(x, sw, cps, level, citems, cstart, cur, last);
+    const int B = p.m.B, C = p.C, J = p.m.J;
+    const int64_t world = x.world;
+    float *sep = sp<float>(x.scr, L.lv_sep);
+    int *okj = sp<int>(x.scr, L.lv_ok);
+    const int *cisl = ids.cisl, *jisl = ids.jisl;
+    int *done = sw.done, *jok = sw.jok;
+    float *minsep = sw.minsep;
+    VCRow *vc = sw.vc;
+    JRow *jr = sw.jr;
+    const Bodies &bd = sw.bd;
+    const bool warm = s.warm_starting, v24 = s.revolute_v24;
+    // warm start: the contacts (when warm starting) then the joints, the contacts-first levels (a level's contacts
+    // keep their independence when the joints are left out)
+    for (int l = 0; l < cnl; ++l) {
+        for (int i = cstart[l] + lane; i < cstart[l + 1]; i += x.wl) {
+            const int e = citems[i];
+            if (cps.is_joint(e)) joint_warm_start(jr[cps.row(e)], bd, v24);
+            else if (warm) contact_warm_start(vc[cps.row(e)], bd);
+        }
+        gsync(x);
+    }
+    // velocity iterations: the joints then the contacts, the same levels every iteration
+    for (int it = 0; it < s.velocity_iterations; ++it)
+        for (int l = 0; l < vnl; ++l) {
+            for (int i = vstart[l] + lane; i < vstart[l + 1]; i += x.wl) {
+                const int e = vitems[i];
+                if (vps.is_joint(e)) joint_solve_velocity(jr[vps.row(e)], bd, v24);
+                else contact_solve_velocity(vc[vps.row(e)], bd);
+            }
+            gsync(x);
+        }
+    // StoreImpulses (contact_solver.py:293-304, joints.py:609-622), one row per lane
+    float *normal_impulse = (float *)p.L.p[GOIB2D_C_NORMAL_IMPULSE] + world * 2 * C;
+    float *tangent_impulse = (float *)p.L.p[GOIB2D_C_TANGENT_IMPULSE] + world * 2 * C;
+    for (int k = lane; k < nc; k += x.wl) {
+        const VCRow &c = vc[k];
+        for (int j = 0; j < c.count; ++j)
+            normal_impulse[2 * c.slot + j] = c.ni[j], tangent_impulse[2 * c.slot + j] = c.ti[j];
+    }
+    float *lower_impulse = (float *)p.L.p[GOIB2D_J_LOWER_IMPULSE] + world * J;
+    float *upper_impulse = (float *)p.L.p[GOIB2D_J_UPPER_IMPULSE] + world * J;
+    float *impulse = (float *)p.L.p[GOIB2D_J_IMPULSE] + world * 3 * J;
+    float *motor_impulse = (float *)p.L.p[GOIB2D_J_MOTOR_IMPULSE] + world * J;
+    int32_t *limit_state = (int32_t *)p.L.p[GOIB2D_J_LIMIT_STATE] + world * J;
+    for (int k = lane; k < nj; k += x.wl) {
+        const JRow &r = jr[k];
+        if (v24) lower_impulse[r.jid] = r.imp[3], upper_impulse[r.jid] = r.imp[4];
+        for (int i = 0; i < 3; ++i) impulse[3 * r.jid + i] = r.imp[i];
+        motor_impulse[r.jid] = r.mimp;
+        limit_state[r.jid] = r.limit_state;
+    }
+    if (p.events) {  // b2Island::Report: PostSolve per island contact, in solve order
+        const int32_t *fa = (const int32_t *)p.L.p[GOIB2D_C_FA] + world * C;
+        const int32_t *fb = (const int32_t *)p.L.p[GOIB2D_C_FB] + world * C;
+        const int base = p.event_count[world];
+        for (int k = lane; k < nc; k += x.wl) {
+            const VCRow &c = vc[k];
+            put_event(p, world, base + k, EV_POST_SOLVE, fa[c.slot], fb[c.slot], c.count, c.ni, c.ti);
+        }
+        gsync(x);
+        if (lane == 0) p.event_count[world] = base + nc;
+    }
+    const float h = p.dt;
+    const float max_t = s.clamps_per_second ? s.max_translation * h : s.max_translation;
+    const float max_r = s.clamps_per_second ? s.max_rotation * h : s.max_rotation;
+    for (int b = lane; b < B; b += x.wl) {  // integrate positions (step.py:120-135)
+        if (ids.bisl[b] < 0) continue;
+        float vx = bd.vx[b], vy = bd.vy[b], ww = bd.vw[b];
+        float tx = h * vx, ty = h * vy;
+        if (tx * tx + ty * ty > max_t * max_t) {
+            float ratio = max_t / length(V2{tx, ty});
+            vx = vx * ratio, vy = vy * ratio;
+        }
+        float rt = h * ww;
+        if (rt * rt > max_r * max_r) ww = ww * (max_r / babs(rt));
+        bd.cx[b] = bd.cx[b] + h * vx, bd.cy[b] = bd.cy[b] + h * vy, bd.ca[b] = bd.ca[b] + h * ww;
+        bd.vx[b] = vx, bd.vy[b] = vy, bd.vw[b] = ww;
+    }
+    for (int i = lane; i < B; i += x.wl) done[i] = i >= n_islands;
+    gsync(x);
+    // position iterations with per-island early exit (step.py:197-251): the contacts then the joints, levelled; the
+    // islands' minimum separations are taken in pass order afterwards (the float minimum's order rules for -0)
+    const LvPass &ps = cps;
+    const int nl = cnl;
+    const int *items = citems, *start = cstart;
+    for (int it = 0; it < s.position_iterations; ++it) {
+        bool open = false;
+        for (int i = lane; i < n_islands; i += x.wl) open = open || !done[i];
+        if (!gballot(x, open)) break;
+        for (int l = 0; l < nl; ++l) {
+            for (int q = start[l] + lane; q < start[l + 1]; q += x.wl) {
+                const int e = items[q];
+                if (ps.is_joint(e)) {
+                    const int k = ps.row(e);
+                    const JRow &r = jr[k];
+                    if (!done[jisl[r.jid]]) okj[k] = joint_solve_position(r, bd, s);
+                } else {
+                    const int k = ps.row(e);
+                    const VCRow &c = vc[k];
+                    if (!done[cisl[c.slot]])
+                        sep[k] = contact_solve_position(c, bd, s.baumgarte, s.linear_slop, s.max_linear_correction,
+                                                        c.mA, c.mB, c.iA, c.iB);
+                }
+            }
+            gsync(x);
+        }
+        if (lane == 0) {
+            for (int i = 0; i < n_islands; ++i) minsep[i] = 0.0f, jok[i] = 1;
+            for (int k = 0; k < nc; ++k) {
+                const int i = cisl[vc[k].slot];
+                if (!done[i]) minsep[i] = bmin(minsep[i], sep[k]);
+            }
+            for (int k = 0; k < nj; ++k) {
+                const int i = jisl[jr[k].jid];
+                if (!done[i]) jok[i] = jok[i] && okj[k];
+            }
+            for (int i = 0; i < n_islands; ++i)
+                if (minsep[i] >= -3.0f * s.linear_slop && jok[i]) done[i] = 1;
+        }
+        gsync(x);
     }
 }
 
@@ -1453,7 +1716,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
     const int region = hot ? p.lay.hot_end + (rows ? p.lay.rows_bytes : 0) : 0;
     char *mine = dyn_smem + warp * region;
     Ctx x{p, p.m, p.s, s_world[warp], p.scratch + world * p.lay.stride, hot ? mine : nullptr,
-          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, p.step, 0, -1, clock64(), world, FULL, 0, 32};
+          rows ? mine + p.lay.hot_end : nullptr, (int)(threadIdx.x & 31), 0, p.step, 0, -1, -1, 0, clock64(), world, FULL, 0, 32};
     run_part<PART>(x);
     put_status(x, PART == 0 && p.step == 0);
 }
@@ -1516,7 +1779,7 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
     char *rows = hot && p.lay.rows_bytes ? hot + p.lay.hot_end : nullptr;
     if (active && (lane32 & (WL - 1)) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
-    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, 0, -1, clock64(), world,
+    Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, 0, -1, -1, 0, clock64(), world,
           WPW == 2 ? 0xffffu << (16 * half) : FULL, WL * half, WL};
     const float dt = p.dt;
     for (int k = 0; k < p.n_steps; ++k) {
@@ -1531,10 +1794,10 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
         IslandWork sw{};
         if (active) sw = solve_rows(x, dt, *w.inv_dt0 * dt, isl);
         step_sync();
-        if (active && x.lane == 0)
-            solve_constraints(p, world, sw,
-                              {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
-                               ap<int>(x, p.lay.jisl)});
+        if (active)
+            solve_constraints_levelled(x, sw,
+                                       {ap<int>(x, p.lay.isl), ap<int>(x, p.lay.bisl), ap<int>(x, p.lay.cisl),
+                                        ap<int>(x, p.lay.jisl)});
         step_sync();
         if (active) {
             GB_PHASE(x, 5);
