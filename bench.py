@@ -179,16 +179,18 @@ def cpu_baseline(sc, model, host, n_sample, threads=0, warmup=True):
     sample = map_state(lambda x: np.ascontiguousarray(np.asarray(x)[:n_sample]), host)
     lib = oracle_lib.load(build=False)
     threads = threads or lib.oracle_max_threads()
-    acts = actions_for(n_sample, CPU_SAMPLE_MAX_STEPS, 0)
+    na = len(sc.action_joints)
+    acts = actions_for(n_sample, CPU_SAMPLE_MAX_STEPS, 0) if na else None  # the workloads with action channels
     if warmup:  # one untimed step of a copy (thread pool start-up, first touches)
         warm = map_state(lambda x: np.array(x, copy=True), sample)
-        oracle_lib.step(model, warm, sc.settings, configs.DT, 1, threads=threads, actions=acts[0],
+        oracle_lib.step(model, warm, sc.settings, configs.DT, 1, threads=threads, actions=acts[0] if na else None,
                         action_joints=sc.action_joints, action_scale=sc.action_scale)
     t0 = time.perf_counter()
     st, steps = sample, 0
     while steps < CPU_SAMPLE_MAX_STEPS and (steps < 2 or time.perf_counter() - t0 < CPU_SAMPLE_SECONDS):
-        st = oracle_lib.step(model, st, sc.settings, configs.DT, 1, threads=threads, actions=acts[steps],
-                             action_joints=sc.action_joints, action_scale=sc.action_scale)
+        st = oracle_lib.step(model, st, sc.settings, configs.DT, 1, threads=threads,
+                             actions=acts[steps] if na else None, action_joints=sc.action_joints,
+                             action_scale=sc.action_scale)
         steps += 1
     dt = time.perf_counter() - t0
     return {"value": n_sample * steps / dt, "unit": UNIT, "cores": int(threads), "kind": "port", "steps": steps,

@@ -16,6 +16,7 @@ namespace gb {
 cudaError_t launch_steps(StepParams p, cudaStream_t stream);  // step.cu
 int kernels_per_step(int64_t n_worlds, int n_joints);         // step.cu
 int64_t launches_per_call(int64_t n_worlds, int n_joints, int n_steps);  // step.cu
+int hot_budget(int64_t n_worlds, int n_joints, int contact_capacity, int step_mode);  // step.cu
 cudaError_t launch_reset(const EnvParams &p, cudaStream_t s);    // env.cuh (compiled in step.cu)
 cudaError_t launch_observe(const EnvParams &p, cudaStream_t s);  // env.cuh
 cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s);  // env.cuh
@@ -59,7 +60,7 @@ const LeafSpec LEAVES[GOIB2D_NUM_LEAVES] = {
     {0, 0, 1}, {1, 3, 1}, {0, 3, 1}, {2, 3, 1}, {2, 3, 1}, {2, 3, 1}, {0, 3, 2}, {0, 3, 2}, {1, 4, 1}};
 
 // Per-world scratch arena: every array of the step's working set, 16-byte aligned, stride a multiple of 256 B.
-gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
+gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits, int hot_max = 6144) {
     gb::Layout L{};
     int64_t off = 0;
     auto take = [&](int64_t bytes) {
@@ -69,14 +70,12 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     };
     const int64_t b4 = 4 * (int64_t)(B > 0 ? B : 1), c4 = 4 * (int64_t)(C > 0 ? C : 1), j4 = 4 * (int64_t)(J > 0 ? J : 1);
     // the hot part first: the small arrays the sequential phases write and read back (see Layout::hot_end), the
-    // most used first, so that the prefix a kernel keeps in shared memory holds them when the whole part does not fit
-#ifndef GOIB2D_HOT_MAX_BYTES
-#define GOIB2D_HOT_MAX_BYTES 6144
-#endif
+    // most used first, so that the prefix a kernel keeps in shared memory (hot_max bytes at most) holds them when the
+    // whole part does not fit; the offsets do not depend on hot_max
     int64_t fits = 0;  // the largest array boundary within the shared-memory budget
     auto hot = [&](int64_t bytes) {
         int64_t o = take(bytes);
-        if (off <= GOIB2D_HOT_MAX_BYTES) fits = off;
+        if (off <= hot_max) fits = off;
         return o;
     };
     L.vx = hot(b4), L.vy = hot(b4), L.vw = hot(b4), L.cx = hot(b4), L.cy = hot(b4), L.ca = hot(b4);
@@ -106,13 +105,10 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits) {
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);
     // the step kernel's constraint rows in shared memory (after the hot part): the joint rows and the first
-    // contact rows, within a small budget, so that 7 blocks of 4 warps per SM keep most of the L1 cache
-#ifndef GOIB2D_ROWS_MAX_BYTES
-#define GOIB2D_ROWS_MAX_BYTES 1536
-#endif
+    // contact rows, within gb::ROWS_MAX_BYTES
     const int jbytes = (int)sizeof(gb::JRow) * J;
-    if (L.hot_end > 0 && jbytes <= GOIB2D_ROWS_MAX_BYTES) {
-        int cap = (GOIB2D_ROWS_MAX_BYTES - jbytes) / (int)sizeof(gb::VCRow);
+    if (L.hot_end > 0 && jbytes <= gb::ROWS_MAX_BYTES) {
+        int cap = (gb::ROWS_MAX_BYTES - jbytes) / (int)sizeof(gb::VCRow);
         cap = cap < C ? cap : C;
         L.sm_jr = 0, L.sm_vc = jbytes, L.sm_vc_cap = cap;
         L.rows_bytes = (jbytes + (int)sizeof(gb::VCRow) * cap + 15) & ~15;
@@ -470,7 +466,8 @@ int goib2d_step_seq(goib2d_model *m, const goib2d_settings *s, float dt, int32_t
     for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
     p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
     p.step_mode = m->step_mode;
-    p.lay = scratch_layout(dm->B, C, dm->J, dm->P, dm->grid ? dm->max_hits : 0);
+    p.lay = scratch_layout(dm->B, C, dm->J, dm->P, dm->grid ? dm->max_hits : 0,
+                           gb::hot_budget(n_worlds, dm->J, C, m->step_mode));
     size_t need = (size_t)p.lay.stride * (size_t)n_worlds;
     if (need > m->scratch_bytes) {
         if (m->scratch) cudaFree(m->scratch), m->scratch = nullptr, m->scratch_bytes = 0;

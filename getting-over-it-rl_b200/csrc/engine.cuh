@@ -177,6 +177,10 @@ struct PairScene {
     int n_no_collide;
 };
 
+// The step kernel's per-world shared-memory region for constraint rows (Layout::rows_bytes at most): the joint rows and
+// the first contact rows of the island solve, within a small budget that leaves most of the L1 cache.
+constexpr int ROWS_MAX_BYTES = 1536;
+
 // Status bits (include/goib2d.h goib2d_status)
 enum { ST_OVERFLOW = 1, ST_NONFINITE = 2, ST_CAP = 4, ST_LIMIT = 8 };
 

@@ -356,9 +356,15 @@ __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int ji
     bool use22 = soft || revz.z == 0;
     V3 wmx = use22 ? i22x : symx, wmy = use22 ? i22y : symy, wmz = use22 ? i22z : symz;
     if (soft) wmz.z = ezz_soft;
-    const V3 Kx = is_rev ? revx : is_pri ? prx : wmx;
-    const V3 Ky = is_rev ? revy : is_pri ? pry : wmy;
-    const V3 Kz = is_rev ? revz : is_pri ? prz : wmz;
+    const bool is_mot = type == MOTOR;
+    const V3 Kx = is_rev || is_mot ? revx : is_pri ? prx : wmx;
+    const V3 Ky = is_rev || is_mot ? revy : is_pri ? pry : wmy;
+    const V3 Kz = is_rev || is_mot ? revz : is_pri ? prz : wmz;
+    // the motor joint's position errors (b2MotorJoint::InitVelocityConstraints): linear offset = (lower, upper),
+    // angular offset = motor_speed in the joint row (see motor_velocity)
+    const V2 mro = rot(qA, V2{lower, upper});
+    const V2 mot_err{(((cB.x + rB.x) - cA.x) - rA.x) - mro.x, (((cB.y + rB.y) - cA.y) - rA.y) - mro.y};
+    const float mot_ang = (aB - aA) - motor_speed;
     const int limit_state = is_rev ? rev_state : is_pri ? pri_state : INACTIVE_LIMIT;
     bool zero_z = is_rev ? (v24 ? false : rev_zero_z) : is_pri ? pri_zero_z : false;
     if (zero_z) iz = 0.0f;
@@ -395,6 +401,12 @@ __device__ __noinline__ void prepare_joint(const DevModel &m, const W &w, int ji
     r.ax = ax, r.pe = pe, r.a1 = a1, r.a2 = a2, r.s1 = s1, r.s2 = s2;
     r.soft = soft, r.gamma = soft ? gamma : 0.0f, r.bias = soft ? bias : 0.0f, r.angle = angle;
     r.lower = lower, r.upper = upper;
+    if (is_mot) {
+        r.ax = mot_err, r.angle = mot_ang, r.motor_mass = rev_mm;
+        r.gamma = dt * frequency;  // the linear impulse's limit, h * max force
+        r.bias = damping;          // the correction factor
+        r.soft = false;
+    }
 }
 
 __device__ __forceinline__ void joint_warm_start(const JRow &r, const Bodies &bd, bool v24) {  // joints.py:202-248
@@ -598,6 +610,42 @@ __device__ __forceinline__ void weld_velocity(JRow &r, V2 &vA, float &wA, V2 &vB
     }
 }
 
+// b2MotorJoint::SolveVelocityConstraints, Box2D 2.3.1's motor joint (the reference engine has none; this follows the
+// published method): the angular impulse toward the angular offset, clamped to h * max torque, then the linear
+// impulse toward the linear offset through the 2x2 point mass, its length clamped to h * max force; both drive the
+// position errors of the step's start, scaled by correction factor / h. Row fields: ax = linear error, angle =
+// angular error, bias = correction factor, max_impulse = h * max torque, gamma = h * max force, imp = (linear x,
+// linear y, angular). The same operations as the oracle's motor_velocity.
+__device__ __forceinline__ void motor_velocity(JRow &r, V2 &vA, float &wA, V2 &vB, float &wB) {
+    const float mA = r.mA, mB = r.mB, iA = r.iA, iB = r.iB;
+    const float k = r.inv_dt * r.bias;
+    {
+        const float cdot = (wB - wA) + k * r.angle;
+        float impulse = -r.motor_mass * cdot;
+        const float old = r.imp[2];
+        const float ni = clampf(old + impulse, -r.max_impulse, r.max_impulse);
+        impulse = ni - old;
+        wA = wA - iA * impulse, wB = wB + iB * impulse;
+        r.imp[2] = ni;
+    }
+    const V2 d = dvel(vB, wB, r.rB, vA, wA, r.rA);
+    const float cx = d.x + k * r.ax.x, cy = d.y + k * r.ax.y;
+    const V2 sv = solve22d(r.Kx.x, r.Ky.x, r.Kx.y, r.Ky.y, cx, cy, r.d22);
+    const float ox = r.imp[0], oy = r.imp[1];
+    float nx = ox - sv.x, ny = oy - sv.y;
+    const float max_f = r.gamma;
+    if (nx * nx + ny * ny > max_f * max_f) {
+        const V2 u = normalize(V2{nx, ny});
+        nx = u.x * max_f, ny = u.y * max_f;
+    }
+    const float jx = nx - ox, jy = ny - oy;
+    vA = {vA.x - mA * jx, vA.y - mA * jy};
+    wA = wA - iA * cross(r.rA, V2{jx, jy});
+    vB = {vB.x + mB * jx, vB.y + mB * jy};
+    wB = wB + iB * cross(r.rB, V2{jx, jy});
+    r.imp[0] = nx, r.imp[1] = ny;
+}
+
 __device__ __forceinline__ void joint_solve_velocity(JRow &r, const Bodies &bd, bool v24) {  // joints.py:440-459
     V2 vA{bd.vx[r.ia], bd.vy[r.ia]}, vB{bd.vx[r.ib], bd.vy[r.ib]};
     float wA = bd.vw[r.ia], wB = bd.vw[r.ib];
@@ -608,6 +656,8 @@ __device__ __forceinline__ void joint_solve_velocity(JRow &r, const Bodies &bd, 
             rev_velocity(r, vA, wA, vB, wB);
     } else if (r.type == PRISMATIC) {
         pri_velocity(r, vA, wA, vB, wB);
+    } else if (r.type == MOTOR) {
+        motor_velocity(r, vA, wA, vB, wB);
     } else {
         weld_velocity(r, vA, wA, vB, wB);
     }
@@ -637,6 +687,7 @@ __device__ __forceinline__ bool rev_point_position(const JRow &r, const Bodies &
 }
 
 __device__ __forceinline__ bool joint_solve_position(const JRow &r, const Bodies &bd, const goib2d_settings &s) {
+    if (r.type == MOTOR) return true;  // b2MotorJoint::SolvePositionConstraints corrects nothing
     V2 cA{bd.cx[r.ia], bd.cy[r.ia]}, cB{bd.cx[r.ib], bd.cy[r.ib]};
     float aA = bd.ca[r.ia], aB = bd.ca[r.ib];
     const float mA = r.mA, mB = r.mB, iA = r.iA, iB = r.iB;

@@ -1894,6 +1894,34 @@ bool step_pairs(int64_t n_worlds, int sms, int contact_capacity) {
     return n_worlds > (int64_t)PAIR_MIN_PER_SM * sms && contact_capacity <= PAIR_MAX_CONTACTS;
 }
 
+// The one-launch step's block for a batch: warps, worlds per warp (2 when paired), before the shared-memory cap - one
+// block per SM where the batch allows.
+struct BlockShape {
+    int warps, wpw;
+};
+BlockShape block_shape(int64_t n, int sms, int contact_capacity, int step_mode) {
+    const int per_sm = (int)((n + sms - 1) / sms);
+    const bool pair = step_mode ? step_mode == 2 : step_pairs(n, sms, contact_capacity);
+    const int wpw = pair ? 2 : 1, max_warps = pair ? PAIR_MAX_WARPS : STEP_MAX_WARPS;
+    int warps = (per_sm + wpw - 1) / wpw;
+    warps = warps < 1 ? 1 : (warps > max_warps ? max_warps : warps);
+    return {warps, wpw};
+}
+// Shared memory per world for the arena's hot part (Layout::hot_end): what a block's share per world leaves after the
+// bound State and the rows region, at least HOT_MIN_BYTES (the part kernels' fixed budget) and at most HOT_MAX_BYTES.
+// A block of few, large worlds (c2: 7 worlds of 257 bodies) keeps their body arrays in shared memory.
+constexpr int HOT_MIN_BYTES = 6144, HOT_MAX_BYTES = 65536;
+int hot_budget(int64_t n_worlds, int n_joints, int contact_capacity, int step_mode) {
+    if (n_worlds <= 0 || part_kernels(n_worlds, n_joints)) return HOT_MIN_BYTES;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) return HOT_MIN_BYTES;
+    const BlockShape b = block_shape(n_worlds, sms, contact_capacity, step_mode);
+    const int per_world = STEP_MAX_SMEM / (b.warps * b.wpw) - (int)((sizeof(W) + 15) & ~size_t(15)) - ROWS_MAX_BYTES;
+    return per_world < HOT_MIN_BYTES ? HOT_MIN_BYTES : per_world > HOT_MAX_BYTES ? HOT_MAX_BYTES : per_world;
+}
+
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     p.world0 = 0, p.world_end = p.n_worlds;
     const int64_t n = p.n_worlds;
@@ -1902,15 +1930,10 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const int region = step_region(p.lay);
-#ifndef GOIB2D_BLOCKS_PER_SM
-#define GOIB2D_BLOCKS_PER_SM 1
-#endif
-        // worlds per block: GOIB2D_BLOCKS_PER_SM blocks per SM where the batch allows
-        int per_sm = (int)((n + (int64_t)sms * GOIB2D_BLOCKS_PER_SM - 1) / ((int64_t)sms * GOIB2D_BLOCKS_PER_SM));
-        const bool pair = p.step_mode ? p.step_mode == 2 : step_pairs(n, sms, p.C);
-        const int wpw = pair ? 2 : 1, max_warps = pair ? PAIR_MAX_WARPS : STEP_MAX_WARPS;
-        int warps = (per_sm + wpw - 1) / wpw;
-        warps = warps < 1 ? 1 : (warps > max_warps ? max_warps : warps);
+        const BlockShape shape = block_shape(n, sms, p.C, p.step_mode);
+        const bool pair = shape.wpw == 2;
+        const int wpw = shape.wpw;
+        int warps = shape.warps;
         const int fit = STEP_MAX_SMEM / (wpw * region);
         warps = warps > fit ? fit : warps;
         const size_t smem = (size_t)wpw * warps * region;

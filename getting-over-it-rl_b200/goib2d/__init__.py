@@ -16,8 +16,8 @@ CPU path behind it.
 import numpy as np
 
 from .settings import Settings
-from .world import (DYNAMIC, KINEMATIC, PRISMATIC, REVOLUTE, STATIC, WELD, Model, State, WorldDef, compact_model,
-                    compact_state, expand_state)
+from .world import (DYNAMIC, KINEMATIC, MOTOR, PRISMATIC, REVOLUTE, STATIC, WELD, Model, State, WorldDef,
+                    compact_model, compact_state, expand_state)
 
 GAME_DT = np.float32(0.008333334)  # Time.fixedDeltaTime as float32 (reference __init__.py:68)
 
@@ -31,5 +31,5 @@ def __getattr__(name):
 
 
 __all__ = ["Settings", "WorldDef", "Model", "State", "step", "step_", "GAME_DT", "STATIC", "KINEMATIC", "DYNAMIC",
-           "REVOLUTE", "PRISMATIC", "WELD", "compact_model", "compact_state", "expand_state", "to_device", "to_host",
+           "REVOLUTE", "PRISMATIC", "WELD", "MOTOR", "compact_model", "compact_state", "expand_state", "to_device", "to_host",
            "broadcast", "Engine"]

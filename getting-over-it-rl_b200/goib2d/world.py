@@ -22,6 +22,7 @@ from .settings import MAX_POLYGON_VERTICES, Settings
 F32, I32 = np.float32, np.int32
 STATIC, KINEMATIC, DYNAMIC = 0, 1, 2  # b2BodyType
 REVOLUTE, PRISMATIC, WELD = 1, 2, 8  # b2JointType
+MOTOR = 11  # b2JointType e_motorJoint: this package's addition (the reference engine has no motor joint)
 INACTIVE_LIMIT, AT_LOWER, AT_UPPER, EQUAL_LIMITS = 0, 1, 2, 3  # b2LimitState
 CIRCLES, FACE_A, FACE_B = 0, 1, 2  # b2Manifold::Type
 
@@ -375,6 +376,20 @@ class WorldDef:
                                axis=(1, 0), enable_limit=False, lower=0.0, upper=0.0, motor_speed=0.0,
                                max_motor=0.0, enable_motor=False, frequency=frequency, damping=damping,
                                collide=collide)
+
+    def add_motor(self, body_a, body_b, linear_offset=(0, 0), angular_offset=0.0, *, max_force=1.0, max_torque=1.0,
+                  correction_factor=0.3, collide=False):
+        """Box2D 2.3.1's b2MotorJoint (not in the reference engine; parity with it cannot be pinned): drives body B
+        toward linear_offset (in body A's frame, from A's origin to B's origin) and angular_offset (B's angle minus
+        A's) with impulses limited to max_force and max_torque per second, correcting correction_factor of the error
+        per step. The joint row of the State carries its parameters, so that each world (and the action channels,
+        which write motor_speed) can set its own targets: lower / upper = the linear offset's x / y, motor_speed =
+        the angular offset, max_motor = max torque, frequency = max force, damping = the correction factor;
+        impulse = (linear x, linear y, angular)."""
+        return self._add_joint(type=MOTOR, a=body_a, b=body_b, la=(0, 0), lb=(0, 0), ref=0.0, axis=(1, 0),
+                               enable_limit=False, lower=float(linear_offset[0]), upper=float(linear_offset[1]),
+                               motor_speed=float(angular_offset), max_motor=max_torque, enable_motor=False,
+                               frequency=max_force, damping=correction_factor, collide=collide)
 
     # ---- build
 

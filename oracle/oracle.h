@@ -25,7 +25,7 @@ constexpr float AABB_EXT = 0.1f, AABB_MUL = 2.0f;
 constexpr int MAX_SUB_STEPS = 8, MAX_TOI_CONTACTS = 32;
 constexpr float MAX_COND = 1000.0f, K_TOL = 0.1f;
 enum { STATIC = 0, KINEMATIC = 1, DYNAMIC = 2 };
-enum { REVOLUTE = 1, PRISMATIC = 2, WELD = 8 };
+enum { REVOLUTE = 1, PRISMATIC = 2, WELD = 8, MOTOR = 11 };  // b2JointType (MOTOR: no counterpart in the reference engine)
 enum { INACTIVE_LIMIT = 0, AT_LOWER = 1, AT_UPPER = 2, EQUAL_LIMITS = 3 };
 enum { CIRCLES = 0, FACE_A = 1, FACE_B = 2 };
 enum { CIRCLE = 0, EDGE = 1, POLYGON = 2 };

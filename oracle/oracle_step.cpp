@@ -588,7 +588,8 @@ static void prepare_joints(const Model &m, const World &w, const std::vector<int
         V3 wmx = use22 ? i22x : symx, wmy = use22 ? i22y : symy, wmz = use22 ? i22z : symz;
         if (soft) wmz.z = ezz_soft;
         float w_gamma = soft ? gamma : 0.0f, w_bias = soft ? bias : 0.0f;
-        if (is_rev)
+        const bool is_mot = r.type == MOTOR;
+        if (is_rev || is_mot)
             r.Kx = revx, r.Ky = revy, r.Kz = revz;
         else if (is_pri)
             r.Kx = prx, r.Ky = pry, r.Kz = prz;
@@ -615,6 +616,16 @@ static void prepare_joints(const Model &m, const World &w, const std::vector<int
         r.ax = ax, r.pe = pe, r.a1 = a1, r.a2 = a2, r.s1 = s1, r.s2 = s2;
         r.soft = soft, r.gamma = w_gamma, r.bias = w_bias, r.angle = angle;
         r.lower = lower, r.upper = upper;
+        if (is_mot) {  // b2MotorJoint::InitVelocityConstraints; the joint row holds its parameters (see motor_velocity)
+            const float lin_x = lower, lin_y = upper, ang_off = w.motor_speed[jid];
+            const V2 ro = rot(qA, V2{lin_x, lin_y});
+            r.ax = {(((cB.x + rB.x) - cA.x) - rA.x) - ro.x, (((cB.y + rB.y) - cA.y) - rA.y) - ro.y};
+            r.angle = (aB - aA) - ang_off;
+            r.motor_mass = rev_mm;
+            r.gamma = dt * w.frequency[jid];  // the linear impulse's limit, h * max force
+            r.bias = w.damping[jid];          // the correction factor
+            r.soft = false;
+        }
     }
 }
 
@@ -838,6 +849,43 @@ static void weld_velocity(JR &r, V2 &vA, float &wA, V2 &vB, float &wB) {  // joi
     }
 }
 
+// b2MotorJoint::SolveVelocityConstraints, Box2D 2.3.1's motor joint (the reference engine has none; this follows the
+// published method): the angular impulse toward the angular offset, clamped to h * max torque, then the linear
+// impulse toward the linear offset through the 2x2 point mass, its length clamped to h * max force; both drive the
+// position errors of the step's start, scaled by correction factor / h. Row fields: ax = linear error, angle =
+// angular error, bias = correction factor, max_impulse = h * max torque, gamma = h * max force, imp = (linear x,
+// linear y, angular).
+static void motor_velocity(JR &r, V2 &vA, float &wA, V2 &vB, float &wB) {
+    const float mA = r.mA, mB = r.mB, iA = r.iA, iB = r.iB;
+    const float k = r.inv_dt * r.bias;
+    {
+        const float cdot = (wB - wA) + k * r.angle;
+        float impulse = -r.motor_mass * cdot;
+        const float old = r.imp[2];
+        const float ni = clampf(old + impulse, -r.max_impulse, r.max_impulse);
+        impulse = ni - old;
+        wA = wA - iA * impulse, wB = wB + iB * impulse;
+        r.imp[2] = ni;
+    }
+    const V2 b = cross_sv(wB, r.rB), a = cross_sv(wA, r.rA);
+    const float dx = ((vB.x + b.x) - vA.x) - a.x, dy = ((vB.y + b.y) - vA.y) - a.y;
+    const float cx = dx + k * r.ax.x, cy = dy + k * r.ax.y;
+    const V2 sv = solve22(r.Kx.x, r.Ky.x, r.Kx.y, r.Ky.y, cx, cy);
+    const float ox = r.imp[0], oy = r.imp[1];
+    float nx = ox - sv.x, ny = oy - sv.y;
+    const float max_f = r.gamma;
+    if (nx * nx + ny * ny > max_f * max_f) {
+        const V2 u = normalize(V2{nx, ny});
+        nx = u.x * max_f, ny = u.y * max_f;
+    }
+    const float jx = nx - ox, jy = ny - oy;
+    vA = {vA.x - mA * jx, vA.y - mA * jy};
+    wA = wA - iA * cross(r.rA, V2{jx, jy});
+    vB = {vB.x + mB * jx, vB.y + mB * jy};
+    wB = wB + iB * cross(r.rB, V2{jx, jy});
+    r.imp[0] = nx, r.imp[1] = ny;
+}
+
 static void joint_solve_velocity(std::vector<JR> &rows, Vel &vel, bool v24) {  // joints.py:440-459
     for (JR &r : rows) {
         V2 vA{vel.vx[r.ia], vel.vy[r.ia]}, vB{vel.vx[r.ib], vel.vy[r.ib]};
@@ -849,6 +897,8 @@ static void joint_solve_velocity(std::vector<JR> &rows, Vel &vel, bool v24) {  /
                 rev_velocity(r, vA, wA, vB, wB);
         } else if (r.type == PRISMATIC) {
             pri_velocity(r, vA, wA, vB, wB);
+        } else if (r.type == MOTOR) {
+            motor_velocity(r, vA, wA, vB, wB);
         } else {
             weld_velocity(r, vA, wA, vB, wB);
         }
@@ -997,6 +1047,7 @@ static bool weld_position(const JR &r, V2 &cA, float &aA, V2 &cB, float &aB, con
 }
 
 static bool joint_solve_position(const JR &r, Pos &pos, const goib2d_settings &s) {  // joints.py:598-606
+    if (r.type == MOTOR) return true;  // b2MotorJoint::SolvePositionConstraints corrects nothing
     V2 cA{pos.cx[r.ia], pos.cy[r.ia]}, cB{pos.cx[r.ib], pos.cy[r.ib]};
     float aA = pos.a[r.ia], aB = pos.a[r.ib];
     bool ok;

@@ -63,6 +63,9 @@ def step(model, state, settings, dt, n_steps=1, threads=0, actions=None, action_
         na = actions.shape[1]
         aj = np.ascontiguousarray(action_joints, np.int32)
         asc = np.ascontiguousarray(action_scale, np.float32)
+        if actions.shape[0] != N or aj.shape != (na,) or asc.shape != (na,):
+            raise ValueError(f"actions {actions.shape} for {N} worlds need {na} action joints and scales, got "
+                             f"{aj.shape[0]} and {asc.shape[0]}")
         act, aj_p, asc_p = actions.ctypes.data, aj.ctypes.data, asc.ctypes.data
     else:
         aj_p = asc_p = None

@@ -53,3 +53,13 @@ def test_model_create_rejects_bad_descriptors_without_a_gpu():
     h = ctypes.c_void_p()
     assert lib.goib2d_model_create(ctypes.byref(d), ctypes.byref(h)) == -1
     assert b"negative" in lib.goib2d_last_error()
+
+
+def test_settings_struct_is_25_words():
+    """The FFI binding passes goib2d_settings as its 25 32-bit words; the struct must stay that."""
+    import numpy as np
+    from goib2d.settings import Settings, SettingsC, settings_struct
+    assert ctypes.sizeof(SettingsC) == 25 * 4
+    words = np.frombuffer(bytes(settings_struct(Settings.game())), np.int32)
+    back = SettingsC.from_buffer_copy(words.tobytes())
+    assert back.velocity_iterations == 300 and back.position_iterations == 30 and back.continuous_physics == 1
