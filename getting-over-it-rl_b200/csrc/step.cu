@@ -1871,7 +1871,10 @@ namespace gb {
 // the same code in the same order within a world, so results are identical. Measured: c4 (22 joints, 65536
 // worlds) 11.1 M world-steps/s as part kernels, 9.1 M as one launch; c1 (2 joints, 16384 worlds) 21.1 M as part
 // kernels, 23.2 M as one launch.
-constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = 16384;
+#ifndef GOIB2D_THREAD_SWEEPS_MIN_WORLDS
+#define GOIB2D_THREAD_SWEEPS_MIN_WORLDS 16384
+#endif
+constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = GOIB2D_THREAD_SWEEPS_MIN_WORLDS;
 constexpr int THREAD_SWEEPS_MIN_JOINTS = 8;
 bool part_kernels(int64_t n_worlds, int n_joints) {
     return n_worlds >= THREAD_SWEEPS_MIN_WORLDS && n_joints >= THREAD_SWEEPS_MIN_JOINTS;
