@@ -287,6 +287,9 @@ __device__ void find_new_contacts(Ctx &x, const int *moved = nullptr) {
     W &w = x.w;
     const int P = m.P, C = w.C, lane = x.lane;
     if (P == 0) return;
+#ifdef GOIB2D_PHASE_TIMERS
+    const long long fnc_t0 = clock64();
+#endif
     uint32_t *bitmap = ap<uint32_t>(x, x.p.lay.bitmap);
     int *freeslot = ap<int>(x, x.p.lay.freeslot);
     const int nw = (P + 31) >> 5;
@@ -306,6 +309,10 @@ __device__ void find_new_contacts(Ctx &x, const int *moved = nullptr) {
     }
     const int key0 = *w.next_key;
     gsync(x);
+#ifdef GOIB2D_PHASE_TIMERS
+    const long long fnc_t1 = clock64();
+    if (lane == 0) atomicAdd(&g_toi_cycles[9], (unsigned long long)(fnc_t1 - fnc_t0));
+#endif
     int n_new = -1;
     if (m.grid) {
         int *hits = ap<int>(x, x.p.lay.hits), *sorted = hits + m.max_hits;
@@ -340,6 +347,9 @@ __device__ void find_new_contacts(Ctx &x, const int *moved = nullptr) {
         *w.overflow += n_new - placed;
         if (n_new > placed) x.status |= ST_OVERFLOW;
     }
+#ifdef GOIB2D_PHASE_TIMERS
+    if (lane == 0) atomicAdd(&g_toi_cycles[8], (unsigned long long)(clock64() - fnc_t0)), atomicAdd(&g_toi_cycles[10], 1ull);
+#endif
     x.fnc_clean = n_new <= n_free;  // both are the same on every lane of the world
     if (n_new > 0 && n_free > 0) x.order_n = -1;  // contacts were placed
     gsync(x);

@@ -108,3 +108,59 @@ def test_edge_worlds_are_independent_in_a_batch():
         for a, b in zip(oracle_lib.state_leaves(map_state(lambda x: np.asarray(x)[i], out)),
                         oracle_lib.state_leaves(one)):
             assert np.array_equal(np.asarray(a), np.asarray(b))
+
+
+def _world_normals(st, box):
+    """The world-frame normals (from the static edge to the box) of the box's touching contacts."""
+    from goib2d.world import FACE_A
+    out = []
+    for s in range(st.contacts.pair.shape[0]):
+        if st.contacts.pair[s] < 0 or not st.contacts.touching[s] or st.contacts.count[s] == 0:
+            continue
+        n = np.asarray(st.contacts.local_normal[s], np.float64)
+        if int(st.contacts.mtype[s]) == FACE_A:  # the edge (body 0, identity transform) holds the reference face
+            out.append(n)
+        else:  # the box's face: rotate into the world and flip (the normal points from the edge to the box)
+            c, sn = float(st.bodies.xf_q[box][0]), float(st.bodies.xf_q[box][1])
+            out.append(-np.array([c * n[0] - sn * n[1], sn * n[0] + c * n[1]]))
+    return out
+
+
+def _settle(verts, pos, angle=0.0, steps=300, friction=0.8):
+    from goib2d.settings import Settings
+    from goib2d.world import DYNAMIC, STATIC, WorldDef
+    d = WorldDef(Settings.stock())
+    g = d.add_body(STATIC)
+    d.add_chain(g, verts, friction=friction)
+    b = d.add_body(DYNAMIC, pos, angle, mass=1.0, inertia=1.0 / 24.0)
+    d.add_box(b, (0.25, 0.25), friction=friction)
+    model, st = d.build(16)
+    for _ in range(steps):
+        st = oracle_lib.step(model, st, d.settings, edge_scenes.DT, 1)
+    return st
+
+
+def test_box_in_a_concave_chain_vertex_takes_both_face_normals():
+    """Known answer: a box at rest in a 90-degree V of a chain touches both walls, and every contact normal is a wall's
+    face normal (perpendicular to its segment, pointing into the V) - the concave vertex admits no other normal."""
+    st = _settle([(-3.0, 3.0), (0.0, 0.0), (3.0, 3.0)], (0.05, 1.5), angle=0.7853982)
+    assert np.abs(st.bodies.v[1]).max() < 1e-3 and abs(float(st.bodies.w[1])) < 1e-3
+    ns = _world_normals(st, 1)
+    r = 1.0 / np.sqrt(2.0)
+    walls = [np.array([r, r]), np.array([-r, r])]  # left wall's normal (into the V) and the right wall's
+    hit = [min(range(2), key=lambda k: np.abs(n - walls[k]).max()) for n in ns]
+    assert set(hit) == {0, 1}, ns
+    for n, k in zip(ns, hit):
+        assert np.abs(n - walls[k]).max() < 1e-6, (n, walls[k])
+
+
+def test_box_over_a_convex_chain_vertex_keeps_the_flat_normal():
+    """Known answer: a box resting on the flat part of a chain with a corner past a convex vertex (the ground falls
+    away beyond it) keeps the flat segment's normal (0, 1) at every contact and does not tip: the ghost vertex
+    excludes the vertex normals a lone edge would produce."""
+    st = _settle([(-3.0, 0.0), (0.0, 0.0), (2.0, -2.0)], (-0.1, 0.27))
+    assert abs(float(st.bodies.a[1])) < 1e-4 and np.abs(st.bodies.v[1]).max() < 1e-3
+    ns = _world_normals(st, 1)
+    # (0, 1) up to the box's own resting tilt (a few 1e-6 rad) where its face is the reference; a vertex normal at
+    # this corner would lean towards the slope's normal (0.71, 0.71)
+    assert ns and all(np.abs(n - np.array([0.0, 1.0])).max() < 1e-4 for n in ns), ns
