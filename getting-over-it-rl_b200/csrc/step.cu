@@ -1,13 +1,15 @@
-// goib2d: the batched b2World::Step for sm_100a. One warp per world; a step is one launch (goib2d_step_kernel), or
-// for batches of 16384 worlds and more a sequence of part kernels.
+// goib2d: the batched b2World::Step for sm_100a. One warp (or half-warp) per world; every step of a call runs in one
+// persistent launch (goib2d_step_kernel / goib2d_step_pair_kernel), or, for batches of 16384 worlds and more of
+// joint-heavy models, as a sequence of part kernels per step.
 //
 // Mapping. Each world's State is a row of every leaf (contiguous per world), so a warp reads and writes its own
-// world with unit-stride lane accesses. Data-parallel phases run one element per lane: the candidate-pair scan
-// (ballot-compacted in candidate order), the narrow phase over contact slots, constraint set-up, integration, fixture
-// synchronisation and b2TimeOfImpact over the TOI candidates. The phases whose order defines the floats - Collide's
-// wake walk, the island DFS, the Gauss-Seidel velocity / position sweeps and the TOI island walk - run on lane 0 in
-// exactly the reference's order (goi_jax/box2d/step.py, island.py, pairs.py, toi.py), so results are bit-identical
-// to it. Per-world working arrays live in a scratch arena (L1/L2-resident), laid out by scratch_layout().
+// world with unit-stride lane accesses. Data-parallel phases run one element per lane: the candidate-pair queries
+// (ballot-compacted), the narrow phase over contact slots, constraint set-up, integration, fixture synchronisation,
+// b2TimeOfImpact over the TOI candidates and the levelled island sweeps. The phases whose order defines the floats -
+// Collide's wake walk, the island DFS, the Gauss-Seidel sweeps of small islands and the TOI island walk - run on
+// lane 0 in exactly the reference's order (goi_jax/box2d/step.py, island.py, pairs.py, toi.py), or are restructured
+// so that every float is computed from the same inputs in the same order, so results are bit-identical to it.
+// Per-world working arrays live in a scratch arena (its hot part in shared memory), laid out by scratch_layout().
 #include <climits>
 #include <cstdio>
 #include <mutex>
@@ -1753,12 +1755,6 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
 //   (goib2d_step_kernel, 28 warps of 72 registers) serves the other batches (launch_steps chooses).
 // Per world in dynamic shared memory: the bound State, the arena's hot part and the rows region. A group of lanes
 // without a world (the batch's tail) runs no phase but meets every barrier, so all threads reach every step_sync.
-// The block's threads also meet between one step and the next: without that barrier a world that finished its
-// TOI phase starts the next step's collide while a TOI event chain runs in another warp, and the two phases' code
-// evicts each other from the instruction cache (c1, steps 50-1000: 18.2 M world-steps/s with it, 17.1 M without).
-#ifndef GOIB2D_STEP_BARRIER
-#define GOIB2D_STEP_BARRIER 1
-#endif
 constexpr int STEP_MAX_WARPS = 28;       // one world per warp: 72 registers per thread
 constexpr int PAIR_MAX_WARPS = 16;       // two worlds per warp: 128 registers per thread
 constexpr int STEP_MAX_SMEM = 232448;    // dynamic shared memory per block
@@ -1766,14 +1762,9 @@ __host__ __device__ __forceinline__ int step_region(const Layout &L) {
     return (int)((sizeof(W) + 15) & ~size_t(15)) + L.hot_end + (L.hot_end > 0 ? L.rows_bytes : 0);
 }
 // the warp reconverges (all its lanes are at this same call), then the block's threads meet
-#ifndef GOIB2D_PHASE_BARRIERS
-#define GOIB2D_PHASE_BARRIERS 1
-#endif
 __device__ __forceinline__ void step_sync() {
-#if GOIB2D_PHASE_BARRIERS
     __syncwarp();
     __syncthreads();
-#endif
 }
 template <int WPW>
 __device__ __forceinline__ void whole_step(const StepParams &p) {
@@ -1819,9 +1810,11 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
             run_part<5>(x);
             put_status(x, k == 0);
         }
-#if GOIB2D_STEP_BARRIER
+        // the block's threads also meet between one step and the next: without this barrier a world that finished
+        // its TOI phase starts the next step's collide while a TOI event chain runs in another warp, and the two
+        // phases' code evicts each other from the instruction cache (c1, steps 50-1000: 18.2 M world-steps/s with
+        // it, 17.1 M without)
         step_sync();
-#endif
     }
 }
 
@@ -1878,13 +1871,10 @@ namespace gb {
 // Batches of at least THREAD_SWEEPS_MIN_WORLDS worlds whose model has at least THREAD_SWEEPS_MIN_JOINTS joints run
 // a step as six part kernels with the constraint sweeps one world per THREAD (goib2d_constraints_kernel): 32
 // worlds' long sequential joint sweeps share one warp instruction. Everything else is the one-launch step. Both run
-// the same code in the same order within a world, so results are identical. Measured: c4 (22 joints, 65536
-// worlds) 11.1 M world-steps/s as part kernels, 9.1 M as one launch; c1 (2 joints, 16384 worlds) 21.1 M as part
-// kernels, 23.2 M as one launch.
-#ifndef GOIB2D_THREAD_SWEEPS_MIN_WORLDS
-#define GOIB2D_THREAD_SWEEPS_MIN_WORLDS 16384
-#endif
-constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = GOIB2D_THREAD_SWEEPS_MIN_WORLDS;
+// the same code in the same order within a world, so results are identical. Measured with calls of 10 steps over
+// the first 300 steps of c4's episode: 65536 worlds 12.7 M world-steps/s as part kernels, 9.3 M as one persistent
+// launch; 16384 worlds 7.8-17.6 M and 7.1-16.2 M per 50-step window.
+constexpr int64_t THREAD_SWEEPS_MIN_WORLDS = 16384;
 constexpr int THREAD_SWEEPS_MIN_JOINTS = 8;
 bool part_kernels(int64_t n_worlds, int n_joints) {
     return n_worlds >= THREAD_SWEEPS_MIN_WORLDS && n_joints >= THREAD_SWEEPS_MIN_JOINTS;
