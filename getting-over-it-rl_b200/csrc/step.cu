@@ -953,7 +953,7 @@ __device__ __forceinline__ bool lv_minus_zero(const Ctx &x, const Bodies &bd) {
 
 // solve_constraints with the passes levelled over the world's lanes: the same results, bit for bit (every lane of
 // the world calls it). Islands below LV_MIN_CONSTRAINTS constraints, and those whose velocity pass has fewer than
-// two constraints per level on average (a joint chain), run sequentially on lane 0.
+// ~1.1 constraints per level on average (a joint chain: nothing to share out), run sequentially on lane 0.
 __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const IslandIds &ids) {
     const StepParams &p = x.p;
     const goib2d_settings &s = x.s;
@@ -967,7 +967,7 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
     bool seq = nc + nj < LV_MIN_CONSTRAINTS || lv_minus_zero(x, sw.bd);
     if (!seq) {
         vnl = lv_levels(x, sw, vps, level, vitems, vstart, cur, last);
-        seq = 2 * vnl > nc + nj;
+        seq = 10 * vnl > 9 * (nc + nj);
     }
     if (seq) {
         if (lane == 0) solve_constraints(p, x.world, sw, ids);
@@ -1756,6 +1756,7 @@ __device__ __forceinline__ void step_part(const StepParams &p) {
 // Per world in dynamic shared memory: the bound State, the arena's hot part and the rows region. A group of lanes
 // without a world (the batch's tail) runs no phase but meets every barrier, so all threads reach every step_sync.
 constexpr int STEP_MAX_WARPS = 28;       // one world per warp: 72 registers per thread
+constexpr int WIDE_MAX_WARPS = 8;        // one world per warp, few warps: 255 registers per thread
 constexpr int PAIR_MAX_WARPS = 16;       // two worlds per warp: 128 registers per thread
 constexpr int STEP_MAX_SMEM = 232448;    // dynamic shared memory per block
 __host__ __device__ __forceinline__ int step_region(const Layout &L) {
@@ -1857,6 +1858,12 @@ extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     step_part<5>(p);
 }
 // the whole step, one world per warp (whole_step)
+// the whole step, one world per warp, for blocks of at most WIDE_MAX_WARPS warps (few worlds per SM: c0, c2): the
+// same code with up to 255 registers per thread instead of 72, so its sequential sections do not spill
+extern "C" __global__ void __launch_bounds__(32 * WIDE_MAX_WARPS, 1)
+    goib2d_step_wide_kernel(const __grid_constant__ StepParams p) {
+    whole_step<1>(p);
+}
 extern "C" __global__ void __launch_bounds__(32 * STEP_MAX_WARPS, 1)
     goib2d_step_kernel(const __grid_constant__ StepParams p) {
     whole_step<1>(p);
@@ -1940,16 +1947,17 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
         const int fit = STEP_MAX_SMEM / (wpw * region);
         warps = warps > fit ? fit : warps;
         const size_t smem = (size_t)wpw * warps * region;
-        auto kern = pair ? goib2d_step_pair_kernel : goib2d_step_kernel;
+        const int which = pair ? 1 : warps <= WIDE_MAX_WARPS ? 2 : 0;
+        auto kern = which == 1 ? goib2d_step_pair_kernel : which == 2 ? goib2d_step_wide_kernel : goib2d_step_kernel;
         // the dynamic shared memory limit set per kernel and device (host threads may launch concurrently)
         static std::mutex smem_mu;
-        static int smem_set[2][64];
+        static int smem_set[3][64];
         if (smem > 48 * 1024) {
             std::lock_guard<std::mutex> lk(smem_mu);
-            if (dev >= 64 || (size_t)smem_set[pair][dev] < smem) {
+            if (dev >= 64 || (size_t)smem_set[which][dev] < smem) {
                 cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
                 if (e != cudaSuccess) return e;
-                if (dev < 64) smem_set[pair][dev] = (int)smem;
+                if (dev < 64) smem_set[which][dev] = (int)smem;
             }
         }
         const int per_block = wpw * warps;
