@@ -198,8 +198,19 @@ int build_grid(const goib2d_model_desc &d, const std::vector<int32_t> &rows, std
         else if (row_of[b] >= 0 && sidx[a] >= 0)
             cand[(size_t)row_of[b] * S + sidx[a]] = p;
     }
+    // each row's entries of dd (indices into dd, ascending): a TOI event's FindNewContacts visits only the moved rows'
+    std::vector<int32_t> dd_start((size_t)R + 1, 0), dd_idx(2 * dd.size() + 1, 0);
+    for (int32_t p : dd) ++dd_start[row_of[d.pair_a[p]] + 1], ++dd_start[row_of[d.pair_b[p]] + 1];
+    for (int r = 0; r < R; ++r) dd_start[r + 1] += dd_start[r];
+    {
+        std::vector<int32_t> fill(dd_start.begin(), dd_start.end() - 1);
+        for (size_t k = 0; k < dd.size(); ++k) {
+            dd_idx[fill[row_of[d.pair_a[dd[k]]]]++] = (int32_t)k;
+            dd_idx[fill[row_of[d.pair_b[dd[k]]]]++] = (int32_t)k;
+        }
+    }
     int rc = 0;
-    const int32_t *d_start, *d_items, *d_sfix, *d_cand, *d_dd;
+    const int32_t *d_start, *d_items, *d_sfix, *d_cand, *d_dd, *d_dd_start, *d_dd_idx;
     const float *d_sfat;
     rc = rc ? rc : upload(allocs, start.data(), start.size(), &d_start);
     rc = rc ? rc : upload(allocs, items.data(), items.size(), &d_items);
@@ -207,10 +218,12 @@ int build_grid(const goib2d_model_desc &d, const std::vector<int32_t> &rows, std
     rc = rc ? rc : upload(allocs, sfat.data(), sfat.size(), &d_sfat);
     rc = rc ? rc : upload(allocs, cand.data(), cand.size(), &d_cand);
     rc = rc ? rc : upload(allocs, dd.data(), dd.size(), &d_dd);
+    rc = rc ? rc : upload(allocs, dd_start.data(), dd_start.size(), &d_dd_start);
+    rc = rc ? rc : upload(allocs, dd_idx.data(), dd_idx.size(), &d_dd_idx);
     if (rc) return rc;
     g.n_static = S, g.n_rows = R, g.nx = nx, g.ny = ny, g.gx0 = x0, g.gy0 = y0;
     g.cell_start = d_start, g.cell_items = d_items, g.sfix = d_sfix, g.sfat = d_sfat, g.cand_rs = d_cand;
-    g.n_dd = (int)dd.size(), g.dd = d_dd;
+    g.n_dd = (int)dd.size(), g.dd = d_dd, g.dd_row_start = d_dd_start, g.dd_row_idx = d_dd_idx;
     g.max_hits = 256;
     g.grid = 1;
     return 0;
@@ -618,6 +631,8 @@ int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int
             return fail(GOIB2D_EINVAL, "leaf %d is null", i);
     gb::StepParams p{};
     p.lay = scratch_layout(dm->B, C, dm->J, dm->P, dm->grid ? dm->max_hits : 0);
+    // The arena's size bounds the batch far below the grid-size limit goib2d_step checks ((n_worlds + 3) / 4 blocks
+    // < 2^31): a world's arena stride is at least 256 bytes, so at most 131072 worlds fit.
     const int64_t max_worlds = (int64_t)GOIB2D_NOALLOC_SCRATCH_BYTES / p.lay.stride;
     if (n_worlds > max_worlds)
         return fail(GOIB2D_ELIMIT,

@@ -36,6 +36,8 @@ struct DevModel {
     const int32_t *cand_rs;       // [n_rows][n_static] candidate of (row's fixture, static fixture), -1 if none
     int n_dd;                     // candidates whose fixtures are both non-static
     const int32_t *dd;            // [n_dd] those candidates, ascending
+    const int32_t *dd_row_start;  // [n_rows + 1] CSR over rows of dd_row_idx
+    const int32_t *dd_row_idx;    // each row's entries of dd (its pairs with another non-static fixture), ascending
     int max_hits;                 // per-world hit buffer; more hits fall back to the full scan
 };
 

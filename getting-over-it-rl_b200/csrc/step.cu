@@ -266,15 +266,46 @@ __device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits, const i
             }
         }
     }
-    for (int base = 0; base < m.n_dd; base += x.wl) {  // pairs of two non-static fixtures: every one, in order
-        int i = base + lane, p = -1;
-        if (i < m.n_dd && (!moved || pair_moved(m, m.dd[i], moved)) && is_new_pair(x, m.dd[i], bitmap)) p = m.dd[i];
-        unsigned mk = gballot(x, p >= 0);
-        if (p >= 0) {
-            int k = n + __popc(mk & ((1u << lane) - 1));
-            if (k < cap) hits[k] = p;
+    if (!moved) {
+        for (int base = 0; base < m.n_dd; base += x.wl) {  // pairs of two non-static fixtures: every one, in order
+            int i = base + lane, p = -1;
+            if (i < m.n_dd && is_new_pair(x, m.dd[i], bitmap)) p = m.dd[i];
+            unsigned mk = gballot(x, p >= 0);
+            if (p >= 0) {
+                int k = n + __popc(mk & ((1u << lane) - 1));
+                if (k < cap) hits[k] = p;
+            }
+            n += __popc(mk);
         }
-        n += __popc(mk);
+    } else {
+        // the pairs of two non-static fixtures that join a moved body's fixture: each moved row's entries of dd, dealt
+        // one per lane; a pair whose two rows both moved is taken from its lower row only
+        for (int r0 = 0; r0 < m.n_rows; r0 += WL) {
+            const int r = r0 + lane;
+            const bool mv = r < m.n_rows && moved[m.fixture_body[m.row_fixture[r]]];
+            const int e0 = mv ? m.dd_row_start[r] : 0, ne = mv ? m.dd_row_start[r + 1] - e0 : 0;
+            int T = 0;
+            const int eoff = gscan(x, ne, &T);
+            for (int t0 = 0; t0 < T; t0 += WL) {
+                const int t = t0 + lane;
+                const int co = gowner(x, eoff, ne, t);
+                const int c_off = gshfl(x, eoff, co), c_e0 = gshfl(x, e0, co), row = r0 + co;
+                int p = -1;
+                if (t < T) {
+                    const int pc = m.dd[m.dd_row_idx[c_e0 + (t - c_off)]];
+                    const int ra = m.fixture_slot[m.pair_a[pc]], rb = m.fixture_slot[m.pair_b[pc]];
+                    const int other = ra == row ? rb : ra;
+                    const bool twice = other < row && moved[m.fixture_body[m.row_fixture[other]]];
+                    if (!twice && is_new_pair(x, pc, bitmap)) p = pc;
+                }
+                const unsigned mk = gballot(x, p >= 0);
+                if (p >= 0) {
+                    const int k = n + __popc(mk & ((1u << lane) - 1));
+                    if (k < cap) hits[k] = p;
+                }
+                n += __popc(mk);
+            }
+        }
     }
     gsync(x);
     return n <= cap ? n : -1;
@@ -1348,7 +1379,11 @@ __device__ void toi_event(Ctx &x, float dt, int min_slot, float min_alpha) {
         solved[s_] = 0;
         if (w.pair[s_] < 0) continue;
         int ba = m.fixture_body[w.fa[s_]], bb = m.fixture_body[w.fb[s_]];
-        if (ba != A && bb != A && ba != Bb && bb != Bb) continue;
+        // the minimum contact and the contacts the island walk visits: those of a dynamic TOI body (a static or
+        // kinematic one's contacts are not walked, toi.py:633-657)
+        const bool of_a = (ba == A || bb == A) && w.type[A] == DYNAMIC;
+        const bool of_b = (ba == Bb || bb == Bb) && w.type[Bb] == DYNAMIC;
+        if (s_ != min_slot && !of_a && !of_b) continue;
         const float *da = adv + 8 * ba, *db = adv + 8 * bb;
         evaluate(m, w.fa[s_], w.fb[s_], Xf{{da[4], da[5]}, {da[6], da[7]}}, Xf{{db[4], db[5]}, {db[6], db[7]}},
                  s.linear_slop, s.angular_slop, man[s_]);
