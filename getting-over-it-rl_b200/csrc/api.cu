@@ -94,8 +94,10 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits, int hot_max 
     L.hot_end = (int)fits;
     // the cold part: rows, manifolds, records and the broadphase buffers
     L.man = take((int64_t)sizeof(gb::Man) * (C > 0 ? C : 1));
+    off = (off + 31) & ~int64_t(31);  // contact rows (7 sectors each) start on a 32-byte sector
     L.vc = take((int64_t)sizeof(gb::VCRow) * (C > 0 ? C : 1));
     L.rec = take(8 * c4);
+    off = (off + 31) & ~int64_t(31);  // joint rows start on a 32-byte sector (gb::JRow)
     L.jr = take((int64_t)sizeof(gb::JRow) * (J > 0 ? J : 1));
     const int64_t n_rows4 = 4 * (int64_t)((C > 0 ? C : 0) + (J > 0 ? J : 0) + 2);
     L.lv_level = take(n_rows4), L.lv_items = take(n_rows4), L.lv_start = take(n_rows4), L.lv_cur = take(n_rows4);

@@ -65,23 +65,29 @@ struct alignas(16) VCRow {
     float radA, radB;
 };
 
-// One ordered joint (joints.py:163-173).
+// One ordered joint (joints.py:163-173). The fields the revolute velocity solves read come first (148 bytes, five
+// 32-byte sectors): a row read from memory on every iteration (the one-world-per-thread sweeps of large batches)
+// then moves five sectors per joint and iteration instead of all eight. 256 bytes, so that rows in an array whose
+// start is 32-byte aligned (the arena's) stay aligned to sectors.
 struct alignas(16) JRow {
-    int jid, type, ia, ib, limit_state, enable_motor, enable_limit, soft;
+    int type, ia, ib, limit_state, enable_motor, enable_limit, soft, jid;
     float mA, mB, iA, iB;
     V2 rA, rB;
-    V3 Kx, Ky, Kz;
-    float motor_mass, motor_speed, max_impulse;
-    V2 ax, pe;
-    float a1, a2, s1, s2;
-    float gamma, bias, angle, inv_dt;
-    V2 la, lb;
-    float ref, lower, upper;
-    V2 lx, ly;
+    V3 Kx, Ky;
+    float motor_mass, motor_speed, max_impulse, angle, inv_dt, lower, upper;
     float imp[5];
     float mimp;
-    float d33, d22;  // inverse determinants of K and of its upper-left 2x2 block (fixed over the velocity iterations)
+    float d22, d33;  // inverse determinants of K's upper-left 2x2 block and of K (fixed over the velocity iterations)
+    V3 Kz;
+    V2 ax, pe;
+    float a1, a2, s1, s2;
+    float gamma, bias;
+    V2 la, lb;
+    float ref;
+    V2 lx, ly;
+    float pad_[4];
 };
+static_assert(sizeof(JRow) == 256, "JRow: 8 sectors");
 
 // A narrow-phase result (collide.py:5-7).
 struct Man {
