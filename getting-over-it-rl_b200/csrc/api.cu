@@ -246,6 +246,7 @@ struct goib2d_model {
     int32_t *action_joint = nullptr;
     float *action_scale = nullptr;
     int32_t step_mode = 0;  // goib2d_set_step_mode
+    int32_t stage_max = 0;  // goib2d_set_state_staging
     int32_t event_cap = 0;  // contact event log per world (0: off)
     goib2d_event *events = nullptr;
     int32_t *event_count = nullptr;
@@ -481,6 +482,7 @@ int goib2d_step_seq(goib2d_model *m, const goib2d_settings *s, float dt, int32_t
     for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
     p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
     p.step_mode = m->step_mode;
+    p.stage_max = m->stage_max;
     p.lay = scratch_layout(dm->B, C, dm->J, dm->P, dm->grid ? dm->max_hits : 0,
                            gb::hot_budget(n_worlds, dm->J, C, m->step_mode));
     size_t need = (size_t)p.lay.stride * (size_t)n_worlds;
@@ -530,6 +532,14 @@ int goib2d_set_step_mode(goib2d_model *m, int32_t mode) {
     if (mode < 0 || mode > 2) return fail(GOIB2D_EINVAL, "step mode %d: 0 (per batch), 1 or 2 worlds per warp", mode);
     std::lock_guard<std::mutex> lk(m->mu);
     m->step_mode = mode;
+    return 0;
+}
+
+int goib2d_set_state_staging(goib2d_model *m, int32_t max_bytes_per_world) {
+    if (!m) return fail(GOIB2D_EINVAL, "null argument");
+    if (max_bytes_per_world < 0) return fail(GOIB2D_EINVAL, "negative staging size");
+    std::lock_guard<std::mutex> lk(m->mu);
+    m->stage_max = max_bytes_per_world;
     return 0;
 }
 
@@ -647,6 +657,7 @@ int goib2d_step_noalloc(goib2d_model *m, const goib2d_settings *s, float dt, int
     for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
     p.s = *s, p.dt = dt, p.C = C, p.rows = rows, p.n_worlds = n_worlds, p.n_steps = n_steps;
     p.step_mode = m->step_mode;
+    p.stage_max = m->stage_max;
     p.scratch = scratch;
     p.status = nullptr;  // no per-world status words (their buffer would need an allocation) ...
     p.events = nullptr;  // ... and no event log: neither reports an earlier call's results as this one's

@@ -153,6 +153,12 @@ struct StepParams {
     goib2d_event *events;  // contact event log [n_worlds][event_cap], or null (goib2d_set_event_log)
     int32_t *event_count;  // [n_worlds]
     int event_cap;
+    // State rows staged in shared memory for a whole launch (the one-launch step): each world copies the rows of the
+    // leaves with stage_off >= 0 into its staging area at stage_off, steps on the copies, and writes them back once
+    int32_t stage_off[GOIB2D_NUM_LEAVES];
+    int32_t leaf_bytes[GOIB2D_NUM_LEAVES];  // bytes of one world's row of each leaf
+    int32_t stage_bytes;                    // the staging area per world (0: nothing staged)
+    int32_t stage_max;                      // the model's staging limit per world (goib2d_set_state_staging)
 };
 
 // Parameters of the env kernels (env.cu): resets, observations, ray casts.

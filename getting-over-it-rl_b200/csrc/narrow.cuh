@@ -85,6 +85,47 @@ __device__ __forceinline__ void bind_world(W &w, const Leaves &L, int64_t wi, in
 #undef GBU
 }
 
+// Point the binding's row of one leaf elsewhere (a copy of the row in shared memory, see stage_rows in step.cu).
+__device__ __forceinline__ void set_leaf(W &w, int leaf, char *row) {
+#define GBS(name, field, T) \
+    case name: w.field = reinterpret_cast<T *>(row); break
+    switch (leaf) {
+        GBS(GOIB2D_B_TYPE, type, int32_t); GBS(GOIB2D_B_ACTIVE, active, uint8_t); GBS(GOIB2D_B_AWAKE, awake, uint8_t);
+        GBS(GOIB2D_B_ALLOW_SLEEP, allow_sleep, uint8_t); GBS(GOIB2D_B_BULLET, bullet, uint8_t);
+        GBS(GOIB2D_B_CONTINUOUS, continuous, uint8_t); GBS(GOIB2D_B_SLEEP_TIME, sleep_time, float);
+        GBS(GOIB2D_B_XF_P, xf_p, float); GBS(GOIB2D_B_XF_Q, xf_q, float); GBS(GOIB2D_B_LOCAL_CENTER, local_center, float);
+        GBS(GOIB2D_B_C0, c0, float); GBS(GOIB2D_B_C, c, float); GBS(GOIB2D_B_A0, a0, float); GBS(GOIB2D_B_A, a, float);
+        GBS(GOIB2D_B_V, v, float); GBS(GOIB2D_B_W, w, float); GBS(GOIB2D_B_FORCE, force, float);
+        GBS(GOIB2D_B_TORQUE, torque, float); GBS(GOIB2D_B_MASS, mass, float); GBS(GOIB2D_B_INV_MASS, inv_mass, float);
+        GBS(GOIB2D_B_INERTIA, inertia, float); GBS(GOIB2D_B_INV_INERTIA, inv_inertia, float);
+        GBS(GOIB2D_B_LINEAR_DAMPING, linear_damping, float); GBS(GOIB2D_B_ANGULAR_DAMPING, angular_damping, float);
+        GBS(GOIB2D_B_GRAVITY_SCALE, gravity_scale, float);
+        GBS(GOIB2D_F_FRICTION, fx_friction, float); GBS(GOIB2D_F_RESTITUTION, fx_restitution, float);
+        GBS(GOIB2D_F_FAT, fx_fat, float);
+        GBS(GOIB2D_J_ENABLE_MOTOR, enable_motor, uint8_t); GBS(GOIB2D_J_MOTOR_SPEED, motor_speed, float);
+        GBS(GOIB2D_J_MAX_MOTOR, max_motor, float); GBS(GOIB2D_J_ENABLE_LIMIT, enable_limit, uint8_t);
+        GBS(GOIB2D_J_LOWER, lower, float); GBS(GOIB2D_J_UPPER, upper, float); GBS(GOIB2D_J_FREQUENCY, frequency, float);
+        GBS(GOIB2D_J_DAMPING, damping, float); GBS(GOIB2D_J_IMPULSE, impulse, float);
+        GBS(GOIB2D_J_MOTOR_IMPULSE, motor_impulse, float); GBS(GOIB2D_J_LIMIT_STATE, limit_state, int32_t);
+        GBS(GOIB2D_J_LOWER_IMPULSE, lower_impulse, float); GBS(GOIB2D_J_UPPER_IMPULSE, upper_impulse, float);
+        GBS(GOIB2D_C_PAIR, pair, int32_t); GBS(GOIB2D_C_FA, fa, int32_t); GBS(GOIB2D_C_FB, fb, int32_t);
+        GBS(GOIB2D_C_KEY, key, int32_t); GBS(GOIB2D_C_TOUCHING, touching, uint8_t); GBS(GOIB2D_C_MTYPE, mtype, int32_t);
+        GBS(GOIB2D_C_COUNT, count, int32_t); GBS(GOIB2D_C_LOCAL_NORMAL, local_normal, float);
+        GBS(GOIB2D_C_LOCAL_POINT, local_point, float); GBS(GOIB2D_C_POINT_LOCAL, point_local, float);
+        GBS(GOIB2D_C_POINT_ID, point_id, int32_t); GBS(GOIB2D_C_NORMAL_IMPULSE, normal_impulse, float);
+        GBS(GOIB2D_C_TANGENT_IMPULSE, tangent_impulse, float); GBS(GOIB2D_C_FRICTION, friction, float);
+        GBS(GOIB2D_C_RESTITUTION, restitution, float); GBS(GOIB2D_C_TANGENT_SPEED, tangent_speed, float);
+        GBS(GOIB2D_GRAVITY, gravity, float); GBS(GOIB2D_INV_DT0, inv_dt0, float); GBS(GOIB2D_NEXT_KEY, next_key, int32_t);
+        GBS(GOIB2D_NEW_FIXTURE, new_fixture, uint8_t); GBS(GOIB2D_OVERFLOW, overflow, int32_t);
+        GBS(GOIB2D_T_ALPHA0, t_alpha0, float); GBS(GOIB2D_T_COUNT, t_count, int32_t); GBS(GOIB2D_T_TOI, t_toi, float);
+        GBS(GOIB2D_T_FLAG, t_flag, uint8_t); GBS(GOIB2D_T_ENABLED, t_enabled, uint8_t);
+        GBS(GOIB2D_T_SOLVED, t_solved, uint8_t); GBS(GOIB2D_T_NORMAL_IMPULSE, t_ni, float);
+        GBS(GOIB2D_T_TANGENT_IMPULSE, t_ti, float); GBS(GOIB2D_T_EVENTS, t_events, int32_t);
+        default: break;
+    }
+#undef GBS
+}
+
 // ---- fixtures in either layout (world.py:413-434)
 __device__ __forceinline__ AABB fixture_fat(const DevModel &m, const W &w, int f) {
     int r = m.fixture_slot[f];

@@ -823,10 +823,30 @@ __device__ __forceinline__ IslandWork solve(Ctx &x, float dt, float dt_ratio) {
 struct IslandIds {
     const int *cnt, *bisl, *cisl, *jisl;
 };
+// The State rows the sweeps write (StoreImpulses) or read (the PostSolve events' fixtures): the world's binding (whose
+// rows may be staged in shared memory), or the global leaves (the one-world-per-thread kernel, which binds nothing).
+struct StoreTo {
+    float *normal_impulse, *tangent_impulse, *lower_impulse, *upper_impulse, *impulse, *motor_impulse;
+    int32_t *limit_state;
+    const int32_t *fa, *fb;
+};
+__device__ __forceinline__ StoreTo store_to(const W &w) {
+    return {w.normal_impulse, w.tangent_impulse, w.lower_impulse, w.upper_impulse, w.impulse, w.motor_impulse,
+            w.limit_state, w.fa, w.fb};
+}
+__device__ __forceinline__ StoreTo store_to(const StepParams &p, int64_t world) {
+    const int C = p.C, J = p.m.J;
+    return {(float *)p.L.p[GOIB2D_C_NORMAL_IMPULSE] + world * 2 * C,
+            (float *)p.L.p[GOIB2D_C_TANGENT_IMPULSE] + world * 2 * C,
+            (float *)p.L.p[GOIB2D_J_LOWER_IMPULSE] + world * J, (float *)p.L.p[GOIB2D_J_UPPER_IMPULSE] + world * J,
+            (float *)p.L.p[GOIB2D_J_IMPULSE] + world * 3 * J, (float *)p.L.p[GOIB2D_J_MOTOR_IMPULSE] + world * J,
+            (int32_t *)p.L.p[GOIB2D_J_LIMIT_STATE] + world * J, (const int32_t *)p.L.p[GOIB2D_C_FA] + world * C,
+            (const int32_t *)p.L.p[GOIB2D_C_FB] + world * C};
+}
 __device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t world, const IslandWork &sw,
-                                                  const IslandIds &ids) {
+                                                  const IslandIds &ids, const StoreTo &st) {
     const goib2d_settings &s = p.s;
-    const int B = p.m.B, C = p.C, J = p.m.J;
+    const int B = p.m.B;
     const int n_contacts = ids.cnt[0], n_joints = ids.cnt[1], n_islands = ids.cnt[2];
     const int *bisl = ids.bisl, *cisl = ids.cisl, *jisl = ids.jisl;
     int *done = sw.done, *jok = sw.jok;
@@ -842,32 +862,23 @@ __device__ __forceinline__ void solve_constraints(const StepParams &p, int64_t w
         for (int k = 0; k < n_joints; ++k) joint_solve_velocity(jr[k], bd, v24);
         for (int k = 0; k < n_contacts; ++k) contact_solve_velocity(vc[k], bd);
     }
-    float *normal_impulse = (float *)p.L.p[GOIB2D_C_NORMAL_IMPULSE] + world * 2 * C;
-    float *tangent_impulse = (float *)p.L.p[GOIB2D_C_TANGENT_IMPULSE] + world * 2 * C;
     for (int k = 0; k < n_contacts; ++k) {  // StoreImpulses (contact_solver.py:293-304)
         const VCRow &c = vc[k];
         for (int j = 0; j < c.count; ++j)
-            normal_impulse[2 * c.slot + j] = c.ni[j], tangent_impulse[2 * c.slot + j] = c.ti[j];
+            st.normal_impulse[2 * c.slot + j] = c.ni[j], st.tangent_impulse[2 * c.slot + j] = c.ti[j];
     }
-    float *lower_impulse = (float *)p.L.p[GOIB2D_J_LOWER_IMPULSE] + world * J;
-    float *upper_impulse = (float *)p.L.p[GOIB2D_J_UPPER_IMPULSE] + world * J;
-    float *impulse = (float *)p.L.p[GOIB2D_J_IMPULSE] + world * 3 * J;
-    float *motor_impulse = (float *)p.L.p[GOIB2D_J_MOTOR_IMPULSE] + world * J;
-    int32_t *limit_state = (int32_t *)p.L.p[GOIB2D_J_LIMIT_STATE] + world * J;
     for (int k = 0; k < n_joints; ++k) {  // joints.py:609-622
         const JRow &r = jr[k];
-        if (v24) lower_impulse[r.jid] = r.imp[3], upper_impulse[r.jid] = r.imp[4];
-        for (int i = 0; i < 3; ++i) impulse[3 * r.jid + i] = r.imp[i];
-        motor_impulse[r.jid] = r.mimp;
-        limit_state[r.jid] = r.limit_state;
+        if (v24) st.lower_impulse[r.jid] = r.imp[3], st.upper_impulse[r.jid] = r.imp[4];
+        for (int i = 0; i < 3; ++i) st.impulse[3 * r.jid + i] = r.imp[i];
+        st.motor_impulse[r.jid] = r.mimp;
+        st.limit_state[r.jid] = r.limit_state;
     }
     if (p.events) {  // b2Island::Report: PostSolve per island contact, in solve order
-        const int32_t *fa = (const int32_t *)p.L.p[GOIB2D_C_FA] + world * C;
-        const int32_t *fb = (const int32_t *)p.L.p[GOIB2D_C_FB] + world * C;
         const int base = p.event_count[world];
         for (int k = 0; k < n_contacts; ++k) {
             const VCRow &c = vc[k];
-            put_event(p, world, base + k, EV_POST_SOLVE, fa[c.slot], fb[c.slot], c.count, c.ni, c.ti);
+            put_event(p, world, base + k, EV_POST_SOLVE, st.fa[c.slot], st.fb[c.slot], c.count, c.ni, c.ti);
         }
         p.event_count[world] = base + n_contacts;
     }
@@ -984,7 +995,8 @@ __device__ __forceinline__ bool lv_minus_zero(const Ctx &x, const Bodies &bd) {
 
 // solve_constraints with the passes levelled over the world's lanes: the same results, bit for bit (every lane of
 // the world calls it). Islands below LV_MIN_CONSTRAINTS constraints, and those whose velocity pass has fewer than
-// ~1.1 constraints per level on average (a joint chain: nothing to share out), run sequentially on lane 0.
+// 1.5 constraints per level on average, run sequentially on lane 0: c4's 20-link chain with the rig (~1.25 per
+// level) runs faster sequentially, c2's piles (~2.1) levelled.
 __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const IslandIds &ids) {
     const StepParams &p = x.p;
     const goib2d_settings &s = x.s;
@@ -998,10 +1010,10 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
     bool seq = nc + nj < LV_MIN_CONSTRAINTS || lv_minus_zero(x, sw.bd);
     if (!seq) {
         vnl = lv_levels(x, sw, vps, level, vitems, vstart, cur, last);
-        seq = 10 * vnl > 9 * (nc + nj);
+        seq = 3 * vnl > 2 * (nc + nj);
     }
     if (seq) {
-        if (lane == 0) solve_constraints(p, x.world, sw, ids);
+        if (lane == 0) solve_constraints(p, x.world, sw, ids, store_to(x.w));
         gsync(x);
         return;
     }
@@ -1010,7 +1022,7 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
         GB_COUNT(15, vnl);
     }
     const int cnl = lv_levels(x, sw, cps, level, citems, cstart, cur, last);
-    const int B = p.m.B, C = p.C, J = p.m.J;
+    const int B = p.m.B;
     const int64_t world = x.world;
     float *sep = sp<float>(x.scr, L.lv_sep);
     int *okj = sp<int>(x.scr, L.lv_ok);
@@ -1042,32 +1054,24 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
             gsync(x);
         }
     // StoreImpulses (contact_solver.py:293-304, joints.py:609-622), one row per lane
-    float *normal_impulse = (float *)p.L.p[GOIB2D_C_NORMAL_IMPULSE] + world * 2 * C;
-    float *tangent_impulse = (float *)p.L.p[GOIB2D_C_TANGENT_IMPULSE] + world * 2 * C;
+    const StoreTo st = store_to(x.w);
     for (int k = lane; k < nc; k += x.wl) {
         const VCRow &c = vc[k];
         for (int j = 0; j < c.count; ++j)
-            normal_impulse[2 * c.slot + j] = c.ni[j], tangent_impulse[2 * c.slot + j] = c.ti[j];
+            st.normal_impulse[2 * c.slot + j] = c.ni[j], st.tangent_impulse[2 * c.slot + j] = c.ti[j];
     }
-    float *lower_impulse = (float *)p.L.p[GOIB2D_J_LOWER_IMPULSE] + world * J;
-    float *upper_impulse = (float *)p.L.p[GOIB2D_J_UPPER_IMPULSE] + world * J;
-    float *impulse = (float *)p.L.p[GOIB2D_J_IMPULSE] + world * 3 * J;
-    float *motor_impulse = (float *)p.L.p[GOIB2D_J_MOTOR_IMPULSE] + world * J;
-    int32_t *limit_state = (int32_t *)p.L.p[GOIB2D_J_LIMIT_STATE] + world * J;
     for (int k = lane; k < nj; k += x.wl) {
         const JRow &r = jr[k];
-        if (v24) lower_impulse[r.jid] = r.imp[3], upper_impulse[r.jid] = r.imp[4];
-        for (int i = 0; i < 3; ++i) impulse[3 * r.jid + i] = r.imp[i];
-        motor_impulse[r.jid] = r.mimp;
-        limit_state[r.jid] = r.limit_state;
+        if (v24) st.lower_impulse[r.jid] = r.imp[3], st.upper_impulse[r.jid] = r.imp[4];
+        for (int i = 0; i < 3; ++i) st.impulse[3 * r.jid + i] = r.imp[i];
+        st.motor_impulse[r.jid] = r.mimp;
+        st.limit_state[r.jid] = r.limit_state;
     }
     if (p.events) {  // b2Island::Report: PostSolve per island contact, in solve order
-        const int32_t *fa = (const int32_t *)p.L.p[GOIB2D_C_FA] + world * C;
-        const int32_t *fb = (const int32_t *)p.L.p[GOIB2D_C_FB] + world * C;
         const int base = p.event_count[world];
         for (int k = lane; k < nc; k += x.wl) {
             const VCRow &c = vc[k];
-            put_event(p, world, base + k, EV_POST_SOLVE, fa[c.slot], fb[c.slot], c.count, c.ni, c.ti);
+            put_event(p, world, base + k, EV_POST_SOLVE, st.fa[c.slot], st.fb[c.slot], c.count, c.ni, c.ti);
         }
         gsync(x);
         if (lane == 0) p.event_count[world] = base + nc;
@@ -1797,6 +1801,37 @@ constexpr int STEP_MAX_SMEM = 232448;    // dynamic shared memory per block
 __host__ __device__ __forceinline__ int step_region(const Layout &L) {
     return (int)((sizeof(W) + 15) & ~size_t(15)) + L.hot_end + (L.hot_end > 0 ? L.rows_bytes : 0);
 }
+// Copy the world's rows of the staged leaves into its staging area in shared memory and point the binding there
+// (in), or copy them back to the State (out). Every leaf row of a world is contiguous; 4-byte leaves' rows start on
+// 4-byte boundaries, and one-byte leaves whose rows are a multiple of 4 bytes do too.
+__device__ __forceinline__ void stage_rows(const StepParams &p, W &w, int64_t world, int lane, int wl,
+                                           unsigned gmask, char *area, bool in) {
+    for (int leaf = 0; leaf < GOIB2D_NUM_LEAVES; ++leaf) {
+        const int off = p.stage_off[leaf];
+        if (off < 0) continue;
+        const int nb = p.leaf_bytes[leaf];
+        char *g = static_cast<char *>(p.L.p[leaf]) + world * (int64_t)nb;
+        char *s = area + off;
+        if ((nb & 3) == 0) {
+            uint32_t *gw = reinterpret_cast<uint32_t *>(g), *sw = reinterpret_cast<uint32_t *>(s);
+            for (int i = lane; i < nb / 4; i += wl) {
+                if (in) sw[i] = gw[i];
+                else gw[i] = sw[i];
+            }
+        } else {
+            for (int i = lane; i < nb; i += wl) {
+                if (in) s[i] = g[i];
+                else g[i] = s[i];
+            }
+        }
+    }
+    __syncwarp(gmask);
+    if (in && lane == 0)
+        for (int leaf = 0; leaf < GOIB2D_NUM_LEAVES; ++leaf)
+            if (p.stage_off[leaf] >= 0) set_leaf(w, leaf, area + p.stage_off[leaf]);
+    __syncwarp(gmask);
+}
+
 // the warp reconverges (all its lanes are at this same call), then the block's threads meet
 __device__ __forceinline__ void step_sync() {
     __syncwarp();
@@ -1810,14 +1845,17 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
     const int64_t world = p.world0 + (int64_t)blockIdx.x * (WPW * (blockDim.x >> 5)) + slot;
     const bool active = world < p.world_end;
     extern __shared__ __align__(16) char dyn_smem[];
-    char *mine = dyn_smem + slot * step_region(p.lay);
+    char *mine = dyn_smem + slot * (step_region(p.lay) + p.stage_bytes);
     W &w = *reinterpret_cast<W *>(mine);
     char *hot = p.lay.hot_end > 0 ? mine + ((sizeof(W) + 15) & ~size_t(15)) : nullptr;
     char *rows = hot && p.lay.rows_bytes ? hot + p.lay.hot_end : nullptr;
+    char *staged = mine + step_region(p.lay);  // the world's staged State rows (p.stage_bytes)
     if (active && (lane32 & (WL - 1)) == 0) bind_world(w, p.L, world, p.m.B, p.rows, p.m.J, p.C);
     __syncwarp();
     Ctx x{p, p.m, p.s, w, p.scratch + world * p.lay.stride, hot, rows, lane32 & (WL - 1), 0, 0, 0, -1, -1, 0, clock64(), world,
           WPW == 2 ? 0xffffu << (16 * half) : FULL, WL * half, WL};
+    const unsigned gmask = WPW == 2 ? 0xffffu << (16 * half) : FULL;
+    if (active && p.stage_bytes) stage_rows(p, w, world, lane32 & (WL - 1), WL, gmask, staged, true);
     const float dt = p.dt;
     for (int k = 0; k < p.n_steps; ++k) {
         x.step = k;
@@ -1852,6 +1890,7 @@ __device__ __forceinline__ void whole_step(const StepParams &p) {
         // it, 17.1 M without)
         step_sync();
     }
+    if (active && p.stage_bytes) stage_rows(p, w, world, lane32 & (WL - 1), WL, gmask, staged, false);
 }
 
 }  // namespace gb
@@ -1878,7 +1917,8 @@ extern "C" __global__ void __launch_bounds__(32) goib2d_constraints_kernel(const
     char *scr = p.scratch + world * p.lay.stride;
     const Layout &L = p.lay;
     solve_constraints(p, world, sweep_arena(scr, L),
-                      {sp<int>(scr, L.isl), sp<int>(scr, L.bisl), sp<int>(scr, L.cisl), sp<int>(scr, L.jisl)});
+                      {sp<int>(scr, L.isl), sp<int>(scr, L.bisl), sp<int>(scr, L.cisl), sp<int>(scr, L.jisl)},
+                      store_to(p, world));
 }
 extern "C" __global__ void __launch_bounds__(128, GOIB2D_MIN_BLOCKS)
     goib2d_finish_kernel(const __grid_constant__ StepParams p) {
@@ -1967,6 +2007,52 @@ int hot_budget(int64_t n_worlds, int n_joints, int contact_capacity, int step_mo
     return per_world < HOT_MIN_BYTES ? HOT_MIN_BYTES : per_world > HOT_MAX_BYTES ? HOT_MAX_BYTES : per_world;
 }
 
+// Which State rows the one-launch step keeps in shared memory for the whole launch (goib2d_set_state_staging; off by
+// default), within `budget` bytes per world (what the block's shared memory leaves after the binding, the arena's hot
+// part and the rows region; at most STAGE_MAX_BYTES and the model's setting): the most used leaves first - the world
+// scalars, the bodies, the joints, the fixtures, then the contact slots' fields in order of use - each taken if it
+// still fits, on 16-byte boundaries. Measured (10-step calls, steps 50-400): c1 +0.5 % with everything that fits,
+// -2.5 % with the non-contact rows only; c0 -7 %, c3 -10 %, c4 at 8192 worlds +2 %. The rows' reads are L1 hits
+// already, the interleaved pairs and quadruples of floats (c[2b], point_local[4s + k]) conflict in shared-memory
+// banks, and the staging area takes from the L1, so the default stages nothing.
+constexpr int STAGE_MAX_BYTES = 16384;
+void plan_staging(StepParams &p, int budget, int model_max) {
+    static const int order[] = {
+        GOIB2D_GRAVITY, GOIB2D_INV_DT0, GOIB2D_NEXT_KEY, GOIB2D_NEW_FIXTURE, GOIB2D_OVERFLOW, GOIB2D_T_EVENTS,
+        GOIB2D_B_TYPE, GOIB2D_B_ACTIVE, GOIB2D_B_AWAKE, GOIB2D_B_ALLOW_SLEEP, GOIB2D_B_BULLET, GOIB2D_B_CONTINUOUS,
+        GOIB2D_B_SLEEP_TIME, GOIB2D_B_XF_P, GOIB2D_B_XF_Q, GOIB2D_B_LOCAL_CENTER, GOIB2D_B_C0, GOIB2D_B_C,
+        GOIB2D_B_A0, GOIB2D_B_A, GOIB2D_B_V, GOIB2D_B_W, GOIB2D_B_FORCE, GOIB2D_B_TORQUE, GOIB2D_B_MASS,
+        GOIB2D_B_INV_MASS, GOIB2D_B_INERTIA, GOIB2D_B_INV_INERTIA, GOIB2D_B_LINEAR_DAMPING,
+        GOIB2D_B_ANGULAR_DAMPING, GOIB2D_B_GRAVITY_SCALE, GOIB2D_T_ALPHA0,
+        GOIB2D_J_ENABLE_MOTOR, GOIB2D_J_MOTOR_SPEED, GOIB2D_J_MAX_MOTOR, GOIB2D_J_ENABLE_LIMIT, GOIB2D_J_LOWER,
+        GOIB2D_J_UPPER, GOIB2D_J_FREQUENCY, GOIB2D_J_DAMPING, GOIB2D_J_IMPULSE, GOIB2D_J_MOTOR_IMPULSE,
+        GOIB2D_J_LIMIT_STATE, GOIB2D_J_LOWER_IMPULSE, GOIB2D_J_UPPER_IMPULSE,
+        GOIB2D_F_FAT, GOIB2D_F_FRICTION, GOIB2D_F_RESTITUTION,
+        GOIB2D_C_PAIR, GOIB2D_C_KEY, GOIB2D_C_FA, GOIB2D_C_FB, GOIB2D_C_TOUCHING, GOIB2D_C_COUNT, GOIB2D_T_FLAG,
+        GOIB2D_T_ENABLED, GOIB2D_T_COUNT, GOIB2D_T_TOI, GOIB2D_C_MTYPE, GOIB2D_C_LOCAL_NORMAL, GOIB2D_C_LOCAL_POINT,
+        GOIB2D_C_POINT_LOCAL, GOIB2D_C_POINT_ID, GOIB2D_C_NORMAL_IMPULSE, GOIB2D_C_TANGENT_IMPULSE,
+        GOIB2D_C_FRICTION, GOIB2D_C_RESTITUTION, GOIB2D_C_TANGENT_SPEED, GOIB2D_T_SOLVED, GOIB2D_T_NORMAL_IMPULSE,
+        GOIB2D_T_TANGENT_IMPULSE};
+    static_assert(sizeof(order) / sizeof(order[0]) == GOIB2D_NUM_LEAVES, "every leaf once");
+    budget = budget < STAGE_MAX_BYTES ? budget : STAGE_MAX_BYTES;
+    budget = budget < model_max ? budget : model_max;
+    int used = 0;
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) {
+        const int leaf = order[i];
+        const int64_t elems = goib2d_leaf_elems(leaf, p.m.B, p.rows, p.m.J, p.C);
+        const int nb = (int)(elems * (goib2d_leaf_dtype(leaf) == 2 ? 1 : 4));
+        p.leaf_bytes[leaf] = nb;
+        const int padded = (nb + 15) & ~15;
+        if (nb > 0 && used + padded <= budget) {
+            p.stage_off[leaf] = used;
+            used += padded;
+        } else {
+            p.stage_off[leaf] = -1;
+        }
+    }
+    p.stage_bytes = used;
+}
+
 cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
     p.world0 = 0, p.world_end = p.n_worlds;
     const int64_t n = p.n_worlds;
@@ -1981,7 +2067,8 @@ cudaError_t launch_steps(StepParams p, cudaStream_t stream) {
         int warps = shape.warps;
         const int fit = STEP_MAX_SMEM / (wpw * region);
         warps = warps > fit ? fit : warps;
-        const size_t smem = (size_t)wpw * warps * region;
+        plan_staging(p, STEP_MAX_SMEM / (wpw * warps) - region, p.stage_max);
+        const size_t smem = (size_t)wpw * warps * (region + p.stage_bytes);
         const int which = pair ? 1 : warps <= WIDE_MAX_WARPS ? 2 : 0;
         auto kern = which == 1 ? goib2d_step_pair_kernel : which == 2 ? goib2d_step_wide_kernel : goib2d_step_kernel;
         // the dynamic shared memory limit set per kernel and device (host threads may launch concurrently)

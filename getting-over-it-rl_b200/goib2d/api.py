@@ -176,6 +176,11 @@ class Engine:
         are identical in every mode."""
         native.check(self.lib.goib2d_set_step_mode(self.handle, int(mode)))
 
+    def set_state_staging(self, max_bytes_per_world):
+        """Keep up to this many bytes of each world's State rows in shared memory across a one-launch call (0, the
+        default: none). Results are identical either way."""
+        native.check(self.lib.goib2d_set_state_staging(self.handle, int(max_bytes_per_world)))
+
     def set_event_log(self, capacity):
         """Log each world's contact events (Begin / End / PostSolve, goib2d_event) of every step, capacity per world
         (0: off)."""

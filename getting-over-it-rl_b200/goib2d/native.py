@@ -208,6 +208,7 @@ def load():
         "goib2d_candidate_pairs": (C.c_int, [C.POINTER(PairDesc), _i, _i, C.c_int64, C.POINTER(C.c_int64)]),
         "goib2d_set_event_log": (C.c_int, [vp, C.c_int32]),
         "goib2d_set_step_mode": (C.c_int, [vp, C.c_int32]),
+        "goib2d_set_state_staging": (C.c_int, [vp, C.c_int32]),
         "goib2d_events": (C.c_int, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int32)]),
         "goib2d_events_copy": (C.c_int, [vp, vp, _i, C.c_int64]),
         "goib2d_reset_masked": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp), vp, vp]),

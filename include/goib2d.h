@@ -163,6 +163,12 @@ int64_t goib2d_launches(const goib2d_model *model, int64_t n_worlds, int32_t n_s
  * No counterpart in the reference engine. */
 int goib2d_set_step_mode(goib2d_model *model, int32_t mode);
 
+/* Keep up to max_bytes_per_world bytes of each world's State rows in shared memory for the whole one-launch step
+ * call (read from HBM at its start, written back at its end; the most used rows first, as far as the block's shared
+ * memory allows). 0 (default) stages nothing. Results are identical either way; only the speed differs. No
+ * counterpart in the reference engine. */
+int goib2d_set_state_staging(goib2d_model *model, int32_t max_bytes_per_world);
+
 /* ---- Env helpers around the step (no counterpart in the reference engine, whose RL env is outside it). Same
  * contact_capacity / fixture_rows / leaves conventions as goib2d_step; asynchronous on `stream`. */
 

@@ -34,6 +34,7 @@ def test_library_exports_every_declared_symbol():
     assert lib.goib2d_launches(None, 4096, 10) < 0
     assert lib.goib2d_step_seq(None, None, 0.02, 8, 1, 1, 1, None, None, 0, None) == -1
     assert lib.goib2d_set_step_mode(None, 1) < 0 and b"null" in lib.goib2d_last_error()
+    assert lib.goib2d_set_state_staging(None, 4096) < 0 and b"null" in lib.goib2d_last_error()
     for leaf in range(71):  # the leaf table agrees with the Python one (no device needed)
         B, rows, J, C = 5, 7, 3, 11
         spec = native.leaf_spec(B, rows, J, C)[leaf]
