@@ -102,7 +102,7 @@ gb::Layout scratch_layout(int B, int C, int J, int P, int max_hits, int hot_max 
     const int64_t n_rows4 = 4 * (int64_t)((C > 0 ? C : 0) + (J > 0 ? J : 0) + 2);
     L.lv_level = take(n_rows4), L.lv_items = take(n_rows4), L.lv_start = take(n_rows4), L.lv_cur = take(n_rows4);
     L.lv_items2 = take(n_rows4), L.lv_start2 = take(n_rows4);
-    L.lv_last = take(b4), L.lv_sep = take(c4), L.lv_ok = take(j4);
+    L.lv_sep = take(c4), L.lv_ok = take(j4);
     L.bitmap = take(4 * (int64_t)((P + 31) / 32 + 1));
     L.hits = take(8 * (int64_t)(max_hits > 0 ? max_hits : 1));  // unsorted + sorted halves
     L.stride = (off + 255) & ~int64_t(255);
@@ -211,8 +211,15 @@ int build_grid(const goib2d_model_desc &d, const std::vector<int32_t> &rows, std
             dd_idx[fill[row_of[d.pair_b[dd[k]]]]++] = (int32_t)k;
         }
     }
+    // each dd entry's two rows and bodies in one 16-byte record (the full scan's one load per pair)
+    std::vector<int32_t> dd4(4 * dd.size() + 4, 0);
+    for (size_t k = 0; k < dd.size(); ++k) {
+        const int a = d.pair_a[dd[k]], b = d.pair_b[dd[k]];
+        dd4[4 * k] = row_of[a], dd4[4 * k + 1] = row_of[b];
+        dd4[4 * k + 2] = d.fixture_body[a], dd4[4 * k + 3] = d.fixture_body[b];
+    }
     int rc = 0;
-    const int32_t *d_start, *d_items, *d_sfix, *d_cand, *d_dd, *d_dd_start, *d_dd_idx;
+    const int32_t *d_start, *d_items, *d_sfix, *d_cand, *d_dd, *d_dd_start, *d_dd_idx, *d_dd4;
     const float *d_sfat;
     rc = rc ? rc : upload(allocs, start.data(), start.size(), &d_start);
     rc = rc ? rc : upload(allocs, items.data(), items.size(), &d_items);
@@ -222,10 +229,12 @@ int build_grid(const goib2d_model_desc &d, const std::vector<int32_t> &rows, std
     rc = rc ? rc : upload(allocs, dd.data(), dd.size(), &d_dd);
     rc = rc ? rc : upload(allocs, dd_start.data(), dd_start.size(), &d_dd_start);
     rc = rc ? rc : upload(allocs, dd_idx.data(), dd_idx.size(), &d_dd_idx);
+    rc = rc ? rc : upload(allocs, dd4.data(), dd4.size(), &d_dd4);
     if (rc) return rc;
     g.n_static = S, g.n_rows = R, g.nx = nx, g.ny = ny, g.gx0 = x0, g.gy0 = y0;
     g.cell_start = d_start, g.cell_items = d_items, g.sfix = d_sfix, g.sfat = d_sfat, g.cand_rs = d_cand;
     g.n_dd = (int)dd.size(), g.dd = d_dd, g.dd_row_start = d_dd_start, g.dd_row_idx = d_dd_idx;
+    g.dd_rb = reinterpret_cast<const int4 *>(d_dd4);
     g.max_hits = 256;
     g.grid = 1;
     return 0;

@@ -38,6 +38,7 @@ struct DevModel {
     const int32_t *dd;            // [n_dd] those candidates, ascending
     const int32_t *dd_row_start;  // [n_rows + 1] CSR over rows of dd_row_idx
     const int32_t *dd_row_idx;    // each row's entries of dd (its pairs with another non-static fixture), ascending
+    const int4 *dd_rb;            // [n_dd] each dd entry's rows (x: fixture a's, y: b's) and bodies (z: a's, w: b's)
     int max_hits;                 // per-world hit buffer; more hits fall back to the full scan
 };
 
@@ -119,7 +120,7 @@ struct Layout {
     // [ceil(P/32)]
     // levelled sweeps (solve_constraints_levelled): per pass position its level and the positions sorted by level,
     // the level starts, fill cursors, each body's next free level, and the position passes' per-row results
-    int64_t lv_level, lv_items, lv_start, lv_items2, lv_start2, lv_cur, lv_last, lv_sep, lv_ok;
+    int64_t lv_level, lv_items, lv_start, lv_items2, lv_start2, lv_cur, lv_sep, lv_ok;
     int64_t bitmap;
     int64_t hits;  // [max_hits] new-pair candidates of the grid path
     int64_t stride;  // bytes per world (multiple of 256)

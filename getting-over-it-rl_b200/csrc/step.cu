@@ -38,7 +38,17 @@ __device__ unsigned long long g_counts[16];
 __device__ unsigned long long g_toi_cycles[16];
 // per-world cycles in a part (sum, worlds, max): 0-2 TOI without events, 3-5 TOI with events, 9-11 collide
 __device__ unsigned long long g_span[16];
+// cycles in the parts of the levelled sweeps (lane 0): 0 velocity levelling, 1 contacts-first levelling, 2 warm
+// start, 3 velocity iterations, 4 impulses and integration, 5 position levels, 6 position reductions
+__device__ unsigned long long g_lv_cycles[16];
 }  // namespace gb
+#define GB_LV_T0(x) long long gb_lv_ = clock64()
+#define GB_LV(x, i)                                                                                \
+    do {                                                                                           \
+        const long long t_ = clock64();                                                            \
+        if ((x).lane == 0) atomicAdd(&g_lv_cycles[i], (unsigned long long)(t_ - gb_lv_));          \
+        gb_lv_ = t_;                                                                               \
+    } while (0)
 #define GB_SPAN(x, k, ev)                                                                   \
     do {                                                                                    \
         if ((x).lane == 0) {                                                                \
@@ -65,6 +75,12 @@ __device__ unsigned long long g_span[16];
     } while (0)
 #define GB_SPAN(x, k, ev) \
     do {                  \
+    } while (0)
+#define GB_LV_T0(x) \
+    do {            \
+    } while (0)
+#define GB_LV(x, i) \
+    do {            \
     } while (0)
 #endif
 
@@ -267,15 +283,36 @@ __device__ int grid_new_pairs(Ctx &x, const uint32_t *bitmap, int *hits, const i
         }
     }
     if (!moved) {
-        for (int base = 0; base < m.n_dd; base += x.wl) {  // pairs of two non-static fixtures: every one, in order
-            int i = base + lane, p = -1;
-            if (i < m.n_dd && is_new_pair(x, m.dd[i], bitmap)) p = m.dd[i];
-            unsigned mk = gballot(x, p >= 0);
-            if (p >= 0) {
-                int k = n + __popc(mk & ((1u << lane) - 1));
-                if (k < cap) hits[k] = p;
+        // pairs of two non-static fixtures: every one, DD_UNROLL per lane at a time so that their loads (the pair's
+        // rows and bodies in one record, then their boxes, types and the contact bitmap) are in flight together
+        constexpr int DD_UNROLL = 4;
+        for (int base = 0; base < m.n_dd; base += DD_UNROLL * WL) {
+            int p[DD_UNROLL];
+            int4 rb[DD_UNROLL];
+#pragma unroll
+            for (int u = 0; u < DD_UNROLL; ++u) {
+                const int i = base + u * WL + lane;
+                p[u] = i < m.n_dd ? m.dd[i] : -1;
+                rb[u] = i < m.n_dd ? m.dd_rb[i] : make_int4(0, 0, 0, 0);
             }
-            n += __popc(mk);
+            bool hit[DD_UNROLL];
+#pragma unroll
+            for (int u = 0; u < DD_UNROLL; ++u) {  // is_new_pair, from the record
+                const float *fa = w.fx_fat + 4 * rb[u].x, *fb = w.fx_fat + 4 * rb[u].y;
+                const bool ov = overlap(AABB{fa[0], fa[1], fa[2], fa[3]}, AABB{fb[0], fb[1], fb[2], fb[3]});
+                const int ba = rb[u].z, bb = rb[u].w;
+                const bool can = (w.type[ba] == DYNAMIC || w.type[bb] == DYNAMIC) && w.active[ba] && w.active[bb];
+                hit[u] = p[u] >= 0 && ov && can && !((bitmap[p[u] >> 5] >> (p[u] & 31)) & 1u);
+            }
+#pragma unroll
+            for (int u = 0; u < DD_UNROLL; ++u) {
+                const unsigned mk = gballot(x, hit[u]);
+                if (hit[u]) {
+                    const int k = n + __popc(mk & ((1u << lane) - 1));
+                    if (k < cap) hits[k] = p[u];
+                }
+                n += __popc(mk);
+            }
         }
     } else {
         // the pairs of two non-static fixtures that join a moved body's fixture: each moved row's entries of dd, dealt
@@ -573,13 +610,13 @@ __device__ IslandOut find_islands(Ctx &x) {
     const int C = w.C, B = w.B, J = w.J, lane = x.lane;
     const Layout &L = x.p.lay;
     int *order = ap<int>(x, L.order), *lpos = ap<int>(x, L.lpos), *edges = ap<int>(x, L.edges);
-    int *corder = ap<int>(x, L.corder), *cisl = ap<int>(x, L.cisl), *cflag = ap<int>(x, L.cflag);
+    int *corder = ap<int>(x, L.corder), *cisl = ap<int>(x, L.cisl);
     int *jorder = ap<int>(x, L.jorder), *jisl = ap<int>(x, L.jisl), *jflag = ap<int>(x, L.jflag);
     int *bisl = ap<int>(x, L.bisl), *bflag = ap<int>(x, L.bflag), *stack = ap<int>(x, L.stack);
     int *adj_start = ap<int>(x, L.adj_start), *adj_cur = ap<int>(x, L.adj_cur);
     int2 *adj = ap<int2>(x, L.adj);
     int n_live = list_order(x, order, lpos);
-    for (int s = lane; s < C; s += x.wl) cisl[s] = -1, cflag[s] = 0;
+    for (int s = lane; s < C; s += x.wl) cisl[s] = -1;
     for (int j = lane; j < J; j += x.wl) jisl[j] = -1, jflag[j] = 0;
     for (int b = lane; b < B; b += x.wl) bisl[b] = -1, bflag[b] = 0, adj_cur[b] = 0;
     gsync(x);
@@ -613,6 +650,7 @@ __device__ IslandOut find_islands(Ctx &x) {
         run += gshfl(x, inc, x.wl - 1);
     }
     if (lane == 0) adj_start[B] = run;
+    const int n_adj = run;
     gsync(x);
     for (int base = 0; base < n_edges; base += x.wl) {  // fill 32 edges at a time, in edge order within each list
         int e = base + lane;
@@ -636,38 +674,101 @@ __device__ IslandOut find_islands(Ctx &x) {
         if (b >= 0) atomicAdd(&adj_cur[b], 1);
         gsync(x);
     }
+    // The walk (b2World::Solve's island DFS, island.py:41-140). A contact sits in the lists of its non-static bodies
+    // only and is taken when the first of them is popped, so it was taken before exactly when its other end is a
+    // non-static body already walked (bisl set): no per-contact flag is read. With the lists in shared memory lane 0
+    // walks alone; otherwise, per popped body, the lanes read its list (32 / 16 entries at a time) and lane 0 takes
+    // the entries in order, and the seed search is a ballot over 32 / 16 bodies at a time, highest index first (the
+    // list starts are then kept in jok, free until the sweeps fill it).
     IslandOut out{0, 0, 0};
-    if (lane == 0) {
-        int sp_ = 0, nc = 0, nj = 0, ni = 0;
-        int next_seed = B - 1;  // bodies above the last seed never qualify again: flags only get set, and only
-                                // bodies already flagged are woken
-        for (;;) {
-            if (sp_ == 0) {
-                int seed = -1;
-                for (int b = next_seed; b >= 0; --b)
-                    if (w.active[b] && w.type[b] != STATIC && w.awake[b] && !bflag[b]) {
-                        seed = b;
-                        break;
-                    }
-                if (seed < 0) break;
-                next_seed = seed - 1;
-                ++ni;
-                stack[sp_++] = seed;
-                bflag[seed] = 1;
-                continue;
+    if (x.hot && L.adj + 16 * (int64_t)C <= L.hot_end) {
+        if (lane == 0) {
+            int sp_ = 0, nc = 0, nj = 0, ni = 0;
+            int next_seed = B - 1;  // bodies above the last seed never qualify again: flags only get set, and only
+                                    // bodies already flagged are woken
+            for (;;) {
+                if (sp_ == 0) {
+                    int seed = -1;
+                    for (int b = next_seed; b >= 0; --b)
+                        if (w.active[b] && w.type[b] != STATIC && w.awake[b] && !bflag[b]) {
+                            seed = b;
+                            break;
+                        }
+                    if (seed < 0) break;
+                    next_seed = seed - 1;
+                    ++ni;
+                    stack[sp_++] = seed;
+                    bflag[seed] = 1;
+                    continue;
+                }
+                const int b = stack[--sp_], id = ni - 1;
+                for (int q = adj_start[b], qe = adj_start[b + 1]; q < qe; ++q) {
+                    const int2 en = adj[q];
+                    const int s_ = en.x, other = en.y;
+                    if (other >= 0 && other != b && bisl[other] >= 0) continue;
+                    corder[nc++] = s_;
+                    cisl[s_] = id;
+                    if (other >= 0 && !bflag[other]) stack[sp_++] = other, bflag[other] = 1;
+                }
+                for (int q = m.jadj_start[b], qe = m.jadj_start[b + 1]; q < qe; ++q) {
+                    int j = m.jadj[2 * q], other = m.jadj[2 * q + 1];
+                    if (jflag[j] || !w.active[other]) continue;
+                    jorder[nj++] = j;
+                    jisl[j] = id;
+                    jflag[j] = 1;
+                    if (!bflag[other] && w.type[other] != STATIC) stack[sp_++] = other, bflag[other] = 1;
+                }
+                bisl[b] = id;
+                wake_body(w, b);
             }
-            int b = stack[--sp_];
-            int id = ni - 1;
-            for (int q = adj_start[b], qe = adj_start[b + 1]; q < qe; ++q) {
-                int2 en = adj[q];
-                int s = en.x;
-                if (cflag[s]) continue;
-                corder[nc++] = s;
-                cisl[s] = id;
-                cflag[s] = 1;
-                int other = en.y;
-                if (other >= 0 && !bflag[other]) stack[sp_++] = other, bflag[other] = 1;
+            out = {nc, nj, ni};
+        }
+        out.n_contacts = gshfl(x, out.n_contacts, 0);
+        out.n_joints = gshfl(x, out.n_joints, 0);
+        out.n_islands = gshfl(x, out.n_islands, 0);
+        gsync(x);
+        return out;
+    }
+    int *astart = ap<int>(x, L.jok);
+    for (int b = lane; b < B; b += x.wl) astart[b] = adj_start[b];
+    gsync(x);
+    int sp_ = 0, nc = 0, nj = 0, ni = 0;  // sp_, nc and nj: lane 0's
+    int next_seed = B - 1;  // bodies above the last seed never qualify again: flags only get set, and only bodies
+                            // already flagged are woken
+    for (;;) {
+        if (gshfl(x, sp_, 0) == 0) {
+            int seed = -1;
+            for (int hi = next_seed; hi >= 0 && seed < 0; hi -= x.wl) {
+                const int c = hi - lane;
+                const bool q = c >= 0 && w.active[c] && w.type[c] != STATIC && w.awake[c] && !bflag[c];
+                const unsigned mk = gballot(x, q);
+                if (mk) seed = hi - (__ffs(mk) - 1);
             }
+            if (seed < 0) break;
+            next_seed = seed - 1;
+            ++ni;
+            if (lane == 0) stack[sp_++] = seed, bflag[seed] = 1;
+            gsync(x);
+            continue;
+        }
+        int b = 0;
+        if (lane == 0) b = stack[--sp_];
+        b = gshfl(x, b, 0);
+        const int id = ni - 1;
+        const int q0 = astart[b], q1 = b + 1 < B ? astart[b + 1] : n_adj;
+        for (int c0 = q0; c0 < q1; c0 += x.wl) {
+            const int2 en = c0 + lane < q1 ? adj[c0 + lane] : make_int2(-1, -1);
+            const int n_en = q1 - c0 < x.wl ? q1 - c0 : x.wl;
+            for (int j = 0; j < n_en; ++j) {
+                const int s_ = gshfl(x, en.x, j), other = gshfl(x, en.y, j);
+                if (lane == 0 && !(other >= 0 && other != b && bisl[other] >= 0)) {
+                    corder[nc++] = s_;
+                    cisl[s_] = id;
+                    if (other >= 0 && !bflag[other]) stack[sp_++] = other, bflag[other] = 1;
+                }
+            }
+        }
+        if (lane == 0) {
             for (int q = m.jadj_start[b], qe = m.jadj_start[b + 1]; q < qe; ++q) {
                 int j = m.jadj[2 * q], other = m.jadj[2 * q + 1];
                 if (jflag[j] || !w.active[other]) continue;
@@ -679,8 +780,9 @@ __device__ IslandOut find_islands(Ctx &x) {
             bisl[b] = id;
             wake_body(w, b);
         }
-        out = {nc, nj, ni};
+        gsync(x);
     }
+    if (lane == 0) out = {nc, nj, ni};
     out.n_contacts = gshfl(x, out.n_contacts, 0);
     out.n_joints = gshfl(x, out.n_joints, 0);
     out.n_islands = gshfl(x, out.n_islands, 0);
@@ -951,18 +1053,29 @@ __device__ int lv_levels(Ctx &x, const IslandWork &sw, const LvPass &ps, int *le
     for (int b = lane; b < w.B; b += x.wl) last[b] = 0;
     gsync(x);
     int nl = 0;
-    if (lane == 0) {  // greedy levelling in pass order (sequential by nature: each level depends on earlier ones)
-        for (int e = 0; e < n; ++e) {
+    // greedy levelling in pass order (sequential by nature: each level depends on earlier ones): the lanes read the
+    // dynamic bodies of 32 (16) elements at a time, lane 0 walks them in order
+    for (int e0 = 0; e0 < n; e0 += x.wl) {
+        const int e = e0 + lane;
+        int a = -1, b = -1;
+        if (e < n) {
             const bool jt = ps.is_joint(e);
             const int r = ps.row(e);
-            const int a = jt ? sw.jr[r].ia : sw.vc[r].ia, b = jt ? sw.jr[r].ib : sw.vc[r].ib;
-            const bool da = w.type[a] == DYNAMIC, db = w.type[b] == DYNAMIC;
-            const int la = da ? last[a] : 0, lb = db ? last[b] : 0;
-            const int l = la > lb ? la : lb;
-            level[e] = l;
-            if (da) last[a] = l + 1;
-            if (db) last[b] = l + 1;
-            nl = nl > l + 1 ? nl : l + 1;
+            a = jt ? sw.jr[r].ia : sw.vc[r].ia, b = jt ? sw.jr[r].ib : sw.vc[r].ib;
+            if (w.type[a] != DYNAMIC) a = -1;
+            if (w.type[b] != DYNAMIC) b = -1;
+        }
+        const int m = n - e0 < x.wl ? n - e0 : x.wl;
+        for (int j = 0; j < m; ++j) {
+            const int ja = gshfl(x, a, j), jb = gshfl(x, b, j);
+            if (lane == 0) {
+                const int la = ja >= 0 ? last[ja] : 0, lb = jb >= 0 ? last[jb] : 0;
+                const int l = la > lb ? la : lb;
+                level[e0 + j] = l;
+                if (ja >= 0) last[ja] = l + 1;
+                if (jb >= 0) last[jb] = l + 1;
+                nl = nl > l + 1 ? nl : l + 1;
+            }
         }
     }
     nl = gshfl(x, nl, 0);
@@ -1002,14 +1115,18 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
     const goib2d_settings &s = x.s;
     const int nc = ids.cnt[0], nj = ids.cnt[1], n_islands = ids.cnt[2], lane = x.lane;
     const Layout &L = p.lay;
-    int *level = sp<int>(x.scr, L.lv_level), *cur = sp<int>(x.scr, L.lv_cur), *last = sp<int>(x.scr, L.lv_last);
+    // the levelling's per-body table in the island walk's stack (shared memory when the arena's hot part holds it;
+    // the stack is free from the end of find_islands to the TOI events, which clear it before use)
+    int *level = sp<int>(x.scr, L.lv_level), *cur = sp<int>(x.scr, L.lv_cur), *last = ap<int>(x, L.stack);
     int *vitems = sp<int>(x.scr, L.lv_items), *vstart = sp<int>(x.scr, L.lv_start);  // velocity pass
     int *citems = sp<int>(x.scr, L.lv_items2), *cstart = sp<int>(x.scr, L.lv_start2);  // contacts-first passes
     const LvPass vps{nc, nj, true}, cps{nc, nj, false};
     int vnl = 0;
+    GB_LV_T0(x);
     bool seq = nc + nj < LV_MIN_CONSTRAINTS || lv_minus_zero(x, sw.bd);
     if (!seq) {
         vnl = lv_levels(x, sw, vps, level, vitems, vstart, cur, last);
+        GB_LV(x, 0);
         seq = 3 * vnl > 2 * (nc + nj);
     }
     if (seq) {
@@ -1022,6 +1139,7 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
         GB_COUNT(15, vnl);
     }
     const int cnl = lv_levels(x, sw, cps, level, citems, cstart, cur, last);
+    GB_LV(x, 1);
     const int B = p.m.B;
     const int64_t world = x.world;
     float *sep = sp<float>(x.scr, L.lv_sep);
@@ -1043,6 +1161,7 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
         }
         gsync(x);
     }
+    GB_LV(x, 2);
     // velocity iterations: the joints then the contacts, the same levels every iteration
     for (int it = 0; it < s.velocity_iterations; ++it)
         for (int l = 0; l < vnl; ++l) {
@@ -1053,6 +1172,7 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
             }
             gsync(x);
         }
+    GB_LV(x, 3);
     // StoreImpulses (contact_solver.py:293-304, joints.py:609-622), one row per lane
     const StoreTo st = store_to(x.w);
     for (int k = lane; k < nc; k += x.wl) {
@@ -1094,6 +1214,7 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
     }
     for (int i = lane; i < B; i += x.wl) done[i] = i >= n_islands;
     gsync(x);
+    GB_LV(x, 4);
     // position iterations with per-island early exit (step.py:197-251): the contacts then the joints, levelled; the
     // islands' minimum separations are taken in pass order afterwards (the float minimum's order rules for -0)
     const LvPass &ps = cps;
@@ -1120,20 +1241,63 @@ __device__ void solve_constraints_levelled(Ctx &x, const IslandWork &sw, const I
             }
             gsync(x);
         }
-        if (lane == 0) {
-            for (int i = 0; i < n_islands; ++i) minsep[i] = 0.0f, jok[i] = 1;
-            for (int k = 0; k < nc; ++k) {
-                const int i = cisl[vc[k].slot];
-                if (!done[i]) minsep[i] = bmin(minsep[i], sep[k]);
-            }
-            for (int k = 0; k < nj; ++k) {
-                const int i = jisl[jr[k].jid];
-                if (!done[i]) jok[i] = jok[i] && okj[k];
-            }
-            for (int i = 0; i < n_islands; ++i)
-                if (minsep[i] >= -3.0f * s.linear_slop && jok[i]) done[i] = 1;
+        GB_LV(x, 5);
+        // An island is done when the minimum of 0 and its contacts' separations, taken in row order, is at least
+        // -3 linear slop and its joints are within tolerance. Without a NaN separation the minimum is at least the
+        // tolerance exactly when 0 and every separation are (any order); a NaN is replaced by the next value of the
+        // fold, so then the minimum is taken in order.
+        const float tol = -3.0f * s.linear_slop;
+        for (int i = lane; i < n_islands; i += x.wl) jok[i] = 1;
+        gsync(x);
+        bool nan = false;
+        for (int k = lane; k < nc; k += x.wl) {
+            const int i = cisl[vc[k].slot];
+            if (done[i]) continue;
+            const float v = sep[k];
+            nan = nan || v != v;
+            if (v < tol) jok[i] = 0;
+        }
+        for (int k = lane; k < nj; k += x.wl) {
+            const int i = jisl[jr[k].jid];
+            if (!done[i] && !okj[k]) jok[i] = 0;
+        }
+        if (!gballot(x, nan)) {
+            gsync(x);
+            const bool zero_ok = 0.0f >= tol;
+            for (int i = lane; i < n_islands; i += x.wl)
+                if (zero_ok && jok[i]) done[i] = 1;
+            gsync(x);
+            GB_LV(x, 6);
+            continue;
         }
         gsync(x);
+        for (int i = lane; i < n_islands; i += x.wl) minsep[i] = 0.0f, jok[i] = 1;
+        gsync(x);
+        // the lanes read 32 (16) rows' islands and separations at a time, lane 0 folds them in order
+        for (int k0 = 0; k0 < nc; k0 += x.wl) {
+            const int k = k0 + lane;
+            int ik = -1;
+            float sk = 0.0f;
+            if (k < nc) {
+                ik = cisl[vc[k].slot], sk = sep[k];
+                if (done[ik]) ik = -1;
+            }
+            const int m = nc - k0 < x.wl ? nc - k0 : x.wl;
+            for (int j = 0; j < m; ++j) {
+                const int i = gshfl(x, ik, j);
+                const float v = gshfl(x, sk, j);
+                if (lane == 0 && i >= 0) minsep[i] = bmin(minsep[i], v);
+            }
+        }
+        for (int k = lane; k < nj; k += x.wl) {  // a logical and: any order
+            const int i = jisl[jr[k].jid];
+            if (!done[i] && !okj[k]) jok[i] = 0;
+        }
+        gsync(x);
+        for (int i = lane; i < n_islands; i += x.wl)
+            if (minsep[i] >= tol && jok[i]) done[i] = 1;
+        gsync(x);
+        GB_LV(x, 6);
     }
 }
 
@@ -2111,6 +2275,7 @@ extern "C" int goib2d_debug_phase_cycles(unsigned long long *out, int reset) {
     if (cudaMemcpyFromSymbol(out + 32, g_toi_cycles, sizeof(g_toi_cycles)) != cudaSuccess) return -2;
     if (cudaMemcpyFromSymbol(out + 48, g_span, sizeof(g_span)) != cudaSuccess) return -2;
     if (cudaMemcpyFromSymbol(out + 64, g_phase_max, sizeof(g_phase_max)) != cudaSuccess) return -2;
+    if (cudaMemcpyFromSymbol(out + 80, g_lv_cycles, sizeof(g_lv_cycles)) != cudaSuccess) return -2;
     if (reset) {
         unsigned long long z[16] = {0};
         cudaMemcpyToSymbol(g_phase_cycles, z, sizeof(z));
@@ -2118,6 +2283,7 @@ extern "C" int goib2d_debug_phase_cycles(unsigned long long *out, int reset) {
         cudaMemcpyToSymbol(g_toi_cycles, z, sizeof(g_toi_cycles));
         cudaMemcpyToSymbol(g_span, z, sizeof(g_span));
         cudaMemcpyToSymbol(g_phase_max, z, sizeof(g_phase_max));
+        cudaMemcpyToSymbol(g_lv_cycles, z, sizeof(g_lv_cycles));
     }
     return 0;
 }

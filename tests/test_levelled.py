@@ -106,3 +106,44 @@ def test_levelled_sweeps_with_every_joint_type(api, mode):
     want = oracle_lib.step(model, host, d.settings, dt, 90, threads=8)
     assert_states_equal(got, want, f"joints mode {mode}")
     assert (got.contacts.touching.sum(1) > 4).all()  # the loose boxes landed on the jointed ones or the ground
+
+
+def wide_level_scene():
+    """One world of 40 boxes resting on the static ground, every fourth with a second box on top: the first level of
+    each pass holds at least 40 contacts, more than a world's lanes, the second the stacked ones."""
+    from goib2d import DYNAMIC, STATIC, Settings, WorldDef
+    d = WorldDef(Settings.stock(gravity=(0.0, -10.0), allow_sleep=False))
+    g = d.add_body(STATIC)
+    d.add_box(g, (60.0, 0.5), center=(0.0, -0.5))
+    for i in range(40):
+        x = -48.0 + 2.4 * i
+        b = d.add_body(DYNAMIC, (x, 0.49), 0.0, mass=1.0, inertia=0.2)
+        d.add_box(b, (0.5, 0.5), friction=0.6)
+        if i % 4 == 0:
+            c = d.add_body(DYNAMIC, (x + 0.1, 1.48), 0.0, mass=0.5, inertia=0.1)
+            d.add_box(c, (0.4, 0.5), friction=0.6)
+    return d
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_levelled_sweeps_with_levels_wider_than_the_lanes(api, mode):
+    from goib2d.world import map_state
+    d = wide_level_scene()
+    model, st = d.build(128)
+    n = 6
+    host = map_state(lambda x: np.ascontiguousarray(np.repeat(np.asarray(x)[None], n, 0)), st)
+    rng = np.random.default_rng(29)
+    dyn = (host.bodies.type == 2)[..., None]
+    host.bodies.v[...] = np.where(dyn, rng.normal(0, 0.3, host.bodies.v.shape), host.bodies.v).astype(np.float32)
+    dt = np.float32(1.0 / 60.0)
+    eng = api.Engine(model, host.bodies.type.shape[1])
+    try:
+        eng.set_step_mode(mode)
+        dev = api.to_device(host)
+        eng.step_(dev, d.settings, dt, n_steps=60)
+        got = api.to_host(dev)
+    finally:
+        eng.close()
+    want = oracle_lib.step(model, host, d.settings, dt, 60, threads=8)
+    assert_states_equal(got, want, f"wide levels mode {mode}")
+    assert (got.contacts.touching.sum(1) >= 50).all()
