@@ -20,6 +20,8 @@ int hot_budget(int64_t n_worlds, int n_joints, int contact_capacity, int step_mo
 cudaError_t launch_reset(const EnvParams &p, cudaStream_t s);    // env.cuh (compiled in step.cu)
 cudaError_t launch_observe(const EnvParams &p, cudaStream_t s);  // env.cuh
 cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s);  // env.cuh
+cudaError_t launch_spawn(const EnvParams &p, cudaStream_t s);    // spawn.cuh (compiled in step.cu)
+cudaError_t launch_seed(const SeedParams &p, cudaStream_t s);    // spawn.cuh
 cudaError_t launch_pair_count(const PairScene &s, int64_t *count);                              // scene.cuh
 cudaError_t launch_pair_fill(const PairScene &s, const int64_t *start, int32_t *pa, int32_t *pb);  // scene.cuh
 }
@@ -771,6 +773,77 @@ int goib2d_raycast(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, v
     if ((rc = device_view(out, &o))) return rc;
     p.body = body, p.n_rays = n_rays, p.max_length = max_length, p.out = (float *)o;
     CUDA_TRY(gb::launch_raycast(p, (cudaStream_t)stream));
+    return 0;
+}
+
+// ---- scene spawn on the device (spawn.cuh)
+int goib2d_spawn(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves,
+                 void *const *template_leaves, int32_t first_body, int32_t n_placed, const float *placements,
+                 int32_t n_speeds, const int32_t *speed_joints, const float *speeds, void *stream) {
+    gb::EnvParams p;
+    int rc = env_params(m, C, rows, n_worlds, leaves, p);
+    if (rc) return rc;
+    if (!template_leaves) return fail(GOIB2D_EINVAL, "null argument");
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) {
+        if (!template_leaves[i] && p.leaf_bytes[i] > 0) return fail(GOIB2D_EINVAL, "template leaf %d is null", i);
+        p.I.p[i] = template_leaves[i];
+    }
+    if (first_body < 0 || n_placed < 0 || (int64_t)first_body + n_placed > p.B)
+        return fail(GOIB2D_EINVAL, "placed bodies %d..%d outside 0..%d", first_body, first_body + n_placed - 1, p.B - 1);
+    if (n_placed > 0 && n_worlds > 0 && !placements) return fail(GOIB2D_EINVAL, "null placements");
+    if (n_speeds < 0 || n_speeds > 16) return fail(GOIB2D_ELIMIT, "%d motor speeds per world (16 at most)", n_speeds);
+    if (n_speeds > 0 && (!speed_joints || (!speeds && n_worlds > 0))) return fail(GOIB2D_EINVAL, "null speeds");
+    p.J = p.m.J;
+    for (int k = 0; k < n_speeds; ++k) {
+        if (speed_joints[k] < 0 || speed_joints[k] >= p.J) return fail(GOIB2D_EINVAL, "joint %d out of range",
+                                                                         speed_joints[k]);
+        p.speed_joint[k] = speed_joints[k];
+    }
+    const void *pl = nullptr, *sp = nullptr;
+    if ((rc = device_view(n_placed > 0 ? placements : nullptr, &pl))) return rc;
+    if ((rc = device_view(n_speeds > 0 ? speeds : nullptr, &sp))) return rc;
+    p.first_body = first_body, p.n_placed = n_placed, p.placements = (const float *)pl;
+    p.n_speeds = n_speeds, p.speeds = (const float *)sp;
+    CUDA_TRY(gb::launch_spawn(p, (cudaStream_t)stream));
+    return 0;
+}
+
+int goib2d_seed_placements(const goib2d_spawn_rule *rule, uint64_t seed, int64_t first_world, int64_t n_worlds,
+                           float *placements, float *speeds, void *stream) {
+    if (!rule) return fail(GOIB2D_EINVAL, "null argument");
+    if (first_world < 0 || n_worlds < 0) return fail(GOIB2D_EINVAL, "negative world range");
+    const goib2d_spawn_rule &r = *rule;
+    if (r.kind < GOIB2D_SPAWN_UNIFORM || r.kind > GOIB2D_SPAWN_RIG) return fail(GOIB2D_EINVAL, "rule kind %d", r.kind);
+    const int nb = r.kind == GOIB2D_SPAWN_RIG ? 3 : r.n_bodies;
+    if (nb < 0 || nb > 65536) return fail(GOIB2D_ELIMIT, "%d bodies per world (65536 at most)", nb);
+    if (r.kind == GOIB2D_SPAWN_RIG && r.n_bodies != 3) return fail(GOIB2D_EINVAL, "the rig rule places 3 bodies");
+    if (r.kind == GOIB2D_SPAWN_GRID && r.grid_side < 1) return fail(GOIB2D_EINVAL, "grid_side %d", r.grid_side);
+    if (r.kind == GOIB2D_SPAWN_RIG) {
+        if (r.max_tries < 1 || r.max_tries > 4096) return fail(GOIB2D_ELIMIT, "max_tries %d (1..4096)", r.max_tries);
+        if (r.n_heights < 1 || !r.heights) return fail(GOIB2D_EINVAL, "the rig rule needs a height field");
+        if (r.n_discs < 0 || (r.n_discs > 0 && !r.discs)) return fail(GOIB2D_EINVAL, "bad discs");
+        if (!(r.h_dx > 0.0f)) return fail(GOIB2D_EINVAL, "h_dx must be positive");
+        if (n_worlds > 0 && !speeds) return fail(GOIB2D_EINVAL, "the rig rule writes motor speeds: null speeds");
+    }
+    if (n_worlds > 0 && nb > 0 && !placements) return fail(GOIB2D_EINVAL, "null placements");
+    if ((uint64_t)(first_world + n_worlds) >> 63) return fail(GOIB2D_ELIMIT, "world range overflows");
+    gb::SeedParams p{};
+    p.rule = r;
+    int rc;
+    const void *v = nullptr;
+    if (r.kind == GOIB2D_SPAWN_RIG) {
+        if ((rc = device_view(r.heights, &v))) return rc;
+        p.rule.heights = (const float *)v;
+        if ((rc = device_view(r.n_discs > 0 ? r.discs : nullptr, &v))) return rc;
+        p.rule.discs = (const float *)v;
+        if ((rc = device_view(speeds, &v))) return rc;
+        p.speeds = (float *)v;
+    }
+    if ((rc = device_view(placements, &v))) return rc;
+    p.placements = (float *)v;
+    p.key0 = (uint32_t)seed, p.key1 = (uint32_t)(seed >> 32);
+    p.first_world = first_world, p.n_worlds = n_worlds;
+    CUDA_TRY(gb::launch_seed(p, (cudaStream_t)stream));
     return 0;
 }
 

@@ -179,6 +179,21 @@ struct EnvParams {
     float *out;
     int n_rays;
     float max_length;
+    // goib2d_spawn (spawn.cuh): I holds one template world (row 0 of every leaf)
+    int first_body, n_placed;
+    const float *placements;  // [n_worlds][n_placed][6]
+    int n_speeds;
+    int32_t speed_joint[16];
+    const float *speeds;      // [n_worlds][n_speeds]
+    int J;
+};
+
+// goib2d_seed_placements (spawn.cuh)
+struct SeedParams {
+    goib2d_spawn_rule rule;
+    uint32_t key0, key1;
+    int64_t first_world, n_worlds;
+    float *placements, *speeds;
 };
 
 // The scene given to the candidate-pair build (scene.cuh), device arrays.

@@ -85,6 +85,7 @@ __device__ unsigned long long g_lv_cycles[16];
 #endif
 
 #include "env.cuh"
+#include "spawn.cuh"
 #include "scene.cuh"
 #include "solver.cuh"
 #include "toi.cuh"

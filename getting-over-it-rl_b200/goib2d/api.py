@@ -165,6 +165,32 @@ class Engine:
                                              C.c_float(max_length), out.data_ptr(), self._stream(device)))
         return out
 
+    def spawn(self, template, n_worlds, first_body, placements, speed_joints=(), speeds=None):
+        """A new device State of n_worlds worlds built on the device (goib2d_spawn): each a copy of `template` (a
+        one-world device State, e.g. world 0's build) with bodies first_body .. first_body + k - 1 placed as the
+        builder's add_body places them, from placements (float32 (n_worlds, k, 6): x, y, angle, v.x, v.y, w; device
+        or pinned host), and joint speed_joints[j]'s motor speed = speeds[:, j] (float32 (n_worlds, len)). The
+        result equals building every world through WorldDef with those poses."""
+        leaves = state_leaves(template)
+        first = leaves[0]
+        if not (isinstance(first, torch.Tensor) and first.is_cuda and first.shape[0] == 1):
+            raise TypeError("spawn needs a one-world device State as its template")
+        out = state_from_leaves([torch.empty((n_worlds,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+                                 for t in leaves])
+        n, C_, rows, device, ptrs = self._bind(out)
+        tmpl = (C.c_void_p * len(leaves))(*[t.data_ptr() for t in leaves])
+        pl = placements.to(device=device, dtype=torch.float32).contiguous()
+        if pl.dim() != 3 or pl.shape[0] != n_worlds or pl.shape[2] != 6:
+            raise ValueError(f"placements must be (n_worlds, k, 6), got {tuple(pl.shape)}")
+        sj = np.ascontiguousarray(speed_joints, np.int32)
+        sp = None
+        if len(sj):
+            sp = speeds.to(device=device, dtype=torch.float32).reshape(n_worlds, len(sj)).contiguous()
+        native.check(self.lib.goib2d_spawn(self.handle, C_, rows, n, ptrs, tmpl, int(first_body), int(pl.shape[1]),
+                                           pl.data_ptr(), len(sj), sj.ctypes.data_as(native._i),
+                                           sp.data_ptr() if sp is not None else None, self._stream(device)))
+        return out
+
     def kernels_per_step(self, n_worlds):
         """Kernel launches one step of n_worlds worlds of this model makes (goib2d_kernels_per_step)."""
         k = self.lib.goib2d_kernels_per_step(self.handle, int(n_worlds))
@@ -276,3 +302,18 @@ def step(model, state, settings, dt, axis_name=None):
 
 
 __all__ = ["Engine", "build", "step", "step_", "to_device", "to_host", "broadcast", "State", "Settings"]
+
+
+def seed_placements(rule, seed, first_world, n_worlds, device="cuda"):
+    """goib2d_seed_placements: (placements (n_worlds, k, 6), speeds (n_worlds,) or None) drawn on the device for
+    worlds first_world .. first_world + n_worlds - 1 of a scene seeded `seed` (rule: native.SpawnRule; its heights
+    and discs must be device or pinned host memory kept alive by the caller)."""
+    lib = native.load()
+    k = 3 if rule.kind == native.SPAWN_RIG else int(rule.n_bodies)
+    pl = torch.empty((n_worlds, k, 6), dtype=torch.float32, device=device)
+    sp = torch.empty(n_worlds, dtype=torch.float32, device=device) if rule.kind == native.SPAWN_RIG else None
+    stream = torch.cuda.current_stream(pl.device).cuda_stream
+    native.check(lib.goib2d_seed_placements(C.byref(rule), C.c_uint64(seed & (2**64 - 1)), int(first_world),
+                                            int(n_worlds), pl.data_ptr(), sp.data_ptr() if sp is not None else None,
+                                            stream))
+    return pl, sp

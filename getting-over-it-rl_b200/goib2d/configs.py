@@ -90,6 +90,7 @@ class Scene:
     action_joints: tuple = ()  # joints whose motor speed follows an action channel
     action_scale: tuple = ()
     level: tuple = ()
+    rocks: list = field(default_factory=list)  # (x, y, r) of the c1 / c4 rocks
     anchor: tuple = ()
 
     def build_world(self, defn, i):
@@ -159,8 +160,7 @@ def _rig(defn, sc, i, x, y, ang):
     pot = defn.add_body(DYNAMIC, (x, y), 0.0, mass=30.0, inertia=5.4)
     defn.add_circle(pot, 0.6, friction=0.8, group=-1)  # group -1: the pot and the hammer never collide
     hub = defn.add_body(DYNAMIC, (x, y), ang, mass=1.0, inertia=0.05)
-    c, s = math.cos(ang), math.sin(ang)
-    hx, hy = x + 1.0 * c, y + 1.0 * s
+    hx, hy = (float(d["hx"][i]), float(d["hy"][i])) if "hx" in d else _hammer_at(x, y, ang)
     ham = defn.add_body(DYNAMIC, (hx, hy), ang, mass=2.0, inertia=0.43, bullet=True)
     defn.add_box(ham, (0.7, 0.04), (-0.1, 0.0), friction=0.6, group=-1)
     defn.add_polygon(ham, _HEAD, friction=0.6, group=-1)
@@ -172,6 +172,12 @@ def _rig(defn, sc, i, x, y, ang):
 
 
 _HEAD = [(0.55, -0.08), (0.8, -0.08), (0.85, 0.0), (0.8, 0.08), (0.55, 0.08)]
+
+
+def _hammer_at(x, y, ang):
+    """The hammer's position one arm length along its angle from the pot (host double trig; the device-seeded
+    scenes give it explicitly, as dyn["hx"], dyn["hy"])."""
+    return x + 1.0 * math.cos(ang), y + 1.0 * math.sin(ang)
 
 
 def _c1_bodies(defn, sc, i):
@@ -225,6 +231,7 @@ def c1(seed=0, n=4096, terrain="quads"):
     sc.dyn = _per_world(seed, n, lambda r: _rig_start(h, x0, dx, rocks, r))
     sc.builder = _c1_bodies
     sc.level = (h, x0, dx)
+    sc.rocks = rocks
     sc.action_joints, sc.action_scale = (0, 1), (4.0, 2.0)
     return sc
 
@@ -400,15 +407,18 @@ def _cuda():
         return False
 
 
-def batch(name, n, seed=0, compact=True, first=0, device_pairs=None):
+def batch(name, n, seed=0, compact=True, first=0, device_pairs=None, dyn=None):
     """(scene, Model, batched State (leaves (n, ...))) for n worlds of a workload. The Model comes from world 0's
     full build; each world's bodies, joints and dynamic-fixture AABBs come from replaying that world's dynamic
     builder calls on a WorldDef holding only the ground body, so every world equals its full WorldDef build (the
     static level is identical in all of them). compact: the compact fixture layout (static fixtures in the Model).
-    device_pairs: build the candidate list on the GPU (default: when CUDA is available)."""
+    device_pairs: build the candidate list on the GPU (default: when CUDA is available). dyn: per-world arrays that
+    replace the scene's own draws (seeded_dyn: the placements drawn on the device)."""
     from .world import Fixtures, State, compact_model, compact_state, empty_contacts, empty_toi
 
     sc = scene(name, seed, n, first)
+    if dyn is not None:
+        sc.dyn = {**sc.dyn, **dyn}
     full = sc.world_def(0)
     # the candidate list on the GPU when there is one (goib2d_candidate_pairs: the host scan's list, checked equal)
     model, st0 = full.build(sc.capacity, device_pairs=_cuda() if device_pairs is None else device_pairs)
@@ -442,3 +452,118 @@ def batch(name, n, seed=0, compact=True, first=0, device_pairs=None):
         model = compact_model(model, state)
         state = compact_state(model, state, check=False)
     return sc, model, state
+
+
+# ---- scene spawn on the device (goib2d_spawn, goib2d_seed_placements)
+
+def placements(sc):
+    """(first_body, placements float32 (n, k, 6), speed_joints, speeds float32 (n, len) or None) of a Scene's worlds:
+    the poses its builder gives bodies 1 .. k (x, y, angle, v.x, v.y, w), as goib2d_spawn takes them."""
+    d, n = sc.dyn, sc.n_worlds
+    base = sc.name.split("_")[0]
+    if base in ("c1", "c4"):
+        x, y, a = (np.asarray(d[k], F32) for k in ("x", "y", "angle"))
+        if "hx" in d:
+            hx, hy = np.asarray(d["hx"], F32), np.asarray(d["hy"], F32)
+        else:
+            hx, hy = (np.array(v, F32) for v in zip(*[_hammer_at(float(x[i]), float(y[i]), float(a[i]))
+                                                    for i in range(n)]))
+        z = np.zeros(n, F32)
+        pl = np.stack([np.stack([x, y, z, z, z, z], -1), np.stack([x, y, a, z, z, z], -1),
+                       np.stack([hx, hy, a, z, z, z], -1)], 1)
+        return 1, pl, (0,), np.asarray(d["w0"], F32).reshape(n, 1)
+    if base == "c3":
+        x, y, vx, vy = (np.asarray(d[k], F32) for k in ("x", "y", "vx", "vy"))
+        z = np.zeros_like(x)
+        return 1, np.stack([x, y, z, vx, vy, z], -1), (), None
+    x, y, a = (np.asarray(d[k], F32) for k in ("x", "y", "angle"))  # c0, c2
+    z = np.zeros_like(x)
+    return 1, np.stack([x, y, a, z, z, z], -1), (), None
+
+
+def spawn_rule(sc, host=False):
+    """The goib2d_spawn_rule of a workload's device-seeded variant (the same spawn pattern as its numpy draws, from
+    Philox streams per (seed, world) instead), and the arrays it points at (keep them alive while it is used):
+    device tensors, or host numpy arrays with host=True (for the parity oracle)."""
+    from . import native
+    r = native.SpawnRule()
+    base = sc.name.split("_")[0]
+    keep = ()
+    if base == "c0":
+        x0, dx = -32.0, 0.5
+        r.kind, r.n_bodies = native.SPAWN_UNIFORM, 8
+        r.x_lo, r.x_hi, r.y_lo, r.y_hi = x0 + 1, x0 + 127 * dx - 1, 2.0, 6.0
+        r.angle_lo, r.angle_hi = 0.0, 2 * np.pi
+    elif base == "c2":
+        k = len(sc.dyn["kind"])
+        side = int(math.ceil(math.sqrt(k)))
+        r.kind, r.n_bodies, r.grid_side = native.SPAWN_GRID, k, side
+        r.grid_x0 = r.grid_y0 = -9.0
+        r.grid_pitch, r.jitter, r.angle_lo, r.angle_hi = 18.0 / side, 0.1, 0.0, 2 * np.pi
+    elif base == "c3":
+        r.kind, r.n_bodies = native.SPAWN_UNIFORM, 32
+        r.x_lo, r.x_hi, r.y_lo, r.y_hi, r.speed_lo, r.speed_hi = -9.5, 9.5, -9.5, 9.5, 50.0, 200.0
+    elif base in ("c1", "c4"):
+        h, x0, dx = sc.level
+        heights = np.ascontiguousarray(h, F32)
+        discs = np.ascontiguousarray(np.asarray(sc.rocks, F32).reshape(-1, 3))
+        if host:
+            keep, ph, pd = (heights, discs), heights.ctypes.data, discs.ctypes.data
+        else:
+            import torch
+            keep = (torch.from_numpy(heights).cuda(), torch.from_numpy(discs).cuda())
+            ph, pd = keep[0].data_ptr(), keep[1].data_ptr()
+        r.kind, r.n_bodies = native.SPAWN_RIG, 3
+        r.x_lo, r.x_hi = x0 + 10, x0 + 2000 * dx - 10
+        r.heights, r.n_heights, r.h_x0, r.h_dx = ph, len(heights), x0, dx
+        r.half_width, r.lift, r.arm = 0.8, 0.62, 1.0
+        r.min_ground = -3.0 if base == "c4" else -np.inf
+        r.discs, r.n_discs, r.clearance, r.max_tries = pd, len(discs), 2.8, 64
+        r.angle_lo, r.angle_hi, r.speed_lo, r.speed_hi = 0.2 * np.pi, 0.8 * np.pi, -2.0, 2.0
+    else:
+        raise ValueError(f"no spawn rule for {sc.name}")
+    return r, keep
+
+
+def seeded_dyn(sc, pl, speeds):
+    """The per-world Scene arrays equal to device-drawn placements (host numpy), for building the same worlds through
+    WorldDef (batch(..., dyn=...))."""
+    pl = np.asarray(pl, F32)
+    base = sc.name.split("_")[0]
+    if base in ("c1", "c4"):
+        return dict(x=pl[:, 0, 0], y=pl[:, 0, 1], angle=pl[:, 1, 2], hx=pl[:, 2, 0], hy=pl[:, 2, 1],
+                    w0=np.asarray(speeds, F32))
+    if base == "c3":
+        return dict(x=pl[..., 0], y=pl[..., 1], vx=pl[..., 3], vy=pl[..., 4])
+    return dict(x=pl[..., 0], y=pl[..., 1], angle=pl[..., 2])
+
+
+def spawn_batch(name, n, seed=0, first=0, seeded=False, device_pairs=None):
+    """(scene, Model, device State, placements, speeds) of n worlds built on the device: the template world (the
+    first) from the host builder, every world placed by goib2d_spawn. seeded=False: the scene's own numpy draws (the
+    State equals batch(name, n, seed, first=first)); True: placements drawn on the device by goib2d_seed_placements
+    (the workload's device-seeded variant, equal to batch(..., dyn=seeded_dyn(...)) of the same draws), with no
+    per-world host work."""
+    import torch
+
+    from . import api
+    sc = scene(name, seed, 1 if seeded else n, first)
+    dyn = None
+    if seeded:
+        rule, keep = spawn_rule(sc)
+        pl, sp = api.seed_placements(rule, seed, first, n)
+        torch.cuda.current_stream().synchronize()
+        del keep
+        dyn = seeded_dyn(sc, pl[:1].cpu().numpy(), None if sp is None else sp[:1].cpu().numpy())
+    else:
+        _, pl_np, _, sp_np = placements(sc)
+        pl = torch.from_numpy(pl_np).cuda()
+        sp = torch.from_numpy(sp_np).cuda() if sp_np is not None else None
+    sc1, model, tmpl_host = batch(name, 1, seed, first=first, device_pairs=device_pairs, dyn=dyn)
+    eng = api.Engine(model, tmpl_host.bodies.type.shape[1])
+    try:
+        state = eng.spawn(api.to_device(tmpl_host), n, 1, pl, (0,) if sp is not None else (), sp)
+        torch.cuda.current_stream().synchronize()
+    finally:
+        eng.close()
+    return sc1, model, state, pl, sp

@@ -26,6 +26,19 @@ class PairDesc(C.Structure):
                 ("joint_b", _i), ("joint_collide", _u)]
 
 
+
+SPAWN_UNIFORM, SPAWN_GRID, SPAWN_RIG = 0, 1, 2  # goib2d_spawn_rule.kind
+
+
+class SpawnRule(C.Structure):
+    """goib2d_spawn_rule: how goib2d_seed_placements draws a world's placements from (seed, world)."""
+    _fields_ = [("kind", C.c_int32), ("n_bodies", C.c_int32)] + \
+        [(k, C.c_float) for k in ("x_lo", "x_hi", "y_lo", "y_hi", "angle_lo", "angle_hi", "speed_lo", "speed_hi")] + \
+        [("grid_side", C.c_int32)] + [(k, C.c_float) for k in ("grid_x0", "grid_y0", "grid_pitch", "jitter")] + \
+        [("heights", C.c_void_p), ("n_heights", C.c_int32)] + \
+        [(k, C.c_float) for k in ("h_x0", "h_dx", "half_width", "lift", "min_ground", "arm")] + \
+        [("discs", C.c_void_p), ("n_discs", C.c_int32), ("clearance", C.c_float), ("max_tries", C.c_int32)]
+
 def candidate_pairs_device(body_type, fixtures, joints, layer_masks=None):
     """goib2d_candidate_pairs on the current CUDA device: fixtures / joints as the WorldDef dicts; returns the
     (P, 2) int32 pair list."""
@@ -217,6 +230,9 @@ def load():
         "goib2d_observe": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.c_int32, _i, vp, vp]),
         "goib2d_raycast": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.c_int32, C.c_int32,
                                      C.c_float, vp, vp]),
+        "goib2d_spawn": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp), C.c_int32,
+                                   C.c_int32, vp, C.c_int32, _i, vp, vp]),
+        "goib2d_seed_placements": (C.c_int, [C.POINTER(SpawnRule), C.c_uint64, C.c_int64, C.c_int64, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

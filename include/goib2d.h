@@ -214,6 +214,61 @@ typedef struct goib2d_pair_desc {
 int goib2d_candidate_pairs(const goib2d_pair_desc *desc, int32_t *pair_a, int32_t *pair_b, int64_t capacity,
                            int64_t *n_pairs);
 
+/* Per-world initial States built on the device: every world of the batch (leaves, as goib2d_step's) starts as a copy
+ * of one template world (template_leaves: a one-world State of the same shape, e.g. world 0's WorldDef.build),
+ * then bodies first_body .. first_body + n_placed - 1 are placed per world as the host builder's
+ * WorldDef.add_body(type, position, angle, velocity, angular_velocity) with the template body's mass data would
+ * place them (reference world.py:186-244, b2Body::SetMassData / SetTransform): placements (float32
+ * [n_worlds][n_placed][6], device or page-locked host memory) = x, y, angle, v.x, v.y, w. Per placed body: xf = (x, y,
+ * sin/cos of the angle), sweep c0 = c = xf * local_center, a0 = a = angle; v and w as given when some is non-zero and
+ * the template body is awake, else zero; the fat AABBs of its fixture rows from b2BroadPhase::CreateProxy (the shape
+ * AABB at xf, extended by b2_aabbExtension). Static bodies keep the template's pose (the level is the batch's). Then
+ * joint speed_joints[k] (host int32 [n_speeds], at most 16) gets motor_speed = speeds[w][k] (float32 [n_worlds]
+ * [n_speeds], device or page-locked host memory). Replaces the host loop that builds each world through WorldDef
+ * (the reference builds each world's State on the host; a batch is a stack of them). Asynchronous on `stream`. */
+int goib2d_spawn(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
+                 void *const *leaves, void *const *template_leaves, int32_t first_body, int32_t n_placed,
+                 const float *placements, int32_t n_speeds, const int32_t *speed_joints, const float *speeds,
+                 void *stream);
+
+/* Seeded per-world placements on the device: world first_world + i of a scene seeded `seed` draws its placements
+ * (and motor speeds) from a counter-based generator, Philox4x32-10 (Salmon et al., SC'11) keyed by the seed with
+ * counter (world low, world high, block, 0): so a world's draws depend only on (seed, world), not on the batch or
+ * the shard. A uniform draw on [lo, hi) is lo + (hi - lo) * u in float32, u = (r >> 8) * 2^-24 of the block's next
+ * 32-bit word. Rules (goib2d_spawn_rule.kind), the benchmark scenes' spawn patterns:
+ *   GOIB2D_SPAWN_UNIFORM: n_bodies bodies, body k from draws 5k .. 5k + 4: x ~ [x_lo, x_hi), y ~ [y_lo, y_hi),
+ *     angle ~ [angle_lo, angle_hi), speed ~ [speed_lo, speed_hi), heading ~ [0, 2 pi): v = speed (cos, sin)
+ *     heading, w = 0 (BASELINE c0's box drop, c3's bullets);
+ *   GOIB2D_SPAWN_GRID: body k at the grid cell (k mod grid_side, k / grid_side) of pitch grid_pitch from
+ *     (grid_x0, grid_y0), cell centre plus a jitter ~ [-jitter, jitter) per axis, angle ~ [angle_lo, angle_hi)
+ *     (draws 3k .. 3k + 2; BASELINE c2);
+ *   GOIB2D_SPAWN_RIG: the character rig (3 bodies: pot, hub, hammer) over a height field (heights: device float32
+ *     [n_heights], x of sample i = h_x0 + i h_dx): try t < max_tries draws x ~ [x_lo, x_hi) (draw t); the ground
+ *     under the pot spans samples (int)((x - half_width - h_x0) / h_dx) .. (int)((x + half_width - h_x0) / h_dx) + 1
+ *     (clamped); y = its highest sample + lift; a try is kept when the lowest sample is >= min_ground and the pot
+ *     clears every disc (discs: device float32 [n_discs][3] = x, y, r; (x - dx)^2 + (y - dy)^2 > (r + clearance)^2),
+ *     the last try otherwise; angle ~ [angle_lo, angle_hi) (draw max_tries), the motor speed ~ [speed_lo,
+ *     speed_hi) (draw max_tries + 1) into speeds; pot at (x, y, 0), hub at (x, y, angle), hammer at
+ *     (x + arm cos angle, y + arm sin angle, angle) (BASELINE c1 and c4).
+ * placements: device float32 [n_worlds][n_bodies][6] (n_bodies = 3 for RIG); speeds: device float32 [n_worlds]
+ * (RIG only, may be NULL otherwise). No counterpart in the reference, whose worlds come from host numpy seeds. */
+enum { GOIB2D_SPAWN_UNIFORM = 0, GOIB2D_SPAWN_GRID = 1, GOIB2D_SPAWN_RIG = 2 };
+typedef struct goib2d_spawn_rule {
+    int32_t kind, n_bodies;
+    float x_lo, x_hi, y_lo, y_hi, angle_lo, angle_hi, speed_lo, speed_hi;
+    int32_t grid_side;
+    float grid_x0, grid_y0, grid_pitch, jitter;
+    const float *heights;
+    int32_t n_heights;
+    float h_x0, h_dx, half_width, lift, min_ground, arm;
+    const float *discs;
+    int32_t n_discs;
+    float clearance;
+    int32_t max_tries;
+} goib2d_spawn_rule;
+int goib2d_seed_placements(const goib2d_spawn_rule *rule, uint64_t seed, int64_t first_world, int64_t n_worlds,
+                           float *placements, float *speeds, void *stream);
+
 /* ---- Contact event log: the reference C API's listener (goi_jax/reference/capi.cpp:45-78, goi_b2_events at
  * :838-847) for a batch. Per world, the Begin (kind 0), End (1) and PostSolve (2) events of the last step, in the
  * order Box2D raises them: Collide's updates in contact-list order (End also for a touching contact that Collide

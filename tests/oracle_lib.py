@@ -121,3 +121,26 @@ def sin_cos(x):
     s, c = np.empty_like(x), np.empty_like(x)
     lib.oracle_sin_cos(x.ctypes.data, x.size, s.ctypes.data, c.ctypes.data)
     return s, c
+
+
+def seed_placements(rule, seed, first_world, n_worlds):
+    """The oracle's restatement of goib2d_seed_placements: (placements (n, k, 6), speeds (n,) or None). rule:
+    native.SpawnRule whose heights / discs point at host float32 arrays."""
+    lib = load()
+    k = 3 if rule.kind == native.SPAWN_RIG else int(rule.n_bodies)
+    pl = np.zeros((n_worlds, k, 6), np.float32)
+    sp = np.zeros(n_worlds, np.float32)
+    lib.oracle_seed_placements.argtypes = [C.POINTER(native.SpawnRule), C.c_uint64, C.c_int64, C.c_int64,
+                                           C.c_void_p, C.c_void_p]
+    assert lib.oracle_seed_placements(C.byref(rule), seed, first_world, n_worlds, pl.ctypes.data,
+                                      sp.ctypes.data) == 0
+    return pl, (sp if rule.kind == native.SPAWN_RIG else None)
+
+
+def philox4x32_10(ctr, k0, k1):
+    lib = load()
+    c = np.ascontiguousarray(ctr, np.uint32)
+    out = np.zeros(4, np.uint32)
+    lib.oracle_philox4x32_10.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
+    lib.oracle_philox4x32_10(c.ctypes.data, k0, k1, out.ctypes.data)
+    return out
