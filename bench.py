@@ -232,6 +232,7 @@ def main():
     import torch
     import torch.distributed as dist
     from goib2d import api, configs, native, shard
+    from goib2d.world import map_state
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world_size > 1:
@@ -239,16 +240,19 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     n = args.worlds or configs.DEFAULT_N[args.config]
     first, _ = shard.world_range(n, rank)  # weak scaling: every rank steps its own n seeded worlds
-    sc, model, host = configs.batch(args.config, n, args.seed, first=first)
-    eng = api.Engine(model, host.bodies.type.shape[1], sc.action_joints, sc.action_scale)
-    state = api.to_device(host, dev)
+    # the batch built on the GPU (goib2d_spawn from the host builder's first world and the scene's per-world poses):
+    # the same State as configs.batch, without the per-world host builder loop (minutes for c4's 65536 worlds)
+    sc, model, state, _, _ = configs.spawn_batch(args.config, n, args.seed, first=first)
+    n_cpu = cpu_sample_worlds(args, n)
+    host = api.to_host(map_state(lambda t: t[:n_cpu].contiguous(), state))  # the CPU baseline's sample
+    eng = api.Engine(model, state.bodies.type.shape[1], sc.action_joints, sc.action_scale)
     K, Wm = args.steps, args.warmup
     na = len(sc.action_joints)
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     # BASELINE c4: every world resets to its seeded initial state when the pot (body 1) falls below y = -5
     resets = args.config.startswith("c4")
-    init_state = api.to_device(host, dev) if resets else None
+    init_state = map_state(torch.clone, state) if resets else None
     reset_count = torch.zeros(n, dtype=torch.int32, device=dev) if resets else None
 
     S = args.substeps
@@ -333,7 +337,7 @@ def main():
             traffic = td.get("dram_bytes_per_world_step", 0) * n * S  # per launch group of one call
         cpu = None
         if not args.no_cpu_baseline:
-            cpu = cpu_baseline(sc, model, host, cpu_sample_worlds(args, n))
+            cpu = cpu_baseline(sc, model, host, n_cpu)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": K, "warmup": Wm,
             "ms_per_step": ms_max / K, "physics_steps_per_step": S, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
