@@ -10,6 +10,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "engine.cuh"
 
 namespace gb {
@@ -22,11 +24,21 @@ cudaError_t launch_observe(const EnvParams &p, cudaStream_t s);  // env.cuh
 cudaError_t launch_raycast(const EnvParams &p, cudaStream_t s);  // env.cuh
 cudaError_t launch_spawn(const EnvParams &p, cudaStream_t s);    // spawn.cuh (compiled in step.cu)
 cudaError_t launch_seed(const SeedParams &p, cudaStream_t s);    // spawn.cuh
+cudaError_t launch_check(const CheckParams &p, cudaStream_t s);  // check.cuh (compiled in step.cu)
 cudaError_t launch_pair_count(const PairScene &s, int64_t *count);                              // scene.cuh
 cudaError_t launch_pair_fill(const PairScene &s, const int64_t *start, int32_t *pa, int32_t *pb);  // scene.cuh
 }
 
 namespace {
+
+// An NVTX range over each C entry point (header-only NVTX3: a no-op unless a profiler such as Nsight Systems or
+// Nsight Compute is attached), so a profile shows which call issued which kernels.
+struct Range {
+    explicit Range(const char *name) { nvtxRangePushA(name); }
+    ~Range() { nvtxRangePop(); }
+    Range(const Range &) = delete;
+    Range &operator=(const Range &) = delete;
+};
 
 thread_local std::string g_err;
 
@@ -262,6 +274,8 @@ struct goib2d_model {
     goib2d_event *events = nullptr;
     int32_t *event_count = nullptr;
     int64_t event_worlds = 0, event_n = 0;
+    int32_t checks = 0;                       // goib2d_set_checks
+    unsigned long long *check_buf = nullptr;  // the validation kernel's result (allocated once, freed with the model)
     std::mutex mu;
 };
 
@@ -312,6 +326,7 @@ int64_t goib2d_leaf_elems(int leaf, int32_t B, int32_t rows, int32_t J, int32_t 
 }
 
 int goib2d_model_create(const goib2d_model_desc *d, goib2d_model **out) {
+    Range range("goib2d_model_create");
     if (!d || !out) return fail(GOIB2D_EINVAL, "null argument");
     *out = nullptr;
     const int B = d->n_bodies, F = d->n_fixtures, J = d->n_joints, P = d->n_pairs;
@@ -465,9 +480,83 @@ int goib2d_model_set_action_map(goib2d_model *m, int32_t n, const int32_t *joint
     return 0;
 }
 
+// The validation kernel over a batch (check.cuh) and its result, with the model's mutex held: the first failing
+// world (-1 when none) and the leaf that failed. Synchronises the stream.
+static const char *leaf_name(int leaf) {
+    switch (leaf) {
+        case GOIB2D_B_TYPE: return "bodies.type";
+        case GOIB2D_J_LIMIT_STATE: return "joints.limit_state";
+        case GOIB2D_C_PAIR: return "contacts.pair";
+        case GOIB2D_C_FA: return "contacts.fa";
+        case GOIB2D_C_FB: return "contacts.fb";
+        case GOIB2D_C_COUNT: return "contacts.count";
+        case GOIB2D_C_MTYPE: return "contacts.mtype";
+        default: return "leaf";
+    }
+}
+static int validate_locked(goib2d_model *m, const gb::DevModel &dm, int32_t C, int64_t n_worlds, void *const *leaves,
+                           int64_t *bad_world, int32_t *bad_leaf, cudaStream_t stream) {
+    if (!m->check_buf) {
+        CUDA_TRY(cudaMalloc(&m->check_buf, sizeof(unsigned long long)));
+        m->allocs.push_back(m->check_buf);
+    }
+    gb::CheckParams p{};
+    p.m = dm;
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
+    p.n_worlds = n_worlds, p.C = C, p.first_bad = m->check_buf;
+    CUDA_TRY(gb::launch_check(p, stream));
+    unsigned long long r = ~0ull;
+    CUDA_TRY(cudaMemcpyAsync(&r, m->check_buf, sizeof r, cudaMemcpyDeviceToHost, stream));
+    CUDA_TRY(cudaStreamSynchronize(stream));
+    *bad_world = r == ~0ull ? -1 : (int64_t)(r >> 8);
+    *bad_leaf = r == ~0ull ? -1 : (int32_t)(r & 0xff);
+    return 0;
+}
+
+int goib2d_set_checks(goib2d_model *m, int32_t on) {
+    if (!m) return fail(GOIB2D_EINVAL, "null argument");
+    std::lock_guard<std::mutex> lk(m->mu);
+    if (on && !m->check_buf) {
+        int dev = 0;
+        CUDA_TRY(cudaGetDevice(&dev));
+        if (dev != m->device) return fail(GOIB2D_EINVAL, "model lives on device %d, current device is %d", m->device,
+                                          dev);
+        CUDA_TRY(cudaMalloc(&m->check_buf, sizeof(unsigned long long)));
+        m->allocs.push_back(m->check_buf);
+    }
+    m->checks = on ? 1 : 0;
+    return 0;
+}
+
+int goib2d_validate(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves,
+                    int64_t *bad_world, int32_t *bad_leaf, void *stream) {
+    Range range("goib2d_validate");
+    if (!m || !leaves || !bad_world || !bad_leaf) return fail(GOIB2D_EINVAL, "null argument");
+    if (C < 0 || n_worlds < 0) return fail(GOIB2D_EINVAL, "negative size");
+    *bad_world = -1, *bad_leaf = -1;
+    std::lock_guard<std::mutex> lk(m->mu);
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != m->device) return fail(GOIB2D_EINVAL, "model lives on device %d, current device is %d", m->device, dev);
+    const gb::DevModel *dm = nullptr;
+    if (rows == m->full.F)
+        dm = &m->full;
+    else if (m->has_compact && rows == m->n_rows_compact)
+        dm = &m->compact;
+    else
+        return fail(GOIB2D_EINVAL, "fixture rows %d match neither the full (%d) nor the compact (%d) layout", rows,
+                    m->full.F, m->has_compact ? m->n_rows_compact : -1);
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i)
+        if (!leaves[i] && goib2d_leaf_elems(i, dm->B, rows, dm->J, C) > 0 && n_worlds > 0)
+            return fail(GOIB2D_EINVAL, "leaf %d is null", i);
+    if (n_worlds == 0) return 0;
+    return validate_locked(m, *dm, C, n_worlds, leaves, bad_world, bad_leaf, (cudaStream_t)stream);
+}
+
 int goib2d_step_seq(goib2d_model *m, const goib2d_settings *s, float dt, int32_t C, int32_t rows, int64_t n_worlds,
                     int32_t n_steps, void *const *leaves, const float *actions, int64_t action_step_stride,
                     void *stream) {
+    Range range("goib2d_step_seq");
     if (!m || !s || !leaves) return fail(GOIB2D_EINVAL, "null argument");
     if (C < 0 || n_worlds < 0 || n_steps < 0) return fail(GOIB2D_EINVAL, "negative size");
     if (action_step_stride < 0) return fail(GOIB2D_EINVAL, "negative action step stride");
@@ -488,6 +577,14 @@ int goib2d_step_seq(goib2d_model *m, const goib2d_settings *s, float dt, int32_t
         if (!leaves[i] && goib2d_leaf_elems(i, dm->B, rows, dm->J, C) > 0 && n_worlds > 0)
             return fail(GOIB2D_EINVAL, "leaf %d is null", i);
     if (n_worlds == 0 || n_steps == 0) return 0;
+    if (m->checks) {  // checked stepping: refuse a State whose index fields the kernels cannot use
+        int64_t bw = -1;
+        int32_t bl = -1;
+        int rc = validate_locked(m, *dm, C, n_worlds, leaves, &bw, &bl, (cudaStream_t)stream);
+        if (rc) return rc;
+        if (bw >= 0) return fail(GOIB2D_EINVAL, "checked step: world %lld has an out-of-range %s; nothing was stepped",
+                                 (long long)bw, leaf_name(bl));
+    }
     gb::StepParams p{};
     p.m = *dm;
     for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) p.L.p[i] = leaves[i];
@@ -721,6 +818,7 @@ int env_params(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void 
 
 int goib2d_reset_masked(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves,
                         void *const *init_leaves, const uint8_t *mask, void *stream) {
+    Range range("goib2d_reset_masked");
     gb::EnvParams p;
     int rc = env_params(m, C, rows, n_worlds, leaves, p);
     if (rc) return rc;
@@ -733,6 +831,7 @@ int goib2d_reset_masked(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worl
 
 int goib2d_reset_below(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves,
                        void *const *init_leaves, int32_t body, float y_min, int32_t *reset_count, void *stream) {
+    Range range("goib2d_reset_below");
     gb::EnvParams p;
     int rc = env_params(m, C, rows, n_worlds, leaves, p);
     if (rc) return rc;
@@ -746,6 +845,7 @@ int goib2d_reset_below(goib2d_model *m, int32_t C, int32_t rows, int64_t n_world
 
 int goib2d_observe(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves, int32_t n_bodies,
                    const int32_t *bodies, float *out, void *stream) {
+    Range range("goib2d_observe");
     gb::EnvParams p;
     int rc = env_params(m, C, rows, n_worlds, leaves, p);
     if (rc) return rc;
@@ -764,6 +864,7 @@ int goib2d_observe(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, v
 
 int goib2d_raycast(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves, int32_t body,
                    int32_t n_rays, float max_length, float *out, void *stream) {
+    Range range("goib2d_raycast");
     gb::EnvParams p;
     int rc = env_params(m, C, rows, n_worlds, leaves, p);
     if (rc) return rc;
@@ -780,6 +881,7 @@ int goib2d_raycast(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, v
 int goib2d_spawn(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, void *const *leaves,
                  void *const *template_leaves, int32_t first_body, int32_t n_placed, const float *placements,
                  int32_t n_speeds, const int32_t *speed_joints, const float *speeds, void *stream) {
+    Range range("goib2d_spawn");
     gb::EnvParams p;
     int rc = env_params(m, C, rows, n_worlds, leaves, p);
     if (rc) return rc;
@@ -810,6 +912,7 @@ int goib2d_spawn(goib2d_model *m, int32_t C, int32_t rows, int64_t n_worlds, voi
 
 int goib2d_seed_placements(const goib2d_spawn_rule *rule, uint64_t seed, int64_t first_world, int64_t n_worlds,
                            float *placements, float *speeds, void *stream) {
+    Range range("goib2d_seed_placements");
     if (!rule) return fail(GOIB2D_EINVAL, "null argument");
     if (first_world < 0 || n_worlds < 0) return fail(GOIB2D_EINVAL, "negative world range");
     const goib2d_spawn_rule &r = *rule;
@@ -849,6 +952,7 @@ int goib2d_seed_placements(const goib2d_spawn_rule *rule, uint64_t seed, int64_t
 
 int goib2d_candidate_pairs(const goib2d_pair_desc *d, int32_t *pair_a, int32_t *pair_b, int64_t capacity,
                            int64_t *n_pairs) {
+    Range range("goib2d_candidate_pairs");
     if (!d || !n_pairs) return fail(GOIB2D_EINVAL, "null argument");
     *n_pairs = 0;
     const int B = d->n_bodies, F = d->n_fixtures, J = d->n_joints;

@@ -188,6 +188,15 @@ struct EnvParams {
     int J;
 };
 
+// goib2d_validate and checked stepping (check.cuh)
+struct CheckParams {
+    DevModel m;
+    Leaves L;
+    int64_t n_worlds;
+    int C;
+    unsigned long long *first_bad;  // min over failures of (world << 8 | leaf); all ones when none
+};
+
 // goib2d_seed_placements (spawn.cuh)
 struct SeedParams {
     goib2d_spawn_rule rule;

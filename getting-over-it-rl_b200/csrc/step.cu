@@ -86,6 +86,7 @@ __device__ unsigned long long g_lv_cycles[16];
 
 #include "env.cuh"
 #include "spawn.cuh"
+#include "check.cuh"
 #include "scene.cuh"
 #include "solver.cuh"
 #include "toi.cuh"

@@ -19,7 +19,7 @@ import torch
 
 from . import native
 from .settings import Settings, settings_struct
-from .world import State, map_state, state_from_leaves, state_leaves
+from .world import State, leaf_names, map_state, state_from_leaves, state_leaves
 
 HERE = Path(__file__).resolve().parent
 CSRC = HERE.parent / "csrc"
@@ -206,6 +206,20 @@ class Engine:
         """Keep up to this many bytes of each world's State rows in shared memory across a one-launch call (0, the
         default: none). Results are identical either way."""
         native.check(self.lib.goib2d_set_state_staging(self.handle, int(max_bytes_per_world)))
+
+    def set_checks(self, on=True):
+        """Checked stepping: each later step validates the State's index fields first and raises (stepping nothing)
+        when a world's are out of range (goib2d_set_checks)."""
+        native.check(self.lib.goib2d_set_checks(self.handle, int(bool(on))))
+
+    def validate(self, state):
+        """(first bad world, its leaf name) of a device State, or None when every index field is in range
+        (goib2d_validate; synchronises)."""
+        n, C_, rows, device, ptrs = self._bind(state)
+        bw, bl = C.c_int64(-1), C.c_int32(-1)
+        native.check(self.lib.goib2d_validate(self.handle, C_, rows, n, ptrs, C.byref(bw), C.byref(bl),
+                                              self._stream(device)))
+        return None if bw.value < 0 else (bw.value, leaf_names()[bl.value])
 
     def set_event_log(self, capacity):
         """Log each world's contact events (Begin / End / PostSolve, goib2d_event) of every step, capacity per world

@@ -230,6 +230,9 @@ def load():
         "goib2d_observe": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.c_int32, _i, vp, vp]),
         "goib2d_raycast": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.c_int32, C.c_int32,
                                      C.c_float, vp, vp]),
+        "goib2d_set_checks": (C.c_int, [vp, C.c_int32]),
+        "goib2d_validate": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(C.c_int64),
+                                      C.POINTER(C.c_int32), vp]),
         "goib2d_spawn": (C.c_int, [vp, C.c_int32, C.c_int32, C.c_int64, C.POINTER(vp), C.POINTER(vp), C.c_int32,
                                    C.c_int32, vp, C.c_int32, _i, vp, vp]),
         "goib2d_seed_placements": (C.c_int, [C.POINTER(SpawnRule), C.c_uint64, C.c_int64, C.c_int64, vp, vp, vp]),

@@ -169,6 +169,21 @@ int goib2d_set_step_mode(goib2d_model *model, int32_t mode);
  * counterpart in the reference engine. */
 int goib2d_set_state_staging(goib2d_model *model, int32_t max_bytes_per_world);
 
+/* Checked stepping: with on != 0, every later goib2d_step / goib2d_step_seq call on this model first validates the
+ * State's index fields on the device (goib2d_validate's checks), synchronises the stream, and returns GOIB2D_EINVAL
+ * naming the first bad world and field, launching no step, when one fails. Off by default (the check costs a kernel
+ * and a synchronisation per call); goib2d_step_noalloc does not run it. No counterpart in the reference engine,
+ * which trusts its State. */
+int goib2d_set_checks(goib2d_model *model, int32_t on);
+
+/* Validate a batch's State without stepping it: the integer fields the step kernels use as indices or loop bounds,
+ * against the Model - bodies.type in STATIC..DYNAMIC, joints.limit_state in 0..3, contacts.pair in -1..P-1 and, for a
+ * live slot, contacts.fa / fb equal to the candidate's fixtures, contacts.count in 0..2, contacts.mtype in 0..2. The
+ * kernel only compares values, so it is safe on any State. *bad_world = the first failing world (-1: none) and
+ * *bad_leaf its failing leaf (GOIB2D_* leaf id). Synchronises the stream. */
+int goib2d_validate(goib2d_model *model, int32_t contact_capacity, int32_t fixture_rows, int64_t n_worlds,
+                    void *const *leaves, int64_t *bad_world, int32_t *bad_leaf, void *stream);
+
 /* ---- Env helpers around the step (no counterpart in the reference engine, whose RL env is outside it). Same
  * contact_capacity / fixture_rows / leaves conventions as goib2d_step; asynchronous on `stream`. */
 
