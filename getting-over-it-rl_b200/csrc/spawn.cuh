@@ -1,37 +1,47 @@
 // goib2d scene spawn on the device: each world's initial State from one template world and per-world body
 // placements (goib2d_spawn), and the placements themselves drawn per world from a seed (goib2d_seed_placements).
-// The reference builds every world on the host through WorldDef (world.py:186-386) and stacks them; here a warp per
-// world writes its rows from the template and places its bodies with the same float32 operations as the builder's
-// add_body / set_mass (world.py:196-244) and b2BroadPhase::CreateProxy's fat AABB (shapes.py:118-153), so the State
-// is the one the builder makes. Compiled with the step (step.cu includes this file).
+// The reference builds every world on the host through WorldDef (world.py:186-386) and stacks them; here one kernel
+// broadcasts the template's rows to every world (coalesced over each leaf), then a warp per world places its bodies
+// with the same float32 operations as the builder's add_body / set_mass (world.py:196-244) and
+// b2BroadPhase::CreateProxy's fat AABB (shapes.py:118-153), so the State is the one the builder makes. Compiled with the step (step.cu includes this file).
 #pragma once
 #include "narrow.cuh"
 
 namespace gb {
 
-// One world's row of a leaf from the template's (row 0): 4-byte words where the row allows, else bytes.
-__device__ __forceinline__ void copy_row(uint8_t *dst, const uint8_t *src, int64_t nb, int lane) {
+// Every world's row of every leaf from the template's (row 0): blockIdx.y = the leaf, the threads stride over the
+// leaf's words (bytes where a row is not a whole number of words) across all worlds, so consecutive threads store
+// consecutive words - coalesced writes of the whole batch instead of a warp per world over 71 short rows.
+__global__ void __launch_bounds__(256) goib2d_spawn_copy_kernel(const __grid_constant__ EnvParams p) {
+    const int i = blockIdx.y;
+    const uint32_t nb = (uint32_t)p.leaf_bytes[i];
+    if (nb == 0) return;
+    const uint8_t *src = (const uint8_t *)p.I.p[i];
+    uint8_t *dst = (uint8_t *)p.L.p[i];
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if ((nb & 3) == 0 && (((uintptr_t)dst | (uintptr_t)src) & 3) == 0) {
-        const uint32_t *s = (const uint32_t *)src;
-        uint32_t *d = (uint32_t *)dst;
-        for (int64_t k = lane; k < nb / 4; k += 32) d[k] = s[k];
+        const uint32_t nw = nb >> 2;
+        const uint64_t tw = (uint64_t)nw * (uint64_t)p.n_worlds;
+        if (tw + stride <= 0xffffffffull) {  // 32-bit index arithmetic, no wrap of t + stride (the usual case)
+            for (uint32_t t = (uint32_t)t0; t < (uint32_t)tw; t += (uint32_t)stride)
+                ((uint32_t *)dst)[t] = ((const uint32_t *)src)[t % nw];
+        } else {
+            for (uint64_t t = t0; t < tw; t += stride) ((uint32_t *)dst)[t] = ((const uint32_t *)src)[t % nw];
+        }
     } else {
-        for (int64_t k = lane; k < nb; k += 32) dst[k] = src[k];
+        const uint64_t tb = (uint64_t)nb * (uint64_t)p.n_worlds;
+        for (uint64_t t = t0; t < tb; t += stride) dst[t] = src[t % nb];
     }
 }
 
-// One warp per world (4 per block): template rows, then the placed bodies, their fixture rows' fat AABBs and the
-// per-world motor speeds. A placed body's transform is recomputed by every lane that needs it (rot_of is the engine's
-// correctly rounded float32 sin/cos, the builder's (float)sin((double)angle)).
+// One warp per world (4 per block), after goib2d_spawn_copy_kernel: the placed bodies, their fixture rows' fat AABBs
+// and the per-world motor speeds. A placed body's transform is recomputed by every lane that needs it (rot_of is the
+// engine's correctly rounded float32 sin/cos, the builder's (float)sin((double)angle)).
 __global__ void __launch_bounds__(128) goib2d_spawn_kernel(const __grid_constant__ EnvParams p) {
     const int64_t w = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= p.n_worlds) return;
-    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) {
-        const int64_t nb = p.leaf_bytes[i];
-        copy_row((uint8_t *)p.L.p[i] + w * nb, (const uint8_t *)p.I.p[i], nb, lane);
-    }
-    __syncwarp();
     const int B = p.B;
     const int32_t *type = (const int32_t *)p.I.p[GOIB2D_B_TYPE];
     const uint8_t *awake = (const uint8_t *)p.I.p[GOIB2D_B_AWAKE];
@@ -172,7 +182,16 @@ __global__ void __launch_bounds__(128) goib2d_seed_kernel(const __grid_constant_
 }
 
 cudaError_t launch_spawn(const EnvParams &p, cudaStream_t s) {
-    if (p.n_worlds > 0) goib2d_spawn_kernel<<<(unsigned)((p.n_worlds + 3) / 4), 128, 0, s>>>(p);
+    if (p.n_worlds <= 0) return cudaSuccess;
+    int64_t most = 1;  // the largest leaf's words (bytes) over the batch sets the grid's width
+    for (int i = 0; i < GOIB2D_NUM_LEAVES; ++i) most = p.leaf_bytes[i] * p.n_worlds > most ? p.leaf_bytes[i] * p.n_worlds : most;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int64_t bx = (most / 4 + 255) / 256;  // up to 4 blocks of 256 threads per SM for each leaf
+    bx = bx < 1 ? 1 : bx > 4 * (int64_t)sms ? 4 * (int64_t)sms : bx;
+    goib2d_spawn_copy_kernel<<<dim3((unsigned)bx, GOIB2D_NUM_LEAVES), 256, 0, s>>>(p);
+    goib2d_spawn_kernel<<<(unsigned)((p.n_worlds + 3) / 4), 128, 0, s>>>(p);
     return cudaGetLastError();
 }
 cudaError_t launch_seed(const SeedParams &p, cudaStream_t s) {
