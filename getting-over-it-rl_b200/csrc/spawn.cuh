@@ -3,7 +3,8 @@
 // The reference builds every world on the host through WorldDef (world.py:186-386) and stacks them; here one kernel
 // broadcasts the template's rows to every world (coalesced over each leaf), then a warp per world places its bodies
 // with the same float32 operations as the builder's add_body / set_mass (world.py:196-244) and
-// b2BroadPhase::CreateProxy's fat AABB (shapes.py:118-153), so the State is the one the builder makes. Compiled with the step (step.cu includes this file).
+// b2BroadPhase::CreateProxy's fat AABB (shapes.py:118-153), so the State is the one the builder makes. Compiled with
+// the step (step.cu includes this file).
 #pragma once
 #include "narrow.cuh"
 
